@@ -1,0 +1,137 @@
+/*
+ * sfb200.h — C ABI of the B200-native servoflow attention path.
+ *
+ * Every entry point takes plain device pointers, sizes and an opaque
+ * cudaStream_t (passed as void*), returns an int status (0 = OK, negative =
+ * error, never throws) and never allocates device memory on the hot path.
+ * The reference's C++ CUDABackend binds these in place of its own ops; the
+ * binding stubs are shown in INTEGRATION.md.
+ *
+ * dtype codes are the numeric values of sf::DType in the reference
+ * (include/servoflow/core/dtype.h:11-19), so a caller can pass
+ * static_cast<int>(tensor.dtype()) straight through.
+ */
+#ifndef SFB200_H
+#define SFB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── status codes ─────────────────────────────────────────────────────────── */
+#define SFB_OK                 0
+#define SFB_ERR_INVALID       -1  /* null pointer / bad argument            */
+#define SFB_ERR_DTYPE         -2  /* dtype not supported by this op         */
+#define SFB_ERR_SHAPE         -3  /* inconsistent or unsupported shape      */
+#define SFB_ERR_ALIGN         -4  /* pointer/stride alignment (TMA: 16 B)   */
+#define SFB_ERR_WORKSPACE     -5  /* workspace missing or too small         */
+#define SFB_ERR_LAUNCH        -6  /* kernel launch failed                   */
+#define SFB_ERR_UNSUPPORTED   -7  /* no sm_100a device / feature missing    */
+#define SFB_ERR_CUDA          -8  /* other CUDA runtime error               */
+#define SFB_ERR_DEVICE_TIMEOUT -9 /* a bounded device-side wait expired     */
+
+/* ── dtype codes (== sf::DType, reference dtype.h:11-19) ──────────────────── */
+#define SFB_F32   0
+#define SFB_F16   1
+#define SFB_BF16  2
+#define SFB_I8    3
+#define SFB_I32   5
+#define SFB_BOOL  6
+
+/* Human-readable message for a status code (static string). */
+const char* sfb_status_string(int status);
+
+/* Library version string, e.g. "0.1.0 sm_100a". */
+const char* sfb_version(void);
+
+/* Reads (and with reset != 0 clears) the device-side error word that bounded
+ * waits inside the kernels set when they time out. *code = 0 means no error.
+ * Synchronous: it waits for the device. */
+int sfb_device_error(int* code, int reset);
+
+/* ── attention ────────────────────────────────────────────────────────────────
+ * Replaces IBackend::attention (reference include/servoflow/backend/backend.h:
+ * 102-110) as implemented by CUDABackend::attention
+ * (src/backend/cuda/cuda_backend.cu:470-501) → cuda_ops::flash_attention
+ * (src/backend/cuda/ops/attention.cu:183-197).
+ *
+ *   out[b,h,i,:] = softmax_j( scale · q[b,h,i,:]·k[b,hk,j,:] + mask ) · v[b,hk,j,:]
+ *
+ * - Layout: the last (head_dim) dimension is contiguous; the other three
+ *   dimensions are addressed by element strides, so BHSD (the reference's
+ *   layout) and BSHD (a fused projection's layout) both work without copies.
+ * - scale == 0 means 1/sqrt(head_dim) (reference attention.cu:41,150).
+ * - is_causal: key j is visible to query i iff j <= i (reference
+ *   attention.cu:117, top-left aligned like torch SDPA).
+ * - kv_len (optional, int32 [batch], device): keys j >= kv_len[b] are masked.
+ * - key_mask (optional, uint8/bool [batch, seq_k], device, row stride
+ *   key_mask_stride_b elements): key j of batch b is kept iff the byte is
+ *   nonzero, masked (logit −inf) otherwise. This is the [B, Sk] key-padding
+ *   convention of the reference model (include/servoflow/models/rdt1b/
+ *   dit_block.h:141,153); the reference backend ignores masks
+ *   (attention.cu:30), this one applies them.
+ * - A query row whose keys are all masked produces zeros (torch SDPA would
+ *   produce NaN).
+ * - heads % heads_kv == 0 (grouped K/V heads, as flash_attn::mha_fwd's H_k).
+ * - dtype: SFB_BF16 / SFB_F16 (tcgen05 tensor-core kernel, head_dim 64) or
+ *   SFB_F32 (SIMT kernel, head_dim <= 128). q, k, v, out share the dtype.
+ */
+typedef struct sfb_attn_args {
+    const void* q;
+    const void* k;
+    const void* v;
+    void*       out;
+    int64_t q_stride[3];    /* element strides: batch, head, seq */
+    int64_t k_stride[3];
+    int64_t v_stride[3];
+    int64_t out_stride[3];
+    int32_t batch;
+    int32_t heads;
+    int32_t heads_kv;
+    int32_t seq_q;
+    int32_t seq_k;
+    int32_t head_dim;
+    int32_t dtype;
+    int32_t is_causal;
+    float   scale;
+    const int32_t* kv_len;        /* optional */
+    const uint8_t* key_mask;      /* optional */
+    int64_t key_mask_stride_b;
+    /* Number of key splits merged inside one thread-block cluster
+     * (0 = choose automatically, else 1..16). Tuning knob only. */
+    int32_t num_splits;
+} sfb_attn_args;
+
+int sfb_attention_fwd(const sfb_attn_args* args, void* stream);
+
+/* Convenience wrapper for contiguous BHSD tensors — the exact argument list
+ * of IBackend::attention with the Tensor metadata unpacked. mask may be NULL
+ * or a [batch, seq_k] byte key-padding mask. */
+int sfb_attention_bhsd(const void* q, const void* k, const void* v, void* out,
+                       int32_t batch, int32_t heads, int32_t heads_kv,
+                       int32_t seq_q, int32_t seq_k, int32_t head_dim,
+                       int32_t dtype, const uint8_t* key_mask, float scale,
+                       int32_t is_causal, void* stream);
+
+/* ── int8 dequantisation ──────────────────────────────────────────────────────
+ * Replaces IBackend::dequantize (backend.h:201-206) → CUDABackend::dequantize
+ * (cuda_backend.cu:565-569) → cuda_ops::dequantize_int8
+ * (src/backend/cuda/ops/quantization.cu:53-95).
+ *   out[n,k] = in[n,k] · scale[n]   (per output channel, scale_numel == rows)
+ *   out[n,k] = in[n,k] · scale[0]   (per tensor, scale_numel == 1)
+ * scale_dtype: SFB_F16 (the reference's only accepted type) or SFB_F32.
+ * out_dtype:   SFB_F16 (reference behaviour: the product is rounded to fp16,
+ *              quantization.cu:44), SFB_BF16 or SFB_F32.
+ */
+int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype,
+                        int64_t scale_numel, void* out, int32_t out_dtype,
+                        int64_t rows, int64_t cols, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* SFB200_H */

@@ -1,0 +1,171 @@
+// attn_simt.cu — CUDA-core attention forward: the fp32 path (RDT-1B action
+// self-attention at fp32, which must agree with the reference's fp32 kernel
+// to 1e-5) and every head_dim other than 64.
+//
+// Same semantics as the reference's fp32 kernel (src/backend/cuda/ops/
+// attention.cu:90-139: fp32 online softmax, causal cut at key > query),
+// different parallelisation: the reference runs one thread per query row
+// serially over all keys; here a warp owns 4 query rows, its 32 lanes score
+// 32 keys of a shared-memory K/V tile in parallel, the tile max and the P
+// broadcast go through warp shuffles, and lane l owns output columns
+// l, l+32, ... of the running O.
+#include "common.cuh"
+
+namespace sfb {
+
+struct AttnSimtParams {
+    const void* q; const void* k; const void* v; void* out;
+    int64_t q_sb, q_sh, q_ss, k_sb, k_sh, k_ss, v_sb, v_sh, v_ss, o_sb, o_sh, o_ss;
+    int32_t B, H, Hkv, Lq, Lk, D;
+    int32_t causal;
+    float   scale;
+    const int32_t* kv_len;
+    const uint8_t* key_mask;
+    int64_t mask_sb;
+};
+
+namespace attn_simt {
+
+constexpr int kWarps   = 4;
+constexpr int kRowsPW  = 4;                   // query rows per warp
+constexpr int kRowsCTA = kWarps * kRowsPW;    // 16
+constexpr int kKeys    = 32;                  // keys per tile
+
+template <typename T> __device__ __forceinline__ float ld(const T* p) { return static_cast<float>(*p); }
+template <> __device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <> __device__ __forceinline__ float ld<__half>(const __half* p) { return __half2float(*p); }
+template <typename T> __device__ __forceinline__ T cvt(float x) { return static_cast<T>(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half cvt<__half>(float x) { return __float2half_rn(x); }
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(kWarps * 32)
+attn_fwd_simt_kernel(const AttnSimtParams p) {
+    constexpr int NC = DP / 32;                  // output columns per lane
+    __shared__ float sQ[kRowsCTA][DP];
+    __shared__ float sK[kKeys][DP + 1];
+    __shared__ float sV[kKeys][DP];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.z, h = blockIdx.y;
+    const int hk = h / (p.H / p.Hkv);
+    const int q0 = blockIdx.x * kRowsCTA;
+    const T* Q = static_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh;
+    const T* K = static_cast<const T*>(p.k) + b * p.k_sb + hk * p.k_sh;
+    const T* V = static_cast<const T*>(p.v) + b * p.v_sb + hk * p.v_sh;
+
+    for (int i = tid; i < kRowsCTA * DP; i += blockDim.x) {
+        const int r = i / DP, d = i % DP;
+        const int qi = q0 + r;
+        sQ[r][d] = (qi < p.Lq && d < p.D) ? ld<T>(Q + qi * p.q_ss + d) : 0.f;
+    }
+
+    int kend = p.Lk;
+    if (p.kv_len != nullptr) kend = min(kend, max(0, p.kv_len[b]));
+    if (p.causal) kend = min(kend, min(p.Lq, q0 + kRowsCTA));
+
+    float m[kRowsPW], l[kRowsPW], o[kRowsPW][NC];
+#pragma unroll
+    for (int r = 0; r < kRowsPW; ++r) {
+        m[r] = -INFINITY; l[r] = 0.f;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) o[r][c] = 0.f;
+    }
+
+    for (int k0 = 0; k0 < kend; k0 += kKeys) {
+        __syncthreads();
+        for (int i = tid; i < kKeys * DP; i += blockDim.x) {
+            const int r = i / DP, d = i % DP;
+            const int kj = k0 + r;
+            const bool in = kj < kend && d < p.D;
+            sK[r][d] = in ? ld<T>(K + kj * p.k_ss + d) : 0.f;
+            sV[r][d] = in ? ld<T>(V + kj * p.v_ss + d) : 0.f;
+        }
+        __syncthreads();
+
+        const int kj = k0 + lane;
+        bool kvalid = kj < kend;
+        if (kvalid && p.key_mask != nullptr) kvalid = p.key_mask[b * p.mask_sb + kj] != 0;
+#pragma unroll
+        for (int r = 0; r < kRowsPW; ++r) {
+            const int row = warp * kRowsPW + r;
+            const int qi = q0 + row;
+            float s = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < DP; ++d) s = fmaf(sQ[row][d], sK[lane][d], s);
+            s *= p.scale;
+            const bool valid = kvalid && (!p.causal || kj <= qi);
+            if (!valid) s = -INFINITY;
+            float tmax = s;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+            const float mnew = fmaxf(m[r], tmax);
+            const float muse = mnew == -INFINITY ? 0.f : mnew;
+            const float alpha = expf(m[r] - muse);
+            const float pk = valid ? expf(s - muse) : 0.f;
+            l[r] = l[r] * alpha + pk;         // per-lane partial, reduced at the end
+            m[r] = mnew;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) o[r][c] *= alpha;
+#pragma unroll 4
+            for (int kk = 0; kk < kKeys; ++kk) {
+                const float pb = __shfl_sync(0xffffffffu, pk, kk);
+#pragma unroll
+                for (int c = 0; c < NC; ++c) o[r][c] = fmaf(pb, sV[kk][lane + 32 * c], o[r][c]);
+            }
+        }
+    }
+
+    T* O = static_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh;
+#pragma unroll
+    for (int r = 0; r < kRowsPW; ++r) {
+        float lt = l[r];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+        const int qi = q0 + warp * kRowsPW + r;
+        if (qi >= p.Lq) continue;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int d = lane + 32 * c;
+            if (d < p.D) O[qi * p.o_ss + d] = cvt<T>(o[r][c] * inv);
+        }
+    }
+}
+
+}  // namespace attn_simt
+
+template <typename T>
+static int launch_simt_t(const AttnSimtParams& p, cudaStream_t stream) {
+    dim3 grid((p.Lq + attn_simt::kRowsCTA - 1) / attn_simt::kRowsCTA, p.H, p.B);
+    dim3 block(attn_simt::kWarps * 32);
+    if (p.D <= 32)
+        attn_simt::attn_fwd_simt_kernel<T, 32><<<grid, block, 0, stream>>>(p);
+    else if (p.D <= 64)
+        attn_simt::attn_fwd_simt_kernel<T, 64><<<grid, block, 0, stream>>>(p);
+    else
+        attn_simt::attn_fwd_simt_kernel<T, 128><<<grid, block, 0, stream>>>(p);
+    return launch_status();
+}
+
+int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream) {
+    if (a.head_dim > 128) return SFB_ERR_SHAPE;
+    AttnSimtParams p{};
+    p.q = a.q; p.k = a.k; p.v = a.v; p.out = a.out;
+    p.q_sb = a.q_stride[0]; p.q_sh = a.q_stride[1]; p.q_ss = a.q_stride[2];
+    p.k_sb = a.k_stride[0]; p.k_sh = a.k_stride[1]; p.k_ss = a.k_stride[2];
+    p.v_sb = a.v_stride[0]; p.v_sh = a.v_stride[1]; p.v_ss = a.v_stride[2];
+    p.o_sb = a.out_stride[0]; p.o_sh = a.out_stride[1]; p.o_ss = a.out_stride[2];
+    p.B = a.batch; p.H = a.heads; p.Hkv = a.heads_kv; p.Lq = a.seq_q; p.Lk = a.seq_k; p.D = a.head_dim;
+    p.causal = a.is_causal ? 1 : 0;
+    p.scale = a.scale == 0.f ? 1.f / sqrtf(static_cast<float>(a.head_dim)) : a.scale;
+    p.kv_len = a.kv_len; p.key_mask = a.key_mask; p.mask_sb = a.key_mask_stride_b;
+    switch (a.dtype) {
+        case SFB_F32:  return launch_simt_t<float>(p, stream);
+        case SFB_F16:  return launch_simt_t<__half>(p, stream);
+        case SFB_BF16: return launch_simt_t<__nv_bfloat16>(p, stream);
+        default:       return SFB_ERR_DTYPE;
+    }
+}
+
+}  // namespace sfb

@@ -1,0 +1,88 @@
+// capi.cu — the extern "C" boundary (include/sfb200.h). Validates arguments,
+// picks the kernel, and converts every failure into a status code; nothing
+// here throws or allocates device memory.
+#include "common.cuh"
+
+namespace sfb {
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream);
+int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream);
+int dequantize_int8_launch(const int8_t* in, const void* scale, int32_t scale_dtype,
+                           int64_t scale_numel, void* out, int32_t out_dtype, int64_t rows,
+                           int64_t cols, cudaStream_t stream);
+}  // namespace sfb
+
+extern "C" {
+
+const char* sfb_status_string(int status) {
+    switch (status) {
+        case SFB_OK:                 return "ok";
+        case SFB_ERR_INVALID:        return "invalid argument";
+        case SFB_ERR_DTYPE:          return "unsupported dtype";
+        case SFB_ERR_SHAPE:          return "unsupported or inconsistent shape";
+        case SFB_ERR_ALIGN:          return "misaligned pointer or stride (16-byte rule)";
+        case SFB_ERR_WORKSPACE:      return "workspace missing or too small";
+        case SFB_ERR_LAUNCH:         return "kernel launch failed";
+        case SFB_ERR_UNSUPPORTED:    return "requires an sm_100a (B200) device";
+        case SFB_ERR_CUDA:           return "CUDA runtime error";
+        case SFB_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+        default:                     return "unknown status";
+    }
+}
+
+const char* sfb_version(void) { return "0.1.0 sm_100a"; }
+
+int sfb_device_error(int* code, int reset) {
+    if (code == nullptr) return SFB_ERR_INVALID;
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, sfb::g_sfb_device_error, sizeof(int)) != cudaSuccess) return SFB_ERR_CUDA;
+    *code = v;
+    if (reset) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(sfb::g_sfb_device_error, &zero, sizeof(int)) != cudaSuccess) return SFB_ERR_CUDA;
+    }
+    return SFB_OK;
+}
+
+int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
+    if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr || a->out == nullptr)
+        return SFB_ERR_INVALID;
+    if (a->batch < 0 || a->heads <= 0 || a->heads_kv <= 0 || a->seq_q < 0 || a->seq_k < 0 ||
+        a->head_dim <= 0)
+        return SFB_ERR_SHAPE;
+    if (a->heads % a->heads_kv != 0) return SFB_ERR_SHAPE;
+    if (a->dtype != SFB_F32 && a->dtype != SFB_F16 && a->dtype != SFB_BF16) return SFB_ERR_DTYPE;
+    if (a->num_splits < 0 || a->num_splits > 16) return SFB_ERR_INVALID;
+    if (a->batch == 0 || a->seq_q == 0) return SFB_OK;
+    const sfb::DeviceInfo& dev = sfb::device_info();
+    if (!sfb::is_sm100(dev)) return SFB_ERR_UNSUPPORTED;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool tc = (a->dtype == SFB_F16 || a->dtype == SFB_BF16) && a->head_dim == 64;
+    return tc ? sfb::attention_tc_launch(*a, s) : sfb::attention_simt_launch(*a, s);
+}
+
+int sfb_attention_bhsd(const void* q, const void* k, const void* v, void* out, int32_t batch,
+                       int32_t heads, int32_t heads_kv, int32_t seq_q, int32_t seq_k,
+                       int32_t head_dim, int32_t dtype, const uint8_t* key_mask, float scale,
+                       int32_t is_causal, void* stream) {
+    sfb_attn_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.q = q; a.k = k; a.v = v; a.out = out;
+    const int64_t D = head_dim;
+    a.q_stride[0] = (int64_t)heads * seq_q * D;    a.q_stride[1] = (int64_t)seq_q * D;  a.q_stride[2] = D;
+    a.out_stride[0] = a.q_stride[0];              a.out_stride[1] = a.q_stride[1];     a.out_stride[2] = D;
+    a.k_stride[0] = (int64_t)heads_kv * seq_k * D; a.k_stride[1] = (int64_t)seq_k * D;  a.k_stride[2] = D;
+    for (int i = 0; i < 3; ++i) a.v_stride[i] = a.k_stride[i];
+    a.batch = batch; a.heads = heads; a.heads_kv = heads_kv; a.seq_q = seq_q; a.seq_k = seq_k;
+    a.head_dim = head_dim; a.dtype = dtype; a.is_causal = is_causal; a.scale = scale;
+    a.key_mask = key_mask; a.key_mask_stride_b = seq_k;
+    return sfb_attention_fwd(&a, stream);
+}
+
+int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype,
+                        int64_t scale_numel, void* out, int32_t out_dtype, int64_t rows,
+                        int64_t cols, void* stream) {
+    return sfb::dequantize_int8_launch(in, scale, scale_dtype, scale_numel, out, out_dtype, rows,
+                                       cols, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,96 @@
+// common.cuh — shared host/device infrastructure of libsfb200.
+//
+// The library is built as one translation unit (sfb200.cu includes every
+// kernel file), so the definitions here exist exactly once.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/sfb200.h"
+
+namespace sfb {
+
+// Error word written by bounded device-side waits that expired (0 = none).
+__device__ int g_sfb_device_error = 0;
+
+struct DeviceInfo {
+    int ordinal = -1;
+    int major = 0, minor = 0;
+    int num_sms = 0;
+    bool valid = false;
+};
+
+// Cached properties of the current device (one entry per ordinal).
+inline const DeviceInfo& device_info() {
+    static DeviceInfo infos[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    DeviceInfo& d = infos[dev & 63];
+    if (!d.valid) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!d.valid) {
+            cudaDeviceProp prop{};
+            if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
+                d.ordinal = dev;
+                d.major = prop.major;
+                d.minor = prop.minor;
+                d.num_sms = prop.multiProcessorCount;
+                d.valid = true;
+            }
+        }
+    }
+    return d;
+}
+
+inline bool is_sm100(const DeviceInfo& d) { return d.valid && d.major == 10 && d.minor == 0; }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library does not link libcuda directly.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+inline int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, void* base,
+                             const cuuint64_t* dims, const cuuint64_t* strides,
+                             const cuuint32_t* box, const cuuint32_t* estr,
+                             CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = get_encode_fn();
+    if (fn == nullptr) return SFB_ERR_UNSUPPORTED;
+    CUresult r = fn(map, dt, static_cast<cuuint32_t>(rank), base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? SFB_OK : SFB_ERR_SHAPE;
+}
+
+inline int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SFB_OK : SFB_ERR_LAUNCH;
+}
+
+}  // namespace sfb

@@ -1,0 +1,6 @@
+// sfb200.cu — single translation unit of libsfb200.so (sm_100a).
+#include "common.cuh"
+#include "attn_tc.cu"
+#include "attn_simt.cu"
+#include "dequant.cu"
+#include "capi.cu"

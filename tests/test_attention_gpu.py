@@ -1,0 +1,255 @@
+"""GPU parity tests of the attention kernels against the CPU oracle, through
+the C ABI (servoflow_b200.backend → libsfb200.so).
+
+Tolerances (stated by the task for this path):
+  fp32: max |ours − oracle| <= 1e-5.
+  bf16/fp16: max |ours − oracle| <= 2e-3 + ½ ulp of the output type at
+  |oracle| — the second term is the rounding of the result itself to
+  bf16/fp16, which any half-precision attention (the reference's FA2
+  included) incurs; it is ≤ 2e-3 for |out| < 0.5 (bf16).
+The oracle always sees the same (rounded) inputs as the kernel.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from servoflow_b200 import _capi
+from servoflow_b200.backend import B200Backend
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def half_ulp(x, dtype):
+    mant = 7 if dtype == torch.bfloat16 else 10
+    ax = np.maximum(np.abs(x), np.float32(2.0 ** -14))
+    return 0.5 * np.exp2(np.floor(np.log2(ax)) - mant)
+
+
+def check_close(out, ref, dtype):
+    out = out.float().cpu().numpy()
+    err = np.abs(out - ref)
+    if dtype == torch.float32:
+        tol = np.float32(1e-5)
+    else:
+        tol = 2e-3 + half_ulp(ref, dtype)
+    bad = err > tol
+    assert not np.isnan(out).any()
+    assert not bad.any(), f"max err {err.max():.3e} at {np.unravel_index(err.argmax(), err.shape)}"
+    return float(err.max())
+
+
+def make(B, H, Hkv, Lq, Lk, D, dtype, seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, Lq, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, Lk, D, generator=g).to(dtype)
+    v = torch.randn(B, Hkv, Lk, D, generator=g).to(dtype)
+    return q.to(dev), k.to(dev), v.to(dev)
+
+
+def run(be, q, k, v, **kw):
+    out = torch.empty_like(q)
+    be.attention(q, k, v, out, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def oracle_of(q, k, v, **kw):
+    return oracle.attention(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                            v.float().cpu().numpy(), **kw)
+
+
+@pytest.fixture(scope="module")
+def be(gpu):
+    b = B200Backend(0)
+    b.device_error(reset=True)
+    yield b
+    assert b.device_error(reset=True) == 0, "a bounded device wait expired during the tests"
+
+
+# ── the BASELINE configs ──────────────────────────────────────────────────────
+def test_config1_self_attention_fp32(be, gpu):
+    q, k, v = make(1, 32, 32, 67, 67, 64, torch.float32, 42, gpu)
+    out = run(be, q, k, v, scale=0.125)
+    check_close(out, oracle_of(q, k, v, scale=0.125), torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_config1_self_attention_half(be, gpu, dtype):
+    q, k, v = make(1, 32, 32, 67, 67, 64, dtype, 43, gpu)
+    out = run(be, q, k, v, scale=0.125)
+    check_close(out, oracle_of(q, k, v, scale=0.125), dtype)
+
+
+def test_config2_image_cross_attention(be, gpu):
+    q, k, v = make(1, 32, 32, 67, 4374, 64, torch.bfloat16, 2, gpu)
+    ref = oracle_of(q, k, v)
+    err = check_close(run(be, q, k, v), ref, torch.bfloat16)
+    assert err <= 2e-3   # |out| is small here: the plain bound holds
+    # K/V are reused across the 5 denoising steps: repeated calls are identical
+    out2 = run(be, q, k, v)
+    assert torch.equal(out2, run(be, q, k, v))
+
+
+def test_config3_language_cross_attention_masked(be, gpu):
+    B, Lk = 16, 1024
+    q, k, v = make(B, 32, 32, 67, Lk, 64, torch.bfloat16, 3, gpu)
+    g = torch.Generator().manual_seed(33)
+    lens = torch.randint(8, 1025, (B,), generator=g, dtype=torch.int32)
+    keep = torch.arange(Lk)[None, :] < lens[:, None]
+    ref = oracle_of(q, k, v, kv_len=lens.numpy())
+    # key-padding mask form (bool [B, Lk]) and valid-length form (int32 [B])
+    check_close(run(be, q, k, v, mask=keep.to(gpu)), ref, torch.bfloat16)
+    check_close(run(be, q, k, v, mask=lens.to(gpu)), ref, torch.bfloat16)
+
+
+# ── golden vectors of the reference's oracle, through the GPU ─────────────────
+def test_golden_self_fp32(be, gpu):
+    g = np.load(os.path.join(GOLDEN, "attn_self_f32.npz"))
+    q, k, v = (torch.from_numpy(g[n]).to(gpu) for n in ("q", "k", "v"))
+    check_close(run(be, q, k, v, scale=float(g["scale"])), g["out"], torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_golden_masked(be, gpu, dtype):
+    g = np.load(os.path.join(GOLDEN, "attn_masked_f32.npz"))
+    q, k, v = (torch.from_numpy(g[n]).to(dtype).to(gpu) for n in ("q", "k", "v"))
+    mask = torch.from_numpy(g["key_mask"]).bool().to(gpu)
+    out = run(be, q, k, v, mask=mask)
+    ref = g["out"] if dtype == torch.float32 else oracle_of(q, k, v, key_mask=g["key_mask"])
+    check_close(out, ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_constant_input_kat(be, gpu, dtype):
+    # reference benchmarks/bench_attention.cu:50-52: V ≡ 0.01 ⇒ out ≡ 0.01
+    q = torch.full((1, 12, 1024, 64), 0.01, dtype=dtype, device=gpu)
+    out = run(be, q, q, q)
+    # half precision: P = 1 for every key, so the result is exactly V;
+    # fp32 sums 1024 copies of 0.01f, a few ulp of rounding
+    atol = 1e-6 if dtype == torch.float32 else 0.0
+    assert torch.allclose(out.float(), q.float(), atol=atol, rtol=0)
+
+
+# ── shapes and edge cases ─────────────────────────────────────────────────────
+@pytest.mark.parametrize("Lq,Lk", [(1, 1), (1, 4374), (67, 1), (67, 8), (67, 127), (67, 128),
+                                   (67, 129), (128, 300), (129, 67), (300, 1000)])
+def test_shapes_bf16(be, gpu, Lq, Lk):
+    q, k, v = make(2, 4, 4, Lq, Lk, 64, torch.bfloat16, Lq * 7 + Lk, gpu)
+    check_close(run(be, q, k, v), oracle_of(q, k, v), torch.bfloat16)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 5, 8, 11, 16])
+def test_split_counts(be, gpu, splits):
+    q, k, v = make(1, 4, 4, 67, 4374, 64, torch.bfloat16, 100 + splits, gpu)
+    check_close(run(be, q, k, v, num_splits=splits), oracle_of(q, k, v), torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("Lq,Lk", [(67, 67), (200, 200), (50, 300)])
+def test_causal(be, gpu, dtype, Lq, Lk):
+    q, k, v = make(1, 4, 4, Lq, Lk, 64, dtype, 11, gpu)
+    check_close(run(be, q, k, v, is_causal=True), oracle_of(q, k, v, causal=True), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_grouped_kv_heads(be, gpu, dtype):
+    q, k, v = make(2, 8, 2, 67, 500, 64, dtype, 12, gpu)
+    check_close(run(be, q, k, v), oracle_of(q, k, v), dtype)
+
+
+@pytest.mark.parametrize("D", [32, 128])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_other_head_dims(be, gpu, D, dtype):
+    q, k, v = make(1, 4, 4, 67, 300, D, dtype, D, gpu)
+    check_close(run(be, q, k, v), oracle_of(q, k, v), dtype)
+
+
+def test_bshd_strided_layout(be, gpu):
+    # [B, S, H, D] views, as a fused projection writes them
+    g = torch.Generator().manual_seed(21)
+    qs = torch.randn(2, 67, 32, 64, generator=g).bfloat16().to(gpu)
+    ks = torch.randn(2, 700, 32, 64, generator=g).bfloat16().to(gpu)
+    vs = torch.randn(2, 700, 32, 64, generator=g).bfloat16().to(gpu)
+    out = torch.empty_like(qs)
+    be.attention(qs, ks, vs, out, layout="bshd")
+    torch.cuda.synchronize()
+    ref = oracle_of(qs.transpose(1, 2), ks.transpose(1, 2), vs.transpose(1, 2))
+    check_close(out.transpose(1, 2), ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fully_masked_rows_are_zero(be, gpu, dtype):
+    q, k, v = make(3, 2, 2, 67, 300, 64, dtype, 13, gpu)
+    lens = torch.tensor([0, 300, 5], dtype=torch.int32)
+    out = run(be, q, k, v, mask=lens.to(gpu))
+    assert torch.all(out[0] == 0)
+    check_close(out, oracle_of(q, k, v, kv_len=lens.numpy()), dtype)
+
+
+def test_mask_with_holes_bf16(be, gpu):
+    q, k, v = make(2, 4, 4, 67, 777, 64, torch.bfloat16, 14, gpu)
+    g = torch.Generator().manual_seed(15)
+    keep = torch.rand(2, 777, generator=g) > 0.3
+    out = run(be, q, k, v, mask=keep.to(gpu))
+    check_close(out, oracle_of(q, k, v, key_mask=keep.numpy()), torch.bfloat16)
+
+
+def test_error_codes(be, gpu):
+    q, k, v = make(1, 4, 4, 67, 128, 64, torch.bfloat16, 1, gpu)
+    out = torch.empty_like(q)
+    with pytest.raises(_capi.SfbError) as e:
+        be.attention(q.view(torch.int16), k.view(torch.int16), v.view(torch.int16),
+                     out.view(torch.int16))
+    assert e.value.status == _capi.SFB_ERR_DTYPE
+    # misaligned base pointer for the TMA path
+    flat = torch.empty(4 * 67 * 64 + 1, dtype=torch.bfloat16, device=gpu)
+    qm = flat[1:].view(1, 4, 67, 64)
+    with pytest.raises(_capi.SfbError) as e:
+        be.attention(qm, k, v, out)
+    assert e.value.status == _capi.SFB_ERR_ALIGN
+    k3 = torch.empty(1, 3, 128, 64, dtype=torch.bfloat16, device=gpu)
+    with pytest.raises(_capi.SfbError) as e:
+        be.attention(q, k3, k3, out)
+    assert e.value.status == _capi.SFB_ERR_SHAPE
+
+
+def test_graph_capture_replay(be, gpu):
+    # the denoise loop is captured once and replayed; the op must be capturable
+    q, k, v = make(1, 32, 32, 67, 4374, 64, torch.bfloat16, 5, gpu)
+    out = torch.empty_like(q)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        be.attention(q, k, v, out, stream=s)       # warm-up outside capture
+        s.synchronize()
+        be.graph_begin_capture(s)
+        for _ in range(5):
+            be.attention(q, k, v, out, stream=s)
+        be.graph_end_capture(s)
+        out.zero_()
+        be.graph_launch(s)
+        s.synchronize()
+    check_close(out, oracle_of(q, k, v), torch.bfloat16)
+
+
+# ── the reference's own CUDA kernel (oracle/_ref), when it was built ──────────
+def test_reference_kernel_pins_oracle(gpu):
+    ref = oracle.ref_lib()
+    if ref is None:
+        pytest.skip("oracle/_ref/libsfref.so not built (needs the reference tree at build time)")
+    q, k, v = make(1, 32, 32, 67, 67, 64, torch.float32, 42, gpu)
+    out = torch.empty_like(q)
+    rc = ref.sfref_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), 0, 1, 32, 67,
+                             67, 64, 0.125, 0, None)
+    torch.cuda.synchronize()
+    assert rc == 0
+    ora = oracle_of(q, k, v, scale=0.125)
+    # the reference builds with --use_fast_math (CMakeLists.txt:37)
+    assert np.abs(out.cpu().numpy() - ora).max() <= 1e-5
+    ours = torch.empty_like(q)
+    B200Backend(0).attention(q, k, v, ours, scale=0.125)
+    torch.cuda.synchronize()
+    assert (ours - out).abs().max().item() <= 1e-5

@@ -1,0 +1,79 @@
+"""CPU checks of the C ABI: the library loads, exports every function that
+include/sfb200.h declares, and its host-only helpers behave. No kernel is
+launched here."""
+import ctypes
+import os
+import re
+import subprocess
+
+from servoflow_b200 import _capi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for f in os.listdir(os.path.join(ROOT, "include")):
+        if f.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", f)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(sfb_\w+)\s*\(", src))
+    return sorted(names)
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for n in ("sfb_attention_fwd", "sfb_attention_bhsd", "sfb_dequantize_int8", "sfb_device_error",
+              "sfb_status_string", "sfb_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _capi.lib()
+    for n in declared_functions():
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", _capi.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (sfb_\w+)", out))
+    assert set(declared_functions()) <= exported
+
+
+def test_status_strings_and_version():
+    assert _capi.status_string(0) == "ok"
+    assert "16-byte" in _capi.status_string(_capi.SFB_ERR_ALIGN)
+    assert _capi.status_string(12345) == "unknown status"
+    assert _capi.lib().sfb_version().decode().endswith("sm_100a")
+
+
+def test_args_struct_layout_matches_header():
+    # offsets of sfb_attn_args as laid out by the C compiler
+    src = r'''
+#include <stddef.h>
+#include <stdio.h>
+#include "sfb200.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu\n", offsetof(sfb_attn_args, q_stride), offsetof(sfb_attn_args, batch),
+         offsetof(sfb_attn_args, scale), offsetof(sfb_attn_args, key_mask_stride_b),
+         sizeof(sfb_attn_args));
+  return 0;
+}
+'''
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(src)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        got = list(map(int, subprocess.run([exe], capture_output=True, text=True).stdout.split()))
+    A = _capi.AttnArgs
+    want = [A.q_stride.offset, A.batch.offset, A.scale.offset, A.key_mask_stride_b.offset,
+            ctypes.sizeof(A)]
+    assert got == want
+
+
+def test_null_args_rejected_without_device():
+    # argument validation runs before any CUDA call
+    assert _capi.lib().sfb_attention_fwd(None, None) == _capi.SFB_ERR_INVALID
+    assert _capi.lib().sfb_dequantize_int8(None, None, 1, 1, None, 1, 0, 0, None) == _capi.SFB_OK
+    assert _capi.lib().sfb_dequantize_int8(None, None, 1, 1, None, 1, 2, 2, None) == \
+        _capi.SFB_ERR_INVALID
