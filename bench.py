@@ -65,53 +65,61 @@ def profiled_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples while the timed region runs."""
+    """Samples SM clock and throttle reasons through NVML (read-only) every
+    5 ms while the timed region runs."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
-        self.proc = None
+        self.samples = []
+        self.smax = None
+        self._stop = None
+
+    def _run(self):
+        import pynvml
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+        self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                util = pynvml.nvmlDeviceGetUtilizationRates(h).gpu
+                self.samples.append((float(sm), int(r), int(util)))
+            except Exception:
+                pass
+            self._stop.wait(0.005)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}", "--format=csv,noheader",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            # NVML enumerates physical GPUs; map through CUDA_VISIBLE_DEVICES when set
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if vis:
+                ids = [x for x in vis.split(",") if x.strip()]
+                if self.gpu < len(ids) and ids[self.gpu].strip().isdigit():
+                    self.gpu = int(ids[self.gpu])
+            self._stop = threading.Event()
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception:
+            self._stop = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self._stop is not None:
+            self._stop.set()
+            self._t.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1].split()[0]))
-                smax = float(f[2].split()[0])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [s for s, _, _ in self.samples]
+        busy = [s for s, _, u in self.samples if u > 0] or sm
+        reasons = sorted({n for _, r, _ in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": float(np.median(busy)) if busy else None, "sm_max_mhz": self.smax,
+                "reasons": reasons, "samples": len(sm), "source": "NVML, 5 ms polling"}
 
 
 def dist_setup(args):
@@ -209,8 +217,11 @@ def main():
 
     from servoflow_b200 import build
     build.build_library()
-    from servoflow_b200.backend import B200Backend
+    import ctypes
+    from servoflow_b200 import _capi
+    from servoflow_b200.backend import B200Backend, attention_args
     be = B200Backend(dev.index)
+    capi = _capi.lib()
 
     # one robot session per GPU (sessions are independent: seed by rank)
     g = torch.Generator().manual_seed(1000 + rank)
@@ -220,9 +231,17 @@ def main():
     out = torch.empty_like(q)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    cargs = attention_args(q, k, v, out)         # sfb_attn_args, built once
+    pargs = ctypes.byref(cargs)
+
+    def attn():
+        rc = capi.sfb_attention_fwd(pargs, sh)
+        if rc:
+            raise _capi.SfbError(rc, "attention")
 
     for _ in range(args.warmup):
-        be.attention(q, k, v, out, stream=stream)
+        attn()
     torch.cuda.synchronize()
     assert be.device_error() == 0
 
@@ -237,7 +256,7 @@ def main():
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            be.attention(q, k, v, out, stream=stream)
+            attn()
             ends[i].record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -248,18 +267,20 @@ def main():
         q_host = q.cpu().pin_memory()
         o_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
         q_dev = torch.empty_like(q)
+        args_e2e = attention_args(q_dev, k, v, out)
+        pe = ctypes.byref(args_e2e)
         e_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         e_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         for i in range(args.warmup):
             q_dev.copy_(q_host, non_blocking=True)
-            be.attention(q_dev, k, v, out, stream=stream)
+            _capi.check(capi.sfb_attention_fwd(pe, sh), "attention")
             o_host.copy_(out, non_blocking=True)
         torch.cuda.synchronize()
         for i in range(args.steps):
             flush.zero_()
             e_start[i].record(stream)
             q_dev.copy_(q_host, non_blocking=True)
-            be.attention(q_dev, k, v, out, stream=stream)
+            _capi.check(capi.sfb_attention_fwd(pe, sh), "attention")
             o_host.copy_(out, non_blocking=True)
             e_end[i].record(stream)
         torch.cuda.synchronize()

@@ -7,28 +7,34 @@
 // RDT-1B's shapes: Lq = 67 action tokens against Lk ∈ {67, 1024 (masked
 // language), 4374 (image)}.
 //
-// One CTA = 128 query rows × a contiguous range of 128-key tiles, 4 warps.
-//   * TMA (SWIZZLE_128B) stages Q once and K/V tiles through a 2-deep ring.
-//   * tcgen05.mma computes S = Q·Kᵀ (M=128, N=128, K=64) into TMEM; thread t
-//     owns query row t (TMEM lane t), so the row max / row sum of the online
-//     softmax are thread-local — no shuffles and no shared-memory reductions.
-//   * P (bf16/fp16) is written to shared memory in the UMMA K-major SW128
-//     layout — keys 0..63 into a dedicated buffer, keys 64..127 over the
-//     K tile of the same stage (free once S is computed) — and
-//     O_tile = P·V (M=128, N=64, K=128) runs on tcgen05 with V read MN-major
-//     straight from its TMA tile. The fp32 running O lives in registers.
-//   * The next tile's S MMA is issued right behind the current P·V, so the
-//     tensor pipe, the softmax and the TMA refill overlap; two CTAs share an
-//     SM (≈97 KB smem, 256 TMEM columns each).
+// One CTA = 128 query rows × a contiguous range of 128-key tiles, 9 warps:
+//   * warp 8 (control): TMA loads (SWIZZLE_128B) of Q once and of K/V tiles
+//     through a 4-deep ring, and every tcgen05.mma: S_j = Q·K_jᵀ (M=128,
+//     N=128, K=64) into one of two TMEM S/P buffers, then O += P_j·V_j
+//     (M=128, N=64, K=128) with P read from TMEM and O accumulated in TMEM
+//     across all tiles.
+//   * warps 0-7 (softmax): warps w and w+4 share TMEM lanes 32·(w%4)..+31
+//     (query rows) and split the 128 key columns in halves; the row max is
+//     exchanged through shared memory under a 64-thread named barrier.
+//     P is written back over S in TMEM as two bf16 (or fp16) parts,
+//     P = P_hi + P_lo, both multiplied into V, so the probabilities keep
+//     ~16 significant bits (plain bf16 P costs up to 2^-9 relative per weight,
+//     6e-3 absolute on few-key rows). The running max is a lazy reference:
+//     O in TMEM is rescaled only when a tile raises the max by more than
+//     8 (log2 units).
+//   * Only warps whose rows hold queries work (Lq = 67 → 6 of 8).
 //   * Split-K over Lk: the CTAs of one (batch, head, q-tile) form a thread-
-//     block cluster; each keeps (m, l, O) for its key range, and the partials
-//     are merged through distributed shared memory at the end. No global
-//     scratch, no atomics, no inter-CTA spin waits (cluster barriers are
-//     hardware barriers).
+//     block cluster; each keeps (O, m, l) for its key range, and the partials
+//     are merged through distributed shared memory. No global scratch, no
+//     atomics, no inter-CTA spin waits (cluster barriers are hardware).
 //
-// Every mbarrier wait is bounded (1 s); on expiry the CTA finishes its
-// control flow without further waiting, skips its output and records
-// SFB_ERR_DEVICE_TIMEOUT in g_sfb_device_error.
+// TMEM (512 columns): S/P buffer 0 at [0,128), buffer 1 at [128,256)
+// (P_hi over columns [0,64) of a buffer, P_lo over [64,128)), O at [256,320).
+//
+// Every mbarrier wait is bounded (1 s); after an expiry a thread stops
+// waiting, skips its output and records SFB_ERR_DEVICE_TIMEOUT in
+// g_sfb_device_error; control flow stays uniform so no barrier is left
+// half-arrived.
 #include "common.cuh"
 #include "sm100_ptx.cuh"
 
@@ -44,80 +50,97 @@ struct AttnTcParams {
     const int32_t* kv_len;
     const uint8_t* key_mask;
     int64_t  mask_sb;
+#ifdef SFB_TRACE
+    unsigned long long* trace;
+#endif
 };
 
 namespace attn_tc {
 
-constexpr int kThreads   = 128;
+#ifdef SFB_TRACE
+#define SFB_T(i) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && \
+                          (threadIdx.x == 0 || threadIdx.x == 256)) { \
+        p.trace[(threadIdx.x == 0 ? 0 : 256) + (i)] = clock64(); } } while (0)
+#else
+#define SFB_T(i) do { } while (0)
+#endif
+
+constexpr int kSoftWarps = 8;
+constexpr int kCtrlWarp  = 8;
+constexpr int kThreads   = (kSoftWarps + 1) * 32;          // 288
+constexpr int kStages    = 4;
 constexpr int kTileKeys  = 128;
-constexpr int kTileBytes = 128 * 128;     // 128 rows × 64 halves
+constexpr int kTileBytes = 128 * 128;                       // 128 rows × 64 halves
 constexpr int kOffQ      = 0;
-constexpr int kOffP      = kOffQ + kTileBytes;
-constexpr int kOffStage  = kOffP + kTileBytes;           // [2] × (K, V)
-constexpr int kOffBar    = kOffStage + 4 * kTileBytes;    // 98304
-constexpr int kOffTmem   = kOffBar + 64;
-constexpr int kOffMask   = kOffTmem + 16;
-constexpr int kSmemUsed  = kOffMask + 128;
-constexpr int kSmemBytes = kSmemUsed + 1024;              // + alignment slack
-constexpr int kTmemCols  = 256;                           // S: 0..127, O tile: 128..191
+constexpr int kOffStage  = kOffQ + kTileBytes;              // [kStages] × (K, V)
+constexpr int kOffBar    = kOffStage + kStages * 2 * kTileBytes;
+constexpr int kNumBars   = 1 + 2 * kStages + 2 + 2 + 2;
+constexpr int kOffTmem   = kOffBar + 8 * 16;
+constexpr int kOffRed    = kOffTmem + 16;                   // float [2][2][128] row max
+constexpr int kOffRedL   = kOffRed + 2 * 2 * 128 * 4;       // float [2][128] row sum
+constexpr int kSmemUsed  = kOffRedL + 2 * 128 * 4;
+constexpr int kSmemBytes = kSmemUsed + 1024;                // + alignment slack
+constexpr int kTmemCols  = 512;
+constexpr uint32_t kTmemO = 256;
 // Split-K merge buffers reuse the stage region once the main loop is done.
-constexpr int kOStride   = 68;                            // floats per row (16-B aligned, skewed)
+constexpr int kOStride   = 68;                              // floats per row
 constexpr int kOffCombO  = kOffStage;
-constexpr int kOffCombM  = kOffCombO + 128 * kOStride * 4;
-constexpr int kOffCombL  = kOffCombM + 128 * 4;
-static_assert(kOffCombL + 128 * 4 <= kOffBar, "merge buffers must fit in the stage region");
+// at most rows + C - 1 <= 143 row slots of (O row, m, l)
+static_assert(143 * (kOStride + 2) * 4 <= kStages * 2 * kTileBytes, "merge buffers must fit in the stage region");
+static_assert(kNumBars <= 16, "barrier area");
 
-enum Bar { kBarQ = 0, kBarK0 = 1, kBarK1 = 2, kBarV0 = 3, kBarV1 = 4, kBarS = 5, kBarO = 6 };
+// barrier indices
+constexpr int kBarQ = 0;
+__host__ __device__ constexpr int bar_k(int s) { return 1 + s; }
+__host__ __device__ constexpr int bar_v(int s) { return 1 + kStages + s; }
+__host__ __device__ constexpr int bar_s(int b) { return 1 + 2 * kStages + b; }      // S_j ready
+__host__ __device__ constexpr int bar_p(int b) { return 3 + 2 * kStages + b; }      // P_j written
+__host__ __device__ constexpr int bar_o(int b) { return 5 + 2 * kStages + b; }      // PV_j done
 
-template <typename T> struct Pack2;
-template <> struct Pack2<__nv_bfloat16> {
-    static __device__ __forceinline__ uint32_t pack(float a, float b, float& ra, float& rb) {
+template <typename T> struct HalfOps;
+template <> struct HalfOps<__nv_bfloat16> {
+    static constexpr uint32_t kFmt = 1;
+    static __device__ __forceinline__ uint32_t pack(float a, float b) {
         __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-        float2 f = __bfloat1622float2(v);
-        ra = f.x; rb = f.y;
         return *reinterpret_cast<uint32_t*>(&v);
     }
+    static __device__ __forceinline__ float2 unpack(uint32_t u) {
+        return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+    }
 };
-template <> struct Pack2<__half> {
-    static __device__ __forceinline__ uint32_t pack(float a, float b, float& ra, float& rb) {
+template <> struct HalfOps<__half> {
+    static constexpr uint32_t kFmt = 0;
+    static __device__ __forceinline__ uint32_t pack(float a, float b) {
         __half2 v = __floats2half2_rn(a, b);
-        float2 f = __half22float2(v);
-        ra = f.x; rb = f.y;
         return *reinterpret_cast<uint32_t*>(&v);
+    }
+    static __device__ __forceinline__ float2 unpack(uint32_t u) {
+        return __half22float2(*reinterpret_cast<__half2*>(&u));
     }
 };
 
 template <typename T>
-__device__ __forceinline__ void store_row8(T* dst, const float* v) {
-    float d0, d1;
-    uint4 u;
-    u.x = Pack2<T>::pack(v[0], v[1], d0, d1);
-    u.y = Pack2<T>::pack(v[2], v[3], d0, d1);
-    u.z = Pack2<T>::pack(v[4], v[5], d0, d1);
-    u.w = Pack2<T>::pack(v[6], v[7], d0, d1);
-    *reinterpret_cast<uint4*>(dst) = u;
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV,
                    const AttnTcParams p) {
     using namespace ptx;
+    using HO = HalfOps<T>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t*  sQ    = smem + kOffQ;
-    uint8_t*  sP    = smem + kOffP;
-    uint64_t* bars  = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint8_t*  sQ   = smem + kOffQ;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffTmem);
-    uint8_t*  sMask = smem + kOffMask;
+    float*    red  = reinterpret_cast<float*>(smem + kOffRed);     // [2 parity][2 half][128]
+    float*    redl = reinterpret_cast<float*>(smem + kOffRedL);    // [2 half][128]
     auto sK = [&](int s) { return smem + kOffStage + (2 * s) * kTileBytes; };
     auto sV = [&](int s) { return smem + kOffStage + (2 * s + 1) * kTileBytes; };
 
     const int tid  = threadIdx.x;
     const int warp = tid >> 5;
+    const int lane = tid & 31;
     const int split = blockIdx.x;
     const int h     = blockIdx.y;
     const int b     = blockIdx.z / p.qtiles;
@@ -125,6 +148,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int hk    = h / (p.H / p.Hkv);
     const int q0    = qt * 128;
     const int rows  = min(128, p.Lq - q0);
+    const int groups = (rows + 31) >> 5;            // active 32-row groups
+    const int nsoft  = 2 * groups;                  // active softmax warps
 
     // Key range of this (batch, q-tile), then this CTA's share of its tiles.
     int kend = p.Lk;
@@ -136,8 +161,15 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int t_begin = split * tbase + min(split, trem);
     const int ntl     = tbase + (split < trem ? 1 : 0);
 
-    if (tid == 0) {
-        for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
+    SFB_T(0);
+    if (tid == kCtrlWarp * 32) {
+        mbar_init(&bars[kBarQ], 1);
+        for (int s = 0; s < kStages; ++s) { mbar_init(&bars[bar_k(s)], 1); mbar_init(&bars[bar_v(s)], 1); }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars[bar_s(i)], 1);
+            mbar_init(&bars[bar_p(i)], nsoft);
+            mbar_init(&bars[bar_o(i)], 1);
+        }
         fence_mbarrier_init();
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -150,217 +182,264 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     tc_fence_before_sync();
     __syncthreads();
     tc_fence_after_sync();
-    const uint32_t tmem     = *tmem_holder;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem, tO = tmem + 128;
-
-    constexpr uint32_t kBF = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-    constexpr uint32_t idS  = idesc_f16(128, 128, kBF, 0, 0);   // Q (K-major) · K (K-major)
-    constexpr uint32_t idPV = idesc_f16(128, 64, kBF, 0, 1);    // P (K-major) · V (MN-major)
+    const uint32_t tmem = *tmem_holder;
+    SFB_T(1);
 
     bool ok = true;
     auto wait = [&](int bar, uint32_t parity) {
         if (!mbar_wait(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
     };
-    auto issue_kv = [&](int stage, int tile) {
-        const int key0 = tile * kTileKeys;
-        mbar_arrive_expect_tx(&bars[kBarK0 + stage], kTileBytes);
-        tma_load_4d(sK(stage), &tmK, &bars[kBarK0 + stage], 0, key0, hk, b);
-        mbar_arrive_expect_tx(&bars[kBarV0 + stage], kTileBytes);
-        tma_load_4d(sV(stage), &tmV, &bars[kBarV0 + stage], 0, key0, hk, b);
-    };
-    auto issue_s = [&](int stage) {
-        const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK(stage));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tS, smem_desc_sw128(aq + kk * 32, 16, 1024),
-                       smem_desc_sw128(ak + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
-        mma_commit(&bars[kBarS]);
-    };
 
-    if (tid == 0 && ntl > 0) {
-        mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
-        tma_load_4d(sQ, &tmQ, &bars[kBarQ], 0, q0, h, b);
-        issue_kv(0, t_begin);
-        if (ntl > 1) issue_kv(1, t_begin + 1);
-        wait(kBarQ, 0);
-        wait(kBarK0, 0);
-        tc_fence_after_sync();
-        issue_s(0);
-    }
+    float o_part[32];                   // this thread's 32 output columns (softmax warps)
+    float m_ref = -INFINITY, l_run = 0.f;
+    const int grp  = warp & 3;          // row group
+    const int half = warp >> 2;         // key-column half (softmax warps)
+    const int row  = grp * 32 + lane;
 
-    float o_acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) o_acc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    const int  qi          = q0 + tid;
-    const bool warp_active = warp * 32 < rows;
-    const bool use_mask    = p.key_mask != nullptr;
-    const float sl2        = p.sl2;
-
-    for (int j = 0; j < ntl; ++j) {
-        const int s    = j & 1;
-        const int key0 = (t_begin + j) * kTileKeys;
-        if (use_mask) {
-            const int key = key0 + tid;
-            sMask[tid] = key < kend ? p.key_mask[static_cast<int64_t>(b) * p.mask_sb + key] : 0;
-        }
-        wait(kBarS, j & 1);
-        tc_fence_after_sync();
-        __syncthreads();   // sMask visible; previous tile fully consumed
-
-        float alpha = 1.f;
-        uint8_t* sPhi = sK(s);
-        if (warp_active) {
-            const bool full_tile = (key0 + kTileKeys <= kend) && !use_mask && !p.causal;
-            auto valid = [&](int c) {
-                const int key = key0 + c;
-                bool v = key < kend;
-                if (use_mask) v = v && sMask[c] != 0;
-                if (p.causal) v = v && key <= qi;
-                return v;
+    if (warp == kCtrlWarp) {
+        // ── control warp: TMA + MMA issue (one thread) ──────────────────────
+        if (lane == 0 && ntl > 0) {
+            constexpr uint32_t idS  = idesc_f16(128, 128, HO::kFmt, 0, 0);  // Q·Kᵀ, both K-major
+            constexpr uint32_t idPV = idesc_f16(128, 64, HO::kFmt, 0, 1);   // P(tmem)·V(MN-major)
+            constexpr bool kSplitP  = std::is_same<T, __nv_bfloat16>::value;
+            auto issue_kv = [&](int tile_idx) {
+                const int s = tile_idx % kStages;
+                const int key0 = (t_begin + tile_idx) * kTileKeys;
+                mbar_arrive_expect_tx(&bars[bar_k(s)], kTileBytes);
+                tma_load_4d(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b);
+                mbar_arrive_expect_tx(&bars[bar_v(s)], kTileBytes);
+                tma_load_4d(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b);
             };
-            // pass 1: row max of the scaled logits (log2 domain)
-            float mx = m_run;
-            float sc[32];
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                tmem_ld32(tS + lane_off + ch * 32, sc);
-                tmem_ld_wait();
-                if (full_tile) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sc[i] * sl2);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (valid(ch * 32 + i)) mx = fmaxf(mx, sc[i] * sl2);
-                }
-            }
-            const float m_use = (mx == -INFINITY) ? 0.f : mx;
-            alpha = ptx::ex2(m_run - m_use);
-            // pass 2: P = exp2(s - m), rounded to the operand type, into smem
-            float lsum = 0.f;
-            const int r7 = tid & 7;
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                tmem_ld32(tS + lane_off + ch * 32, sc);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const bool v = full_tile || valid(ch * 32 + i);
-                    sc[i] = v ? ptx::ex2(sc[i] * sl2 - m_use) : 0.f;
-                }
-                uint8_t* base = (ch < 2 ? sP : sPhi) + tid * 128;
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {          // 4 chunks of 8 keys
-                    const int chunk = (ch & 1) * 4 + g;
-                    float r0, r1;
-                    uint4 u;
-                    u.x = Pack2<T>::pack(sc[g * 8 + 0], sc[g * 8 + 1], r0, r1); lsum += r0 + r1;
-                    u.y = Pack2<T>::pack(sc[g * 8 + 2], sc[g * 8 + 3], r0, r1); lsum += r0 + r1;
-                    u.z = Pack2<T>::pack(sc[g * 8 + 4], sc[g * 8 + 5], r0, r1); lsum += r0 + r1;
-                    u.w = Pack2<T>::pack(sc[g * 8 + 6], sc[g * 8 + 7], r0, r1); lsum += r0 + r1;
-                    *reinterpret_cast<uint4*>(base + ((chunk ^ r7) << 4)) = u;
-                }
-            }
-            l_run = l_run * alpha + lsum;
-            m_run = mx;
-        }
-        fence_proxy_async_smem();
-        tc_fence_before_sync();
-        __syncthreads();   // P complete; S consumed
-
-        if (tid == 0) {
-            tc_fence_after_sync();
-            wait(kBarV0 + s, (j >> 1) & 1);
-            const uint32_t ap = smem_u32(sP), aph = smem_u32(sPhi), av = smem_u32(sV(s));
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t a = (k < 4 ? ap : aph) + (k & 3) * 32;
-                mma_f16_ss(tO, smem_desc_sw128(a, 16, 1024),
-                           smem_desc_sw128(av + k * 2048, 8192, 1024), idPV, k > 0 ? 1u : 0u);
-            }
-            mma_commit(&bars[kBarO]);
-            if (j + 1 < ntl) {
-                wait(kBarK0 + (s ^ 1), ((j + 1) >> 1) & 1);
+            auto issue_pv = [&](int j) {
+                const int bf = j & 1, s = j % kStages;
+                wait(bar_p(bf), (j >> 1) & 1);
+                wait(bar_v(s), (j / kStages) & 1);
                 tc_fence_after_sync();
-                issue_s(s ^ 1);
-            }
-        }
-        wait(kBarO, j & 1);
-        tc_fence_after_sync();
-        if (warp_active) {
-            float ot[32];
+                const uint32_t tP = tmem + bf * 128;
+                const uint32_t av = smem_u32(sV(s));
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch) {
-                tmem_ld32(tO + lane_off + ch * 32, ot);
-                tmem_ld_wait();
+                for (int k = 0; k < 8; ++k)
+                    mma_f16_ts(tmem + kTmemO, tP + 8 * k, smem_desc_sw128(av + k * 2048, 8192, 1024),
+                               idPV, (j > 0 || k > 0) ? 1u : 0u);
+                if (kSplitP) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o_acc[ch * 32 + i] = o_acc[ch * 32 + i] * alpha + ot[i];
+                    for (int k = 0; k < 8; ++k)
+                        mma_f16_ts(tmem + kTmemO, tP + 64 + 8 * k,
+                                   smem_desc_sw128(av + k * 2048, 8192, 1024), idPV, 1u);
+                }
+                mma_commit(&bars[bar_o(bf)]);
+            };
+            mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
+            tma_load_4d(sQ, &tmQ, &bars[kBarQ], 0, q0, h, b);
+            for (int t = 0; t < min(kStages, ntl); ++t) issue_kv(t);
+            wait(kBarQ, 0);
+            const uint32_t aq = smem_u32(sQ);
+            for (int j = 0; j < ntl; ++j) {
+                const int bf = j & 1, s = j % kStages;
+                if (j >= 2) {
+                    // PV_{j-2} done: S/P buffer bf and stage (j-2)%kStages are free
+                    wait(bar_o(bf), ((j - 2) >> 1) & 1);
+                    if (j + 2 < ntl && j + 2 >= kStages) issue_kv(j + 2);
+                }
+                wait(bar_k(s), (j / kStages) & 1);
+                tc_fence_after_sync();
+                const uint32_t ak = smem_u32(sK(s));
+                const uint32_t tS = tmem + bf * 128;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16_ss(tS, smem_desc_sw128(aq + kk * 32, 16, 1024),
+                               smem_desc_sw128(ak + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+                mma_commit(&bars[bar_s(bf)]);
+                SFB_T(2 + 6 * j);
+                if (j >= 1) issue_pv(j - 1);
+                SFB_T(3 + 6 * j);
             }
+            issue_pv(ntl - 1);
         }
-        if (tid == 0 && j + 2 < ntl) issue_kv(s, t_begin + j + 2);
+    } else if (grp < groups) {
+        // ── softmax warps ───────────────────────────────────────────────────
+        const uint32_t lane_off = static_cast<uint32_t>(grp * 32) << 16;
+        const int qi = q0 + row;
+        const float sl2 = p.sl2;
+        const bool use_mask = p.key_mask != nullptr;
+        const uint32_t bar_id = 1 + grp;
+        for (int j = 0; j < ntl; ++j) {
+            const int bf = j & 1;
+            const uint32_t tS = tmem + bf * 128 + lane_off;
+            const int key0 = (t_begin + j) * kTileKeys + half * 64;
+            SFB_T(2 + 6 * j);
+            wait(bar_s(bf), (j >> 1) & 1);
+            SFB_T(3 + 6 * j);
+            tc_fence_after_sync();
+            float sc[64];
+            tmem_ld32(tS + half * 64, *reinterpret_cast<float(*)[32]>(&sc[0]));
+            tmem_ld32(tS + half * 64 + 32, *reinterpret_cast<float(*)[32]>(&sc[32]));
+            tmem_ld_wait();
+            const bool full = (key0 + 64 <= kend) && !use_mask && !p.causal;
+            if (!full) {
+                const uint8_t* mrow = use_mask ? p.key_mask + static_cast<int64_t>(b) * p.mask_sb : nullptr;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const int key = key0 + i;
+                    bool v = key < kend;
+                    if (use_mask && v) v = mrow[key] != 0;
+                    if (p.causal) v = v && key <= qi;
+                    if (!v) sc[i] = -INFINITY;
+                }
+            }
+            float mxa = sc[0], mxb = sc[1], mxc = sc[2], mxd = sc[3];
+#pragma unroll
+            for (int i = 4; i < 64; i += 4) {
+                mxa = fmaxf(mxa, sc[i]); mxb = fmaxf(mxb, sc[i + 1]);
+                mxc = fmaxf(mxc, sc[i + 2]); mxd = fmaxf(mxd, sc[i + 3]);
+            }
+            float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
+            // exchange the half-row max with the partner warp
+            red[(bf * 2 + half) * 128 + row] = mx;
+            tc_fence_before_sync();
+            SFB_T(4 + 6 * j);
+            named_bar_sync(bar_id, 64);
+            SFB_T(5 + 6 * j);
+            tc_fence_after_sync();
+            mx = fmaxf(mx, red[(bf * 2 + (half ^ 1)) * 128 + row]);
+            const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl2;
+            if (m_tile > m_ref + 8.f) {          // also true when m_ref == -inf
+                if (m_ref != -INFINITY) {
+                    const float alpha = ptx::ex2(m_ref - m_tile);
+                    l_run *= alpha;
+                    // O holds PV_0..PV_{j-1}: wait for PV_{j-1}, rescale our 32 columns
+                    wait(bar_o((j - 1) & 1), ((j - 1) >> 1) & 1);
+                    tc_fence_after_sync();
+                    float ot[32];
+                    tmem_ld32(tmem + kTmemO + lane_off + half * 32, ot);
+                    tmem_ld_wait();
+                    uint32_t ou[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(ot[i] * alpha);
+                    tmem_st32(tmem + kTmemO + lane_off + half * 32, ou);
+                }
+                m_ref = m_tile;
+            }
+            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+            uint32_t phi[32], plo[32];
+            float lsum0 = 0.f, lsum1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float p0 = ptx::ex2(fmaf(sc[2 * i], sl2, -m_use));
+                const float p1 = ptx::ex2(fmaf(sc[2 * i + 1], sl2, -m_use));
+                lsum0 += p0;
+                lsum1 += p1;
+                if (std::is_same<T, __nv_bfloat16>::value) {
+                    // hi = p truncated to bf16 (exact top 16 bits), lo = p - hi (exact in
+                    // fp32), truncated to bf16 as well: hi + lo carries 16 significant bits.
+                    const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
+                    const float lo0 = p0 - __uint_as_float(u0 & 0xffff0000u);
+                    const float lo1 = p1 - __uint_as_float(u1 & 0xffff0000u);
+                    phi[i] = ptx::prmt(u0, u1, 0x7632u);
+                    plo[i] = ptx::prmt(__float_as_uint(lo0), __float_as_uint(lo1), 0x7632u);
+                } else {
+                    phi[i] = HO::pack(p0, p1);
+                }
+            }
+            const float lsum = lsum0 + lsum1;
+            l_run += lsum;
+            // P_hi over S columns [0,64), P_lo over [64,128) of this buffer; the
+            // partner warp's S half was consumed before the named barrier.
+            SFB_T(6 + 6 * j);
+            tmem_st32(tS + half * 32, phi);
+            if (std::is_same<T, __nv_bfloat16>::value) tmem_st32(tS + 64 + half * 32, plo);
+            tmem_st_wait();
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[bar_p(bf)]);
+            SFB_T(7 + 6 * j);
+        }
+        // final O: wait for the last PV, read our 32 columns
+        if (ntl > 0) {
+            wait(bar_o((ntl - 1) & 1), ((ntl - 1) >> 1) & 1);
+            tc_fence_after_sync();
+            tmem_ld32(tmem + kTmemO + lane_off + half * 32, o_part);
+            tmem_ld_wait();
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o_part[i] = 0.f;
+        }
+        // full row sum
+        redl[half * 128 + row] = l_run;
+        named_bar_sync(bar_id, 64);
+        l_run += redl[(half ^ 1) * 128 + row];
     }
+    SFB_T(200);
 
     // ── epilogue ────────────────────────────────────────────────────────────
     T* out = static_cast<T*>(p.out);
     const int64_t row_base = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh;
+    const bool has_rows = warp < kSoftWarps && grp < groups && row < rows;
     if (p.splits == 1) {
-        if (tid < rows && ok) {
+        if (has_rows && ok) {
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            T* dst = out + row_base + static_cast<int64_t>(q0 + tid) * p.o_ss;
+            T* dst = out + row_base + static_cast<int64_t>(q0 + row) * p.o_ss + half * 32;
 #pragma unroll
-            for (int c = 0; c < 64; c += 8) {
-                float v[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = o_acc[c + i] * inv;
-                store_row8<T>(dst + c, v);
+            for (int c = 0; c < 32; c += 8) {
+                uint4 u;
+                u.x = HO::pack(o_part[c + 0] * inv, o_part[c + 1] * inv);
+                u.y = HO::pack(o_part[c + 2] * inv, o_part[c + 3] * inv);
+                u.z = HO::pack(o_part[c + 4] * inv, o_part[c + 5] * inv);
+                u.w = HO::pack(o_part[c + 6] * inv, o_part[c + 7] * inv);
+                *reinterpret_cast<uint4*>(dst + c) = u;
             }
         }
     } else {
-        float* sO = reinterpret_cast<float*>(smem + kOffCombO);
-        float* sM = reinterpret_cast<float*>(smem + kOffCombM);
-        float* sL = reinterpret_cast<float*>(smem + kOffCombL);
-        if (tid < rows) {
+        // Row r is owned by CTA r % C at slot r / C. Every CTA pushes its partial
+        // (O row, m, l) into the owner's shared memory with remote stores, one
+        // cluster barrier publishes them, and each owner merges its rows locally.
+        const int C = p.splits;
+        const int slots = (rows + C - 1) / C;
+        float* sO = reinterpret_cast<float*>(smem + kOffCombO);        // [C][slots][kOStride]
+        float* sM = sO + C * slots * kOStride;                         // [C][slots]
+        float* sL = sM + C * slots;                                    // [C][slots]
+        cluster_sync();   // every CTA is past its main loop: stage regions are free
+        if (has_rows) {
+            const int owner = row % C, slot = row / C;
+            const uint32_t dO = dsmem_map(smem_u32(sO + (split * slots + slot) * kOStride + half * 32), owner);
 #pragma unroll
-            for (int c = 0; c < 64; c += 4)
-                *reinterpret_cast<float4*>(sO + tid * kOStride + c) =
-                    make_float4(o_acc[c], o_acc[c + 1], o_acc[c + 2], o_acc[c + 3]);
-            sM[tid] = m_run;
-            sL[tid] = l_run;
+            for (int c = 0; c < 32; c += 4)
+                dsmem_st_f32x4(dO + c * 4, make_float4(o_part[c], o_part[c + 1], o_part[c + 2], o_part[c + 3]));
+            if (half == 0) {
+                dsmem_st_f32(dsmem_map(smem_u32(sM + split * slots + slot), owner), m_ref);
+                dsmem_st_f32(dsmem_map(smem_u32(sL + split * slots + slot), owner), l_run);
+            }
         }
         cluster_sync();
-        // CTA `split` merges rows split, split+C, ...; 16 threads per row, 4 columns each.
-        const int C   = p.splits;
-        const int sub = tid >> 4, c4 = (tid & 15) * 4;
-        const uint32_t aO = smem_u32(sO), aM = smem_u32(sM), aL = smem_u32(sL);
-        for (int row = split + sub * C; row < rows; row += 8 * C) {
+        const int nsub = kThreads / 16;
+        const int sub  = tid >> 4, c4 = (tid & 15) * 4;
+        for (int slot = sub; slot < slots; slot += nsub) {
+            const int r = slot * C + split;
+            if (r >= rows) break;
             float M = -INFINITY;
-            for (int r = 0; r < C; ++r) M = fmaxf(M, dsmem_ld_f32(dsmem_map(aM + row * 4, r)));
+            for (int k = 0; k < C; ++k) M = fmaxf(M, sM[k * slots + slot]);
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             float L = 0.f;
             if (M != -INFINITY) {
-                for (int r = 0; r < C; ++r) {
-                    const float mr = dsmem_ld_f32(dsmem_map(aM + row * 4, r));
-                    const float w  = ptx::ex2(mr - M);
-                    L += w * dsmem_ld_f32(dsmem_map(aL + row * 4, r));
-                    const float4 o = dsmem_ld_f32x4(dsmem_map(aO + (row * kOStride + c4) * 4, r));
+                for (int k = 0; k < C; ++k) {
+                    const float w = ptx::ex2(sM[k * slots + slot] - M);
+                    L += w * sL[k * slots + slot];
+                    const float4 o = *reinterpret_cast<const float4*>(sO + (k * slots + slot) * kOStride + c4);
                     acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
                 }
             }
             const float inv = L > 0.f ? 1.f / L : 0.f;
             if (ok) {
-                T* dst = out + row_base + static_cast<int64_t>(q0 + row) * p.o_ss + c4;
-                float d0, d1;
+                T* dst = out + row_base + static_cast<int64_t>(q0 + r) * p.o_ss + c4;
                 uint2 u;
-                u.x = Pack2<T>::pack(acc.x * inv, acc.y * inv, d0, d1);
-                u.y = Pack2<T>::pack(acc.z * inv, acc.w * inv, d0, d1);
+                u.x = HO::pack(acc.x * inv, acc.y * inv);
+                u.y = HO::pack(acc.z * inv, acc.w * inv);
                 *reinterpret_cast<uint2*>(dst) = u;
             }
         }
-        cluster_sync();   // keep this CTA's smem alive until every peer has read it
     }
 
+    SFB_T(201);
     if (!ok) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
     tc_fence_before_sync();
     __syncthreads();
@@ -386,12 +465,18 @@ static int make_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType d
                              CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+#ifdef SFB_TRACE
+static unsigned long long* g_trace_ptr = nullptr;
+extern "C" void sfb_debug_set_trace(void* p) { g_trace_ptr = static_cast<unsigned long long*>(p); }
+#endif
+
+// Cluster size along Lk: as many splits as keep every CTA co-resident in one
+// wave (one CTA per SM), at least two key tiles per split.
 int choose_attn_splits(int units, int ntiles_max, int num_sms) {
-    const int target = 2 * num_sms;   // two resident CTAs per SM
-    int s = (target + units - 1) / units;
+    int s = std::max(1, num_sms / std::max(units, 1));
     s = std::min(s, 16);
-    s = std::min(s, std::max(1, ntiles_max / 2));  // keep >= 2 tiles per split
-    return std::max(1, s);
+    s = std::min(s, std::max(1, ntiles_max / 2));
+    return s;
 }
 
 int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream) {
@@ -427,6 +512,9 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream) {
     p.kv_len = a.kv_len;
     p.key_mask = a.key_mask;
     p.mask_sb = a.key_mask_stride_b;
+#ifdef SFB_TRACE
+    p.trace = g_trace_ptr;
+#endif
     const int units = a.batch * a.heads * p.qtiles;
     const int ntiles_max = (a.seq_k + 127) / 128;
     p.splits = a.num_splits > 0 ? std::min(a.num_splits, 16)
