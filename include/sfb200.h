@@ -32,6 +32,7 @@ extern "C" {
 #define SFB_ERR_UNSUPPORTED   -7  /* no sm_100a device / feature missing    */
 #define SFB_ERR_CUDA          -8  /* other CUDA runtime error               */
 #define SFB_ERR_DEVICE_TIMEOUT -9 /* a bounded device-side wait expired     */
+#define SFB_ERR_RANGE        -10  /* input outside the kernel's value range */
 
 /* ── dtype codes (== sf::DType, reference dtype.h:11-19) ──────────────────── */
 #define SFB_F32   0
@@ -43,6 +44,10 @@ extern "C" {
 
 /* Human-readable message for a status code (static string). */
 const char* sfb_status_string(int status);
+
+/* Text of the last CUDA error this library saw on the calling thread
+ * ("" if none): the detail behind SFB_ERR_LAUNCH / SFB_ERR_CUDA. */
+const char* sfb_last_error(void);
 
 /* Library version string, e.g. "0.1.0 sm_100a". */
 const char* sfb_version(void);
@@ -78,6 +83,10 @@ int sfb_device_error(int* code, int reset);
  * - heads % heads_kv == 0 (grouped K/V heads, as flash_attn::mha_fwd's H_k).
  * - dtype: SFB_BF16 / SFB_F16 (tcgen05 tensor-core kernel, head_dim 64) or
  *   SFB_F32 (SIMT kernel, head_dim <= 128). q, k, v, out share the dtype.
+ * - Tensor-core path: softmax in fp32; the probabilities and V enter the P·V
+ *   product as fp16 (bf16 V is converted exactly in shared memory). bf16 V
+ *   entries beyond the fp16 range (|v| > 65504) are not supported: the kernel
+ *   then records SFB_ERR_RANGE in the device error word (sfb_device_error).
  */
 typedef struct sfb_attn_args {
     const void* q;

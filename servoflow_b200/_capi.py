@@ -23,6 +23,7 @@ SFB_ERR_LAUNCH = -6
 SFB_ERR_UNSUPPORTED = -7
 SFB_ERR_CUDA = -8
 SFB_ERR_DEVICE_TIMEOUT = -9
+SFB_ERR_RANGE = -10
 
 SFB_F32, SFB_F16, SFB_BF16, SFB_I8, SFB_I32, SFB_BOOL = 0, 1, 2, 3, 5, 6
 
@@ -60,7 +61,10 @@ class SfbError(RuntimeError):
 
     def __init__(self, status: int, what: str):
         self.status = status
-        super().__init__(f"{what}: {status_string(status)} (status {status})")
+        detail = ""
+        if status in (SFB_ERR_LAUNCH, SFB_ERR_CUDA):
+            detail = " — " + lib().sfb_last_error().decode()
+        super().__init__(f"{what}: {status_string(status)} (status {status}){detail}")
 
 
 _lib = None
@@ -71,6 +75,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     c = ctypes
     lib.sfb_status_string.restype = c.c_char_p
     lib.sfb_status_string.argtypes = [c.c_int]
+    lib.sfb_last_error.restype = c.c_char_p
+    lib.sfb_last_error.argtypes = []
     lib.sfb_version.restype = c.c_char_p
     lib.sfb_version.argtypes = []
     lib.sfb_device_error.restype = c.c_int

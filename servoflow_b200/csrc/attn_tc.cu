@@ -7,29 +7,46 @@
 // RDT-1B's shapes: Lq = 67 action tokens against Lk ∈ {67, 1024 (masked
 // language), 4374 (image)}.
 //
-// One CTA = 128 query rows × a contiguous range of 128-key tiles, 9 warps:
-//   * warp 8 (control): TMA loads (SWIZZLE_128B) of Q once and of K/V tiles
-//     through a 4-deep ring, and every tcgen05.mma: S_j = Q·K_jᵀ (M=128,
-//     N=128, K=64) into one of two TMEM S/P buffers, then O += P_j·V_j
-//     (M=128, N=64, K=128) with P read from TMEM and O accumulated in TMEM
-//     across all tiles.
-//   * warps 0-7 (softmax): warps w and w+4 share TMEM lanes 32·(w%4)..+31
-//     (query rows) and split the 128 key columns in halves; the row max is
-//     exchanged through shared memory under a 64-thread named barrier.
-//     P is written back over S in TMEM as two bf16 (or fp16) parts,
-//     P = P_hi + P_lo, both multiplied into V, so the probabilities keep
-//     ~16 significant bits (plain bf16 P costs up to 2^-9 relative per weight,
-//     6e-3 absolute on few-key rows). The running max is a lazy reference:
-//     O in TMEM is rescaled only when a tile raises the max by more than
-//     8 (log2 units).
-//   * Only warps whose rows hold queries work (Lq = 67 → 6 of 8).
+// One CTA = 128 query rows × a contiguous range of 128-key tiles, 12 warps:
+//   * warp 11 (control): TMA loads (SWIZZLE_128B) of Q once and of K/V tiles
+//     through a 5-deep ring, and every tcgen05.mma: S_j = Q·K_jᵀ (M=128,
+//     N=128, K=64) into TMEM, then O_g += P_j·V_j (M=128, N=64, K=128) with
+//     P read from TMEM. It runs an event loop (non-blocking mbarrier probes)
+//     that issues whichever of {K/V refill, next S, next P·V} is ready, and it
+//     sits alone on SM sub-partition 3 whenever Lq <= 96 (the softmax warps of
+//     rows 96..127 are then idle), so its spinning steals no issue slots.
+//   * Two softmax groups ping-pong over the key tiles, FlashAttention-4 style
+//     but along Lk (there is a single 67-row Q tile): group g (warps 4g..4g+3)
+//     takes the tiles j ≡ g (mod 2), owns accumulator O_g and keeps its own
+//     running max / sum. Thread = query row = TMEM lane, so row reductions
+//     are thread-local and the two groups never wait for each other; their
+//     latencies overlap. O_A and O_B are merged once at the end.
+//   * P is written to TMEM as fp16 (11 significant bits; a bf16 P, 8 bits,
+//     costs up to 2^-9 relative per weight — 6e-3 absolute on few-key rows).
+//     The P·V product therefore runs in fp16: for bf16 inputs, warps 8..10
+//     convert each V tile to fp16 in shared memory (exact for |v| <= 65504;
+//     larger values record SFB_ERR_RANGE). The running max is a lazy
+//     reference: O_g in TMEM is rescaled only when a tile raises the max by
+//     more than 8 (log2 units), which keeps P <= 256.
+//   * Only warps whose rows hold queries work (Lq = 67 → 3 of 4 per group).
 //   * Split-K over Lk: the CTAs of one (batch, head, q-tile) form a thread-
-//     block cluster; each keeps (O, m, l) for its key range, and the partials
-//     are merged through distributed shared memory. No global scratch, no
-//     atomics, no inter-CTA spin waits (cluster barriers are hardware).
+//     block cluster; each pushes its (O, m, l) rows into the owning CTA's
+//     dedicated merge buffer with remote shared-memory stores, one cluster
+//     barrier publishes them, and each owner merges its rows locally. No
+//     global scratch, no atomics, no inter-CTA spin waits.
 //
-// TMEM (512 columns): S/P buffer 0 at [0,128), buffer 1 at [128,256)
-// (P_hi over columns [0,64) of a buffer, P_lo over [64,128)), O at [256,320).
+// TMEM (512 columns): three S/P buffers at [128u, 128u+128) — tile j uses
+// buffer j mod 3, so a tile's S MMA waits only for the P·V three tiles back;
+// the fp16 P of keys [32c, 32c+32) overwrites the first 16 of that chunk's
+// own 32 S columns — and O_g at [384+64g, 448+64g). Three warps per SM
+// sub-partition cap a thread at 168 registers: S is read in 32-column chunks,
+// twice (row max, then exponentials), and the hot loop is kept compact
+// (rolled chunk loops; masked keys are set to -inf in TMEM during the first
+// pass), because instruction-fetch stalls dominated a fully unrolled form.
+//
+// Measured on B200 while designing this (microbenchmarks): MUFU ex2 runs at
+// 16 results/clk/SM; tcgen05.mma M=128 at N=64 takes 48 cycles (66% of peak)
+// and at N>=128 runs at full rate, with A from TMEM as fast as from smem.
 //
 // Every mbarrier wait is bounded (1 s); after an expiry a thread stops
 // waiting, skips its output and records SFB_ERR_DEVICE_TIMEOUT in
@@ -59,65 +76,91 @@ namespace attn_tc {
 
 #ifdef SFB_TRACE
 #define SFB_T(i) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && \
-                          (threadIdx.x == 0 || threadIdx.x == 256)) { \
-        p.trace[(threadIdx.x == 0 ? 0 : 256) + (i)] = clock64(); } } while (0)
+                          (threadIdx.x == 0 || threadIdx.x == 128 || threadIdx.x == 352)) { \
+        p.trace[(threadIdx.x == 352 ? 2 : threadIdx.x / 128) * 170 + (i)] = clock64(); } } while (0)
 #else
 #define SFB_T(i) do { } while (0)
 #endif
 
 constexpr int kSoftWarps = 8;
-constexpr int kCtrlWarp  = 8;
-constexpr int kThreads   = (kSoftWarps + 1) * 32;          // 288
-constexpr int kStages    = 4;
+constexpr int kConvWarp0 = 8;                               // warps 8..10: bf16 V → fp16
+constexpr int kConvWarps = 3;
+constexpr int kCtrlWarp  = 11;                              // 11 % 4 == 3
+constexpr int kThreads   = 12 * 32;                         // 384
+constexpr int kStages    = 5;
+constexpr int kBufs      = 3;                               // TMEM S/P buffers
 constexpr int kTileKeys  = 128;
 constexpr int kTileBytes = 128 * 128;                       // 128 rows × 64 halves
+constexpr int kMaxSplits = 16;
+constexpr int kOStride   = 36;                              // floats per merge half-row
+constexpr int kMergeRows = 128 + kMaxSplits - 1;            // row slots over all sources
 constexpr int kOffQ      = 0;
 constexpr int kOffStage  = kOffQ + kTileBytes;              // [kStages] × (K, V)
-constexpr int kOffBar    = kOffStage + kStages * 2 * kTileBytes;
-constexpr int kNumBars   = 1 + 2 * kStages + 2 + 2 + 2;
-constexpr int kOffTmem   = kOffBar + 8 * 16;
-constexpr int kOffRed    = kOffTmem + 16;                   // float [2][2][128] row max
-constexpr int kOffRedL   = kOffRed + 2 * 2 * 128 * 4;       // float [2][128] row sum
-constexpr int kSmemUsed  = kOffRedL + 2 * 128 * 4;
+constexpr int kOffMerge  = kOffStage + kStages * 2 * kTileBytes;
+constexpr int kMergeBytes = kMergeRows * (2 * kOStride + 2) * 4;
+constexpr int kOffBar    = kOffMerge + kMergeBytes;
+constexpr int kOffTmem   = kOffBar + 8 * 32;
+constexpr int kOffRed    = kOffTmem + 16;                   // float [2 groups][m|l][128]
+constexpr int kSmemUsed  = kOffRed + 2 * 2 * 128 * 4;
 constexpr int kSmemBytes = kSmemUsed + 1024;                // + alignment slack
 constexpr int kTmemCols  = 512;
-constexpr uint32_t kTmemO = 256;
-// Split-K merge buffers reuse the stage region once the main loop is done.
-constexpr int kOStride   = 68;                              // floats per row
-constexpr int kOffCombO  = kOffStage;
-// at most rows + C - 1 <= 143 row slots of (O row, m, l)
-static_assert(143 * (kOStride + 2) * 4 <= kStages * 2 * kTileBytes, "merge buffers must fit in the stage region");
-static_assert(kNumBars <= 16, "barrier area");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kOffBar % 8 == 0, "barrier alignment");
 
 // barrier indices
 constexpr int kBarQ = 0;
 __host__ __device__ constexpr int bar_k(int s) { return 1 + s; }
 __host__ __device__ constexpr int bar_v(int s) { return 1 + kStages + s; }
-__host__ __device__ constexpr int bar_s(int b) { return 1 + 2 * kStages + b; }      // S_j ready
-__host__ __device__ constexpr int bar_p(int b) { return 3 + 2 * kStages + b; }      // P_j written
-__host__ __device__ constexpr int bar_o(int b) { return 5 + 2 * kStages + b; }      // PV_j done
+__host__ __device__ constexpr int bar_vc(int s) { return 1 + 2 * kStages + s; }              // V in fp16
+__host__ __device__ constexpr int bar_s(int u) { return 1 + 3 * kStages + u; }               // S_j ready
+__host__ __device__ constexpr int bar_p(int u) { return 1 + 3 * kStages + kBufs + u; }       // P_j written
+__host__ __device__ constexpr int bar_o(int u) { return 1 + 3 * kStages + 2 * kBufs + u; }   // PV_j done
+__host__ __device__ constexpr int bar_og(int g) { return 1 + 3 * kStages + 3 * kBufs + g; }  // group's PV done
+constexpr int kNumBars = 3 + 3 * kStages + 3 * kBufs;
+static_assert(kNumBars <= 32, "barrier area");
 
 template <typename T> struct HalfOps;
 template <> struct HalfOps<__nv_bfloat16> {
-    static constexpr uint32_t kFmt = 1;
     static __device__ __forceinline__ uint32_t pack(float a, float b) {
         __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
         return *reinterpret_cast<uint32_t*>(&v);
     }
-    static __device__ __forceinline__ float2 unpack(uint32_t u) {
-        return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
-    }
 };
 template <> struct HalfOps<__half> {
-    static constexpr uint32_t kFmt = 0;
     static __device__ __forceinline__ uint32_t pack(float a, float b) {
         __half2 v = __floats2half2_rn(a, b);
         return *reinterpret_cast<uint32_t*>(&v);
     }
-    static __device__ __forceinline__ float2 unpack(uint32_t u) {
-        return __half22float2(*reinterpret_cast<__half2*>(&u));
-    }
 };
+
+// Validity bits of keys [key, key+32) for one query row: key < kend_row and,
+// with a key-padding mask, a nonzero mask byte. Mask rows are read 16 bytes
+// at a time when aligned.
+__device__ __forceinline__ uint32_t key_bits(const AttnTcParams& p, int b, int key, int kend_row) {
+    const int n = kend_row - key;
+    uint32_t bits = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+    if (p.key_mask != nullptr && bits != 0u) {
+        const uint8_t* m = p.key_mask + static_cast<int64_t>(b) * p.mask_sb + key;
+        uint32_t mb = 0;
+        if ((reinterpret_cast<uintptr_t>(m) & 15u) == 0 && key + 32 <= p.Lk) {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(m);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(m + 16);
+            const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                // one bit per nonzero byte, gathered into 4 bits
+                const uint32_t nz = (__vcmpne4(w[q], 0u) & 0x01010101u) * 0x01020408u;
+                mb |= ((nz >> 24) & 0xfu) << (4 * q);
+            }
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < 32; ++i)
+                if (key + i < p.Lk && m[i] != 0) mb |= 1u << i;
+        }
+        bits &= mb;
+    }
+    return bits;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -127,14 +170,15 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const AttnTcParams p) {
     using namespace ptx;
     using HO = HalfOps<T>;
+    constexpr bool kConvV = std::is_same<T, __nv_bfloat16>::value;   // bf16 V needs an fp16 copy
+    constexpr uint32_t kFmtQK = kConvV ? 1u : 0u;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t*  sQ   = smem + kOffQ;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffTmem);
-    float*    red  = reinterpret_cast<float*>(smem + kOffRed);     // [2 parity][2 half][128]
-    float*    redl = reinterpret_cast<float*>(smem + kOffRedL);    // [2 half][128]
+    float*    red  = reinterpret_cast<float*>(smem + kOffRed);
     auto sK = [&](int s) { return smem + kOffStage + (2 * s) * kTileBytes; };
     auto sV = [&](int s) { return smem + kOffStage + (2 * s + 1) * kTileBytes; };
 
@@ -148,8 +192,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int hk    = h / (p.H / p.Hkv);
     const int q0    = qt * 128;
     const int rows  = min(128, p.Lq - q0);
-    const int groups = (rows + 31) >> 5;            // active 32-row groups
-    const int nsoft  = 2 * groups;                  // active softmax warps
+    const int groups = (rows + 31) >> 5;            // active 32-row windows per group
 
     // Key range of this (batch, q-tile), then this CTA's share of its tiles.
     int kend = p.Lk;
@@ -164,12 +207,18 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     SFB_T(0);
     if (tid == kCtrlWarp * 32) {
         mbar_init(&bars[kBarQ], 1);
-        for (int s = 0; s < kStages; ++s) { mbar_init(&bars[bar_k(s)], 1); mbar_init(&bars[bar_v(s)], 1); }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars[bar_s(i)], 1);
-            mbar_init(&bars[bar_p(i)], nsoft);
-            mbar_init(&bars[bar_o(i)], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars[bar_k(s)], 1);
+            mbar_init(&bars[bar_v(s)], 1);
+            mbar_init(&bars[bar_vc(s)], kConvWarps);
         }
+        for (int u = 0; u < kBufs; ++u) {
+            mbar_init(&bars[bar_s(u)], 1);
+            mbar_init(&bars[bar_p(u)], groups);
+            mbar_init(&bars[bar_o(u)], 1);
+        }
+        mbar_init(&bars[bar_og(0)], 1);
+        mbar_init(&bars[bar_og(1)], 1);
         fence_mbarrier_init();
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -190,227 +239,286 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (!mbar_wait(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
     };
 
-    float o_part[32];                   // this thread's 32 output columns (softmax warps)
+    const int win = warp & 3;            // 32-lane window = row block
+    const int grp = (warp >> 2) & 1;     // softmax group (tile parity)
+    const int row = win * 32 + lane;
     float m_ref = -INFINITY, l_run = 0.f;
-    const int grp  = warp & 3;          // row group
-    const int half = warp >> 2;         // key-column half (softmax warps)
-    const int row  = grp * 32 + lane;
 
     if (warp == kCtrlWarp) {
         // ── control warp: TMA + MMA issue (one thread) ──────────────────────
         if (lane == 0 && ntl > 0) {
-            constexpr uint32_t idS  = idesc_f16(128, 128, HO::kFmt, 0, 0);  // Q·Kᵀ, both K-major
-            constexpr uint32_t idPV = idesc_f16(128, 64, HO::kFmt, 0, 1);   // P(tmem)·V(MN-major)
-            constexpr bool kSplitP  = std::is_same<T, __nv_bfloat16>::value;
-            auto issue_kv = [&](int tile_idx) {
-                const int s = tile_idx % kStages;
-                const int key0 = (t_begin + tile_idx) * kTileKeys;
+            constexpr uint32_t idS  = idesc_f16(128, 128, kFmtQK, 0, 0);  // Q·Kᵀ, both K-major
+            constexpr uint32_t idPV = idesc_f16(128, 64, 0, 0, 1);        // P(tmem)·V(MN-major), fp16
+            auto issue_kv = [&](int t) {
+                const int s = t % kStages;
+                const int key0 = (t_begin + t) * kTileKeys;
                 mbar_arrive_expect_tx(&bars[bar_k(s)], kTileBytes);
                 tma_load_4d(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b);
                 mbar_arrive_expect_tx(&bars[bar_v(s)], kTileBytes);
                 tma_load_4d(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b);
             };
-            auto issue_pv = [&](int j) {
-                const int bf = j & 1, s = j % kStages;
-                wait(bar_p(bf), (j >> 1) & 1);
-                wait(bar_v(s), (j / kStages) & 1);
+            const uint32_t aq = smem_u32(sQ);
+            auto issue_s = [&](int j) {
+                const int u = j % kBufs, s = j % kStages;
                 tc_fence_after_sync();
-                const uint32_t tP = tmem + bf * 128;
+                const uint32_t ak = smem_u32(sK(s));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16_ss(tmem + u * 128, smem_desc_sw128(aq + kk * 32, 16, 1024),
+                               smem_desc_sw128(ak + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+                mma_commit(&bars[bar_s(u)]);
+            };
+            auto issue_pv = [&](int j) {
+                const int u = j % kBufs, g = j & 1, s = j % kStages;
+                tc_fence_after_sync();
+                const uint32_t tP = tmem + u * 128, tO = tmem + 384 + g * 64;
                 const uint32_t av = smem_u32(sV(s));
+                // fp16 P of keys [32c, 32c+32) sits in columns 32c..32c+15
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    mma_f16_ts(tmem + kTmemO, tP + 8 * k, smem_desc_sw128(av + k * 2048, 8192, 1024),
-                               idPV, (j > 0 || k > 0) ? 1u : 0u);
-                if (kSplitP) {
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        mma_f16_ts(tmem + kTmemO, tP + 64 + 8 * k,
-                                   smem_desc_sw128(av + k * 2048, 8192, 1024), idPV, 1u);
-                }
-                mma_commit(&bars[bar_o(bf)]);
+                    mma_f16_ts(tO, tP + 32 * (k >> 1) + 8 * (k & 1),
+                               smem_desc_sw128(av + k * 2048, 8192, 1024), idPV,
+                               (j >= 2 || k > 0) ? 1u : 0u);
+                mma_commit(&bars[bar_o(u)]);
+                mma_commit(&bars[bar_og(g)]);
             };
             mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
             tma_load_4d(sQ, &tmQ, &bars[kBarQ], 0, q0, h, b);
-            for (int t = 0; t < min(kStages, ntl); ++t) issue_kv(t);
+            int nL = min(kStages, ntl);                // tiles whose K/V load is issued
+            for (int t = 0; t < nL; ++t) issue_kv(t);
             wait(kBarQ, 0);
-            const uint32_t aq = smem_u32(sQ);
-            for (int j = 0; j < ntl; ++j) {
-                const int bf = j & 1, s = j % kStages;
-                if (j >= 2) {
-                    // PV_{j-2} done: S/P buffer bf and stage (j-2)%kStages are free
-                    wait(bar_o(bf), ((j - 2) >> 1) & 1);
-                    if (j + 2 < ntl && j + 2 >= kStages) issue_kv(j + 2);
+            // Event loop. P·V completions are retired in issue order, so every
+            // parity probe is at most one phase behind its barrier.
+            int nS = 0, nP = 0, pv_done = 0;
+            const uint64_t t_start = global_timer_ns();
+            uint32_t idle = 0;
+            while (nP < ntl && ok) {
+                bool progress = false;
+                while (pv_done < nP && mbar_test(&bars[bar_o(pv_done % kBufs)], (pv_done / kBufs) & 1))
+                    ++pv_done;
+                // stage of tile t is free once P·V of tile t - kStages is done
+                while (nL < ntl && nL - kStages < pv_done) { issue_kv(nL); ++nL; progress = true; }
+                // S/P buffer of tile j is free once P·V of tile j - kBufs is done
+                if (nS < ntl && (nS < kBufs || nS - kBufs < pv_done) &&
+                    mbar_test(&bars[bar_k(nS % kStages)], (nS / kStages) & 1)) {
+                    issue_s(nS);
+                    SFB_T(2 + 4 * nS);
+                    ++nS;
+                    progress = true;
                 }
-                wait(bar_k(s), (j / kStages) & 1);
-                tc_fence_after_sync();
-                const uint32_t ak = smem_u32(sK(s));
-                const uint32_t tS = tmem + bf * 128;
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16_ss(tS, smem_desc_sw128(aq + kk * 32, 16, 1024),
-                               smem_desc_sw128(ak + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
-                mma_commit(&bars[bar_s(bf)]);
-                SFB_T(2 + 6 * j);
-                if (j >= 1) issue_pv(j - 1);
-                SFB_T(3 + 6 * j);
+                if (nP < nS && mbar_test(&bars[bar_p(nP % kBufs)], (nP / kBufs) & 1) &&
+                    mbar_test(&bars[kConvV ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
+                              (nP / kStages) & 1)) {
+                    issue_pv(nP);
+                    SFB_T(3 + 4 * nP);
+                    ++nP;
+                    progress = true;
+                }
+                if (progress) { idle = 0; continue; }
+                if ((++idle & 1023u) == 1023u && global_timer_ns() - t_start > 1000000000ull) ok = false;
             }
-            issue_pv(ntl - 1);
         }
-    } else if (grp < groups) {
-        // ── softmax warps ───────────────────────────────────────────────────
-        const uint32_t lane_off = static_cast<uint32_t>(grp * 32) << 16;
+    } else if (kConvV && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
+        // ── V conversion warps: bf16 → fp16 in place (same swizzled layout) ──
+        const int ct = (warp - kConvWarp0) * 32 + lane;
+        uint32_t bad = 0;
+        for (int t = 0; t < ntl; ++t) {
+            const int s = t % kStages;
+            wait(bar_v(s), (t / kStages) & 1);
+            uint4* v4 = reinterpret_cast<uint4*>(sV(s));
+#pragma unroll 2
+            for (int i = ct; i < kTileBytes / 16; i += kConvWarps * 32) {
+                uint4 w = v4[i];
+                uint32_t* q = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float lo = __uint_as_float(q[e] << 16), hi = __uint_as_float(q[e] & 0xffff0000u);
+                    bad |= (fabsf(lo) > 65504.f) | (fabsf(hi) > 65504.f);
+                    q[e] = HalfOps<__half>::pack(lo, hi);
+                }
+                v4[i] = w;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[bar_vc(s)]);
+        }
+        if (__any_sync(0xffffffffu, bad != 0) && lane == 0) atomicExch(&g_sfb_device_error, SFB_ERR_RANGE);
+    } else if (warp < kSoftWarps && win < groups) {
+        // ── softmax group grp: tiles j ≡ grp (mod 2) ────────────────────────
+        const uint32_t lane_off = static_cast<uint32_t>(win * 32) << 16;
+        const uint32_t tO = tmem + 384 + grp * 64 + lane_off;
         const int qi = q0 + row;
+        const int kend_row = p.causal ? min(kend, qi + 1) : kend;
         const float sl2 = p.sl2;
         const bool use_mask = p.key_mask != nullptr;
-        const uint32_t bar_id = 1 + grp;
-        for (int j = 0; j < ntl; ++j) {
-            const int bf = j & 1;
-            const uint32_t tS = tmem + bf * 128 + lane_off;
-            const int key0 = (t_begin + j) * kTileKeys + half * 64;
-            SFB_T(2 + 6 * j);
-            wait(bar_s(bf), (j >> 1) & 1);
-            SFB_T(3 + 6 * j);
+        int uses = 0;
+        for (int j = grp; j < ntl; j += 2, ++uses) {
+            const int key0 = (t_begin + j) * kTileKeys;
+            const int u = j % kBufs;
+            const uint32_t tS = tmem + u * 128 + lane_off;
+            SFB_T(2 + 4 * uses);
+            wait(bar_s(u), (j / kBufs) & 1);
+            SFB_T(3 + 4 * uses);
             tc_fence_after_sync();
-            float sc[64];
-            tmem_ld32(tS + half * 64, *reinterpret_cast<float(*)[32]>(&sc[0]));
-            tmem_ld32(tS + half * 64 + 32, *reinterpret_cast<float(*)[32]>(&sc[32]));
-            tmem_ld_wait();
-            const bool full = (key0 + 64 <= kend) && !use_mask && !p.causal;
-            if (!full) {
-                const uint8_t* mrow = use_mask ? p.key_mask + static_cast<int64_t>(b) * p.mask_sb : nullptr;
+            const bool full = (key0 + kTileKeys <= kend) && !use_mask && !p.causal;
+            // pass 1: row max of the raw logits. In a tile with invalid keys
+            // (beyond kv_len, masked, or causal) those logits are replaced by
+            // -inf in TMEM first, so pass 2 is the same code for every tile.
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                float a[32], bb[32];
+                tmem_ld32(tS + 64 * hh, a);
+                tmem_ld32(tS + 64 * hh + 32, bb);
+                tmem_ld_wait();
+                if (!full) {
+                    const uint32_t va = key_bits(p, b, key0 + 64 * hh, kend_row);
+                    const uint32_t vb = key_bits(p, b, key0 + 64 * hh + 32, kend_row);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const int key = key0 + i;
-                    bool v = key < kend;
-                    if (use_mask && v) v = mrow[key] != 0;
-                    if (p.causal) v = v && key <= qi;
-                    if (!v) sc[i] = -INFINITY;
+                    for (int i = 0; i < 32; ++i) {
+                        a[i]  = (va >> i) & 1u ? a[i] : -INFINITY;
+                        bb[i] = (vb >> i) & 1u ? bb[i] : -INFINITY;
+                    }
+                    tmem_st32(tS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(a));
+                    tmem_st32(tS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(bb));
                 }
-            }
-            float mxa = sc[0], mxb = sc[1], mxc = sc[2], mxd = sc[3];
 #pragma unroll
-            for (int i = 4; i < 64; i += 4) {
-                mxa = fmaxf(mxa, sc[i]); mxb = fmaxf(mxb, sc[i + 1]);
-                mxc = fmaxf(mxc, sc[i + 2]); mxd = fmaxf(mxd, sc[i + 3]);
+                for (int i = 0; i < 32; ++i) { mx0 = fmaxf(mx0, a[i]); mx1 = fmaxf(mx1, bb[i]); }
             }
-            float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
-            // exchange the half-row max with the partner warp
-            red[(bf * 2 + half) * 128 + row] = mx;
-            tc_fence_before_sync();
-            SFB_T(4 + 6 * j);
-            named_bar_sync(bar_id, 64);
-            SFB_T(5 + 6 * j);
-            tc_fence_after_sync();
-            mx = fmaxf(mx, red[(bf * 2 + (half ^ 1)) * 128 + row]);
-            const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl2;
+            if (!full) tmem_st_wait();
+            const float mraw = fmaxf(mx0, mx1);
+            const float m_tile = mraw == -INFINITY ? -INFINITY : mraw * sl2;
             if (m_tile > m_ref + 8.f) {          // also true when m_ref == -inf
                 if (m_ref != -INFINITY) {
                     const float alpha = ptx::ex2(m_ref - m_tile);
                     l_run *= alpha;
-                    // O holds PV_0..PV_{j-1}: wait for PV_{j-1}, rescale our 32 columns
-                    wait(bar_o((j - 1) & 1), ((j - 1) >> 1) & 1);
+                    // O_grp holds this group's earlier tiles: wait for its last PV
+                    wait(bar_og(grp), (uses - 1) & 1);
                     tc_fence_after_sync();
-                    float ot[32];
-                    tmem_ld32(tmem + kTmemO + lane_off + half * 32, ot);
-                    tmem_ld_wait();
-                    uint32_t ou[32];
+#pragma unroll 1
+                    for (int c = 0; c < 2; ++c) {
+                        float ot[32];
+                        tmem_ld32(tO + 32 * c, ot);
+                        tmem_ld_wait();
+                        uint32_t ou[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(ot[i] * alpha);
-                    tmem_st32(tmem + kTmemO + lane_off + half * 32, ou);
+                        for (int i = 0; i < 32; ++i) ou[i] = __float_as_uint(ot[i] * alpha);
+                        tmem_st32(tO + 32 * c, ou);
+                    }
                 }
                 m_ref = m_tile;
             }
             const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-            uint32_t phi[32], plo[32];
-            float lsum0 = 0.f, lsum1 = 0.f;
+            SFB_T(4 + 4 * uses);
+            // pass 2: P = 2^(s·scale·log2e − m) in 32-key chunks; the next chunk's
+            // TMEM load is in flight while the current one is computed. The fp16
+            // P of chunk c overwrites S columns [32c, 32c+16), already read.
+            float lacc0 = 0.f, lacc1 = 0.f;
+            auto chunk = [&](const float (&v)[32], int c) {
+                uint32_t ph[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float p0 = ptx::ex2(fmaf(sc[2 * i], sl2, -m_use));
-                const float p1 = ptx::ex2(fmaf(sc[2 * i + 1], sl2, -m_use));
-                lsum0 += p0;
-                lsum1 += p1;
-                if (std::is_same<T, __nv_bfloat16>::value) {
-                    // hi = p truncated to bf16 (exact top 16 bits), lo = p - hi (exact in
-                    // fp32), truncated to bf16 as well: hi + lo carries 16 significant bits.
-                    const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
-                    const float lo0 = p0 - __uint_as_float(u0 & 0xffff0000u);
-                    const float lo1 = p1 - __uint_as_float(u1 & 0xffff0000u);
-                    phi[i] = ptx::prmt(u0, u1, 0x7632u);
-                    plo[i] = ptx::prmt(__float_as_uint(lo0), __float_as_uint(lo1), 0x7632u);
-                } else {
-                    phi[i] = HO::pack(p0, p1);
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = ptx::ex2(fmaf(v[2 * i], sl2, -m_use));
+                    const float p1 = ptx::ex2(fmaf(v[2 * i + 1], sl2, -m_use));
+                    lacc0 += p0;
+                    lacc1 += p1;
+                    ph[i] = HalfOps<__half>::pack(p0, p1);
                 }
+                tmem_st16(tS + 32 * c, ph);
+            };
+            float ca[32], cb[32];
+            tmem_ld32(tS, ca);
+            tmem_ld_wait();
+#pragma unroll 1
+            for (int c = 0; c < 4; c += 2) {
+                tmem_ld32(tS + 32 * (c + 1), cb);
+                chunk(ca, c);
+                tmem_ld_wait();
+                if (c + 2 < 4) tmem_ld32(tS + 32 * (c + 2), ca);
+                chunk(cb, c + 1);
+                if (c + 2 < 4) tmem_ld_wait();
             }
-            const float lsum = lsum0 + lsum1;
-            l_run += lsum;
-            // P_hi over S columns [0,64), P_lo over [64,128) of this buffer; the
-            // partner warp's S half was consumed before the named barrier.
-            SFB_T(6 + 6 * j);
-            tmem_st32(tS + half * 32, phi);
-            if (std::is_same<T, __nv_bfloat16>::value) tmem_st32(tS + 64 + half * 32, plo);
+            l_run += lacc0 + lacc1;
             tmem_st_wait();
             tc_fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[bar_p(bf)]);
-            SFB_T(7 + 6 * j);
+            if (lane == 0) mbar_arrive(&bars[bar_p(u)]);
+            SFB_T(5 + 4 * uses);
         }
-        // final O: wait for the last PV, read our 32 columns
-        if (ntl > 0) {
-            wait(bar_o((ntl - 1) & 1), ((ntl - 1) >> 1) & 1);
-            tc_fence_after_sync();
-            tmem_ld32(tmem + kTmemO + lane_off + half * 32, o_part);
-            tmem_ld_wait();
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o_part[i] = 0.f;
-        }
-        // full row sum
-        redl[half * 128 + row] = l_run;
-        named_bar_sync(bar_id, 64);
-        l_run += redl[(half ^ 1) * 128 + row];
+        // publish (m, l) of this group for the in-CTA merge
+        red[(grp * 2 + 0) * 128 + row] = m_ref;
+        red[(grp * 2 + 1) * 128 + row] = l_run;
     }
-    SFB_T(200);
+    SFB_T(160);
+    __syncthreads();    // (m, l) of both groups visible
+    SFB_T(161);
+
+    // ── merge O_A and O_B: group g's threads take output columns [32g, 32g+32)
+    float o_row[32];
+    const bool has_rows = warp < kSoftWarps && win < groups && row < rows;
+    if (warp < kSoftWarps && win < groups) {
+        const uint32_t lane_off = static_cast<uint32_t>(win * 32) << 16;
+        const float mA = red[0 * 128 + row], lA = red[1 * 128 + row];
+        const float mB = red[2 * 128 + row], lB = red[3 * 128 + row];
+        const float M  = fmaxf(mA, mB);
+        const float wA = (mA == -INFINITY) ? 0.f : ptx::ex2(mA - M);
+        const float wB = (mB == -INFINITY) ? 0.f : ptx::ex2(mB - M);
+        // wait for the last PV of each group that had tiles
+        if (ntl >= 1) wait(bar_og(0), ((ntl + 1) / 2 - 1) & 1);
+        if (ntl >= 2) wait(bar_og(1), (ntl / 2 - 1) & 1);
+        tc_fence_after_sync();
+        float a[32], bb[32];
+        tmem_ld32(tmem + 384 + lane_off + 32 * grp, a);
+        tmem_ld32(tmem + 448 + lane_off + 32 * grp, bb);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            o_row[i] = (wA != 0.f ? wA * a[i] : 0.f) + (wB != 0.f ? wB * bb[i] : 0.f);
+        m_ref = M;
+        l_run = wA * lA + wB * lB;
+    }
+    SFB_T(162);
 
     // ── epilogue ────────────────────────────────────────────────────────────
     T* out = static_cast<T*>(p.out);
     const int64_t row_base = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh;
-    const bool has_rows = warp < kSoftWarps && grp < groups && row < rows;
     if (p.splits == 1) {
         if (has_rows && ok) {
-            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            T* dst = out + row_base + static_cast<int64_t>(q0 + row) * p.o_ss + half * 32;
+            const float inv = (l_run > 0.f && m_ref != -INFINITY) ? 1.f / l_run : 0.f;
+            T* dst = out + row_base + static_cast<int64_t>(q0 + row) * p.o_ss + 32 * grp;
 #pragma unroll
             for (int c = 0; c < 32; c += 8) {
                 uint4 u;
-                u.x = HO::pack(o_part[c + 0] * inv, o_part[c + 1] * inv);
-                u.y = HO::pack(o_part[c + 2] * inv, o_part[c + 3] * inv);
-                u.z = HO::pack(o_part[c + 4] * inv, o_part[c + 5] * inv);
-                u.w = HO::pack(o_part[c + 6] * inv, o_part[c + 7] * inv);
+                u.x = HO::pack(o_row[c + 0] * inv, o_row[c + 1] * inv);
+                u.y = HO::pack(o_row[c + 2] * inv, o_row[c + 3] * inv);
+                u.z = HO::pack(o_row[c + 4] * inv, o_row[c + 5] * inv);
+                u.w = HO::pack(o_row[c + 6] * inv, o_row[c + 7] * inv);
                 *reinterpret_cast<uint4*>(dst + c) = u;
             }
         }
     } else {
-        // Row r is owned by CTA r % C at slot r / C. Every CTA pushes its partial
-        // (O row, m, l) into the owner's shared memory with remote stores, one
-        // cluster barrier publishes them, and each owner merges its rows locally.
+        // Row r is owned by CTA r % C at slot r / C of source block `split`. The
+        // merge buffer is dedicated (never a TMA target), so partials are pushed
+        // as soon as they are ready; one cluster barrier publishes them.
         const int C = p.splits;
         const int slots = (rows + C - 1) / C;
-        float* sO = reinterpret_cast<float*>(smem + kOffCombO);        // [C][slots][kOStride]
-        float* sM = sO + C * slots * kOStride;                         // [C][slots]
+        float* sO = reinterpret_cast<float*>(smem + kOffMerge);        // [C][slots][2][kOStride]
+        float* sM = sO + C * slots * 2 * kOStride;                     // [C][slots]
         float* sL = sM + C * slots;                                    // [C][slots]
-        cluster_sync();   // every CTA is past its main loop: stage regions are free
         if (has_rows) {
             const int owner = row % C, slot = row / C;
-            const uint32_t dO = dsmem_map(smem_u32(sO + (split * slots + slot) * kOStride + half * 32), owner);
+            const uint32_t dO = dsmem_map(smem_u32(sO + ((split * slots + slot) * 2 + grp) * kOStride), owner);
 #pragma unroll
             for (int c = 0; c < 32; c += 4)
-                dsmem_st_f32x4(dO + c * 4, make_float4(o_part[c], o_part[c + 1], o_part[c + 2], o_part[c + 3]));
-            if (half == 0) {
+                dsmem_st_f32x4(dO + c * 4, make_float4(o_row[c], o_row[c + 1], o_row[c + 2], o_row[c + 3]));
+            if (grp == 0) {
                 dsmem_st_f32(dsmem_map(smem_u32(sM + split * slots + slot), owner), m_ref);
                 dsmem_st_f32(dsmem_map(smem_u32(sL + split * slots + slot), owner), l_run);
             }
         }
+        SFB_T(163);
         cluster_sync();
+        SFB_T(164);
         const int nsub = kThreads / 16;
         const int sub  = tid >> 4, c4 = (tid & 15) * 4;
         for (int slot = sub; slot < slots; slot += nsub) {
@@ -422,9 +530,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             float L = 0.f;
             if (M != -INFINITY) {
                 for (int k = 0; k < C; ++k) {
-                    const float w = ptx::ex2(sM[k * slots + slot] - M);
+                    const float mk = sM[k * slots + slot];
+                    if (mk == -INFINITY) continue;
+                    const float w = ptx::ex2(mk - M);
                     L += w * sL[k * slots + slot];
-                    const float4 o = *reinterpret_cast<const float4*>(sO + (k * slots + slot) * kOStride + c4);
+                    const float4 o = *reinterpret_cast<const float4*>(
+                        sO + ((k * slots + slot) * 2 + (c4 >> 5)) * kOStride + (c4 & 31));
                     acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
                 }
             }
@@ -439,7 +550,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         }
     }
 
-    SFB_T(201);
+    SFB_T(165);
     if (!ok) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
     tc_fence_before_sync();
     __syncthreads();
@@ -527,10 +638,14 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream) {
     static bool attr_done[2][64] = {};
     const int ki = a.dtype == SFB_BF16 ? 0 : 1;
     if (!attr_done[ki][dev.ordinal & 63]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 attn_tc::kSmemBytes) != cudaSuccess ||
-            cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        cudaError_t e1 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              attn_tc::kSmemBytes);
+        cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            (void)cudaGetLastError();
+            record_cuda_error(e1 != cudaSuccess ? e1 : e2, "attention kernel attributes");
             return SFB_ERR_CUDA;
+        }
         attr_done[ki][dev.ordinal & 63] = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -548,6 +663,7 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream) {
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, p);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
+        record_cuda_error(e, "attention (tcgen05) launch");
         return SFB_ERR_LAUNCH;
     }
     return SFB_OK;

@@ -25,11 +25,14 @@ const char* sfb_status_string(int status) {
         case SFB_ERR_UNSUPPORTED:    return "requires an sm_100a (B200) device";
         case SFB_ERR_CUDA:           return "CUDA runtime error";
         case SFB_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+        case SFB_ERR_RANGE:          return "input value outside the kernel's supported range";
         default:                     return "unknown status";
     }
 }
 
 const char* sfb_version(void) { return "0.1.0 sm_100a"; }
+
+const char* sfb_last_error(void) { return sfb::last_error_buf(); }
 
 int sfb_device_error(int* code, int reset) {
     if (code == nullptr) return SFB_ERR_INVALID;

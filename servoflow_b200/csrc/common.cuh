@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -88,9 +89,20 @@ inline int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, int rank,
     return r == CUDA_SUCCESS ? SFB_OK : SFB_ERR_SHAPE;
 }
 
+// Text of the last CUDA error seen by this library on the calling thread.
+inline char* last_error_buf() {
+    static thread_local char buf[256] = "";
+    return buf;
+}
+inline void record_cuda_error(cudaError_t e, const char* where) {
+    snprintf(last_error_buf(), 256, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
 inline int launch_status() {
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? SFB_OK : SFB_ERR_LAUNCH;
+    if (e == cudaSuccess) return SFB_OK;
+    record_cuda_error(e, "kernel launch");
+    return SFB_ERR_LAUNCH;
 }
 
 }  // namespace sfb
