@@ -205,6 +205,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int ntl     = tbase + (split < trem ? 1 : 0);
 
     SFB_T(0);
+#ifdef SFB_TRACE
+    const uint64_t cta_t0 = ptx::global_timer_ns();
+#endif
     if (tid == kCtrlWarp * 32) {
         mbar_init(&bars[kBarQ], 1);
         for (int s = 0; s < kStages; ++s) {
@@ -245,28 +248,37 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     float m_ref = -INFINITY, l_run = 0.f;
 
     if (warp == kCtrlWarp) {
-        // ── control warp: TMA + MMA issue (one thread) ──────────────────────
-        if (lane == 0 && ntl > 0) {
+        // ── control warp: TMA + MMA issue ───────────────────────────────────
+        // All 32 lanes run the loop with identical, warp-uniform state; each
+        // TMA / MMA / commit is issued by one elected lane. (Issuing from a
+        // single divergent lane cost ~100 cycles per tcgen05.mma, measured.)
+        if (ntl > 0) {
             constexpr uint32_t idS  = idesc_f16(128, 128, kFmtQK, 0, 0);  // Q·Kᵀ, both K-major
             constexpr uint32_t idPV = idesc_f16(128, 64, 0, 0, 1);        // P(tmem)·V(MN-major), fp16
             auto issue_kv = [&](int t) {
                 const int s = t % kStages;
                 const int key0 = (t_begin + t) * kTileKeys;
-                mbar_arrive_expect_tx(&bars[bar_k(s)], kTileBytes);
-                tma_load_4d(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b);
-                mbar_arrive_expect_tx(&bars[bar_v(s)], kTileBytes);
-                tma_load_4d(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b);
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(&bars[bar_k(s)], kTileBytes);
+                    tma_load_4d(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b);
+                    mbar_arrive_expect_tx(&bars[bar_v(s)], kTileBytes);
+                    tma_load_4d(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b);
+                }
+                __syncwarp();
             };
             const uint32_t aq = smem_u32(sQ);
             auto issue_s = [&](int j) {
                 const int u = j % kBufs, s = j % kStages;
                 tc_fence_after_sync();
                 const uint32_t ak = smem_u32(sK(s));
+                if (elect_one()) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16_ss(tmem + u * 128, smem_desc_sw128(aq + kk * 32, 16, 1024),
-                               smem_desc_sw128(ak + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
-                mma_commit(&bars[bar_s(u)]);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16_ss(tmem + u * 128, smem_desc_sw128(aq + kk * 32, 16, 1024),
+                                   smem_desc_sw128(ak + kk * 32, 16, 1024), idS, kk > 0 ? 1u : 0u);
+                    mma_commit(&bars[bar_s(u)]);
+                }
+                __syncwarp();
             };
             auto issue_pv = [&](int j) {
                 const int u = j % kBufs, g = j & 1, s = j % kStages;
@@ -274,16 +286,22 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 const uint32_t tP = tmem + u * 128, tO = tmem + 384 + g * 64;
                 const uint32_t av = smem_u32(sV(s));
                 // fp16 P of keys [32c, 32c+32) sits in columns 32c..32c+15
+                if (elect_one()) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    mma_f16_ts(tO, tP + 32 * (k >> 1) + 8 * (k & 1),
-                               smem_desc_sw128(av + k * 2048, 8192, 1024), idPV,
-                               (j >= 2 || k > 0) ? 1u : 0u);
-                mma_commit(&bars[bar_o(u)]);
-                mma_commit(&bars[bar_og(g)]);
+                    for (int k = 0; k < 8; ++k)
+                        mma_f16_ts(tO, tP + 32 * (k >> 1) + 8 * (k & 1),
+                                   smem_desc_sw128(av + k * 2048, 8192, 1024), idPV,
+                                   (j >= 2 || k > 0) ? 1u : 0u);
+                    mma_commit(&bars[bar_o(u)]);
+                    mma_commit(&bars[bar_og(g)]);
+                }
+                __syncwarp();
             };
-            mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
-            tma_load_4d(sQ, &tmQ, &bars[kBarQ], 0, q0, h, b);
+            if (elect_one()) {
+                mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
+                tma_load_4d(sQ, &tmQ, &bars[kBarQ], 0, q0, h, b);
+            }
+            __syncwarp();
             int nL = min(kStages, ntl);                // tiles whose K/V load is issued
             for (int t = 0; t < nL; ++t) issue_kv(t);
             wait(kBarQ, 0);
@@ -292,7 +310,14 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             int nS = 0, nP = 0, pv_done = 0;
             const uint64_t t_start = global_timer_ns();
             uint32_t idle = 0;
+#ifdef SFB_TRACE
+            long long seen_p = 0, seen_v = 0;
+#endif
+            long long last_iter = 0;
             while (nP < ntl && ok) {
+#ifdef SFB_TRACE
+                last_iter = clock64();
+#endif
                 bool progress = false;
                 while (pv_done < nP && mbar_test(&bars[bar_o(pv_done % kBufs)], (pv_done / kBufs) & 1))
                     ++pv_done;
@@ -301,21 +326,51 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 // S/P buffer of tile j is free once P·V of tile j - kBufs is done
                 if (nS < ntl && (nS < kBufs || nS - kBufs < pv_done) &&
                     mbar_test(&bars[bar_k(nS % kStages)], (nS / kStages) & 1)) {
+#ifdef SFB_TRACE
+                    const long long ts0 = clock64();
+#endif
                     issue_s(nS);
+#ifdef SFB_TRACE
+                    if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && nS < 40) {
+                        p.trace[3400 + 2 * nS] = ts0; p.trace[3401 + 2 * nS] = clock64();
+                    }
+#endif
                     SFB_T(2 + 4 * nS);
                     ++nS;
                     progress = true;
                 }
+#ifdef SFB_TRACE
+                if (nP < nS) {
+                    if (!seen_p && mbar_test(&bars[bar_p(nP % kBufs)], (nP / kBufs) & 1)) seen_p = clock64();
+                    if (!seen_v && mbar_test(&bars[kConvV ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
+                                             (nP / kStages) & 1)) seen_v = clock64();
+                }
+#endif
                 if (nP < nS && mbar_test(&bars[bar_p(nP % kBufs)], (nP / kBufs) & 1) &&
                     mbar_test(&bars[kConvV ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
                               (nP / kStages) & 1)) {
+#ifdef SFB_TRACE
+                    const long long tb0 = clock64();
+#endif
                     issue_pv(nP);
+#ifdef SFB_TRACE
+                    const long long tb1 = clock64();
+                    if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && nP < 40) {
+                        p.trace[3200 + 4 * nP] = seen_p; p.trace[3201 + 4 * nP] = tb0;
+                        p.trace[3202 + 4 * nP] = tb1; p.trace[3203 + 4 * nP] = last_iter;
+                    }
+                    seen_p = seen_v = 0;
+#endif
                     SFB_T(3 + 4 * nP);
                     ++nP;
                     progress = true;
                 }
                 if (progress) { idle = 0; continue; }
-                if ((++idle & 1023u) == 1023u && global_timer_ns() - t_start > 1000000000ull) ok = false;
+                if ((++idle & 1023u) == 1023u) {
+                    // lane 0 decides, so the whole warp leaves the loop together
+                    const int expired = global_timer_ns() - t_start > 1000000000ull ? 1 : 0;
+                    if (__shfl_sync(0xffffffffu, expired, 0)) ok = false;
+                }
             }
         }
     } else if (kConvV && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
@@ -551,6 +606,15 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
 
     SFB_T(165);
+#ifdef SFB_TRACE
+    if (p.trace && tid == 0) {
+        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        if (cta < 1024) {
+            p.trace[1024 + 2 * cta] = cta_t0;
+            p.trace[1025 + 2 * cta] = ptx::global_timer_ns();
+        }
+    }
+#endif
     if (!ok) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
     tc_fence_before_sync();
     __syncthreads();
