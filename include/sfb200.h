@@ -139,6 +139,27 @@ int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype
                         int64_t scale_numel, void* out, int32_t out_dtype,
                         int64_t rows, int64_t cols, void* stream);
 
+/* ── int8-weight linear layer (dequantisation fused into the GEMM) ─────────────
+ * Replaces, for the RDT-1B projections (Q/K/V/O, MLP fc1/fc2), the pair
+ * IBackend::dequantize (backend.h:201-206, quantization.cu:18-95) followed by
+ * IBackend::gemm_bias_act (backend.h:160-185, cuda_backend.cu:337-467):
+ *
+ *   y[m,n] = act( w_scale[n] · Σ_k x[m,k]·w[n,k] + bias[n] ) + residual[m,n]
+ *
+ * x: bf16 [M, K], row stride ldx (elements, ldx·2 a multiple of 16 bytes);
+ * w: int8 [N, K] row-major, contiguous (one row per output channel);
+ * w_scale: fp32 [N]; bias: bf16 [N] or NULL; residual: bf16 [M, N] with row
+ * stride ldr, or NULL (may alias y); y: y_dtype (SFB_BF16 or SFB_F32) [M, N]
+ * with row stride ldy. act: 0 none, 1 GELU (tanh form, as the reference's
+ * cuBLASLt GELU epilogue and the RDT-1B MLPs use). K % 64 == 0, N % 32 == 0.
+ * num_splits: split-K cluster size for small M (0 = automatic).
+ * The result equals dequantise-then-GEMM up to fp32 summation order.
+ */
+int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
+                     const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
+                     int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
+                     int32_t num_splits, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

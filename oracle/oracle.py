@@ -50,6 +50,8 @@ def lib() -> ctypes.CDLL:
         h.sfo_round_bf16.restype = _f
         h.sfo_round_bf16.argtypes = [_f]
         h.sfo_num_threads.restype = _i
+        h.sfo_w8a16_linear.restype = None
+        h.sfo_w8a16_linear.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]
         _lib = h
     return _lib
 
@@ -84,6 +86,21 @@ def dequant_int8(q, scale, round_mode=0):
     out = np.empty(q.shape, dtype=np.float32)
     lib().sfo_dequant_int8(_ptr(q), _ptr(s), s.size, _ptr(out), rows, cols, int(round_mode))
     return out
+
+
+def w8a16_linear(x, q, scale, bias=None, residual=None, act=0, nthreads=0):
+    """Oracle int8-weight linear layer: float32 x [M, K], int8 q [N, K]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    s = np.ascontiguousarray(scale, dtype=np.float32)
+    M, K = x.shape
+    N = q.shape[0]
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+    y = np.empty((M, N), np.float32)
+    lib().sfo_w8a16_linear(_ptr(x), _ptr(q), _ptr(s), _ptr(b), _ptr(r), _ptr(y), M, N, K, int(act),
+                           int(nthreads))
+    return y
 
 
 def num_threads() -> int:

@@ -129,3 +129,30 @@ int sfo_num_threads(void) {
     return 1;
 #endif
 }
+
+/* ── int8-weight linear layer ────────────────────────────────────────────────
+ * The reference computes this in two steps: dequantise the weight,
+ * w[n,k] = q[n,k]·s[n] (src/backend/cuda/ops/quantization.cu:18-51), then
+ * gemm_bias_act (src/backend/cuda/cuda_backend.cu:337-467):
+ *   y[m,n] = act( Σ_k x[m,k]·w[n,k] + bias[n] ) + residual[m,n]
+ * with act = GELU in its tanh form (the RDT-1B MLPs, F.gelu(approximate="tanh")
+ * in tests/alignment/test_rdt1b_alignment.py:104,119). Evaluated in double.
+ * bias / residual may be NULL.
+ */
+void sfo_w8a16_linear(const float* x, const int8_t* q, const float* s, const float* bias,
+                      const float* residual, float* y, int M, int N, int K, int act,
+                      int nthreads) {
+#ifdef _OPENMP
+    if (nthreads <= 0) nthreads = omp_get_max_threads();
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+#endif
+    for (int64_t mn = 0; mn < (int64_t)M * N; ++mn) {
+        const int m = (int)(mn / N), n = (int)(mn % N);
+        double acc = 0.0;
+        for (int k = 0; k < K; ++k) acc += (double)x[(int64_t)m * K + k] * (double)q[(int64_t)n * K + k];
+        double v = acc * (double)s[n] + (bias ? (double)bias[n] : 0.0);
+        if (act == 1) v = 0.5 * v * (1.0 + tanh(0.7978845608028654 * (v + 0.044715 * v * v * v)));
+        if (residual) v += (double)residual[mn];
+        y[mn] = (float)v;
+    }
+}

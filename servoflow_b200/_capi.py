@@ -88,6 +88,11 @@ def _declare(lib: ctypes.CDLL) -> None:
                                        c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                                        c.c_int32, c.c_int32, c.c_void_p, c.c_float, c.c_int32,
                                        c.c_void_p]
+    lib.sfb_w8a16_linear.restype = c.c_int
+    lib.sfb_w8a16_linear.argtypes = [c.c_void_p, c.c_int64, c.c_void_p, c.c_void_p, c.c_void_p,
+                                     c.c_void_p, c.c_int64, c.c_void_p, c.c_int64, c.c_int32,
+                                     c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
+                                     c.c_void_p]
     lib.sfb_dequantize_int8.restype = c.c_int
     lib.sfb_dequantize_int8.argtypes = [c.c_void_p, c.c_void_p, c.c_int32, c.c_int64, c.c_void_p,
                                         c.c_int32, c.c_int64, c.c_int64, c.c_void_p]

@@ -138,6 +138,34 @@ class B200Backend:
             output.data_ptr(), dtype_code(output.dtype), rows, cols, _stream_handle(stream)),
             "dequantize")
 
+    # Fused replacement of dequantize + gemm_bias_act (backend.h:160-185, 205-206)
+    def w8a16_linear(self, x, w_q, w_scale, out, bias=None, residual=None, act: str = "none",
+                     num_splits: int = 0, stream=None) -> None:
+        """out[M, N] = act(x[M, K] · (w_q[N, K] · w_scale[N])ᵀ + bias) + residual."""
+        for t, n in ((x, "x"), (w_q, "w_q"), (w_scale, "w_scale"), (out, "out")):
+            _check_device(t, n)
+        if x.dtype != torch.bfloat16 or w_q.dtype != torch.int8 or w_scale.dtype != torch.float32:
+            raise _capi.SfbError(_capi.SFB_ERR_DTYPE, "x bf16, w_q int8, w_scale fp32 expected")
+        if x.stride(1) != 1 or not w_q.is_contiguous() or out.stride(1) != 1:
+            raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "row-major tensors expected")
+        M, K = x.shape
+        N = w_q.shape[0]
+        if w_q.shape[1] != K or tuple(out.shape) != (M, N) or w_scale.numel() != N:
+            raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "inconsistent shapes")
+        if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != N):
+            raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "bias must be bf16 [N]")
+        if residual is not None and (residual.dtype != torch.bfloat16 or tuple(residual.shape) != (M, N)
+                                     or residual.stride(1) != 1):
+            raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "residual must be bf16 [M, N] row-major")
+        acts = {"none": 0, "gelu": 1}
+        _capi.check(self._lib.sfb_w8a16_linear(
+            x.data_ptr(), x.stride(0), w_q.data_ptr(), w_scale.data_ptr(),
+            None if bias is None else bias.data_ptr(),
+            None if residual is None else residual.data_ptr(),
+            0 if residual is None else residual.stride(0), out.data_ptr(), out.stride(0),
+            dtype_code(out.dtype), M, N, K, acts[act], int(num_splits), _stream_handle(stream)),
+            "w8a16_linear")
+
     # Graph hooks (backend.h:227-229; CUDABackend keeps one graph per stream,
     # cuda_backend.cu:592-608).
     def graph_begin_capture(self, stream) -> None:

@@ -6,6 +6,10 @@
 namespace sfb {
 int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream);
 int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream);
+int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
+                      const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
+                      int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
+                      int32_t num_splits, cudaStream_t stream);
 int dequantize_int8_launch(const int8_t* in, const void* scale, int32_t scale_dtype,
                            int64_t scale_numel, void* out, int32_t out_dtype, int64_t rows,
                            int64_t cols, cudaStream_t stream);
@@ -86,6 +90,14 @@ int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype
                         int64_t cols, void* stream) {
     return sfb::dequantize_int8_launch(in, scale, scale_dtype, scale_numel, out, out_dtype, rows,
                                        cols, static_cast<cudaStream_t>(stream));
+}
+
+int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
+                     const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
+                     int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
+                     int32_t num_splits, void* stream) {
+    return sfb::w8a16_gemm_launch(x, ldx, w, w_scale, bias, residual, ldr, y, ldy, y_dtype, M, N, K,
+                                  act, num_splits, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

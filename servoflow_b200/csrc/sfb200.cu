@@ -3,4 +3,5 @@
 #include "attn_tc.cu"
 #include "attn_simt.cu"
 #include "dequant.cu"
+#include "w8a16_gemm.cu"
 #include "capi.cu"
