@@ -57,6 +57,10 @@ const char* sfb_version(void);
  * Synchronous: it waits for the device. */
 int sfb_device_error(int* code, int reset);
 
+/* Synchronous copy between any two addresses (cudaMemcpyDefault); a helper
+ * for hosts without their own CUDA runtime binding (tests read parameters). */
+int sfb_copy_device(void* dst, const void* src, int64_t bytes);
+
 /* ── attention ────────────────────────────────────────────────────────────────
  * Replaces IBackend::attention (reference include/servoflow/backend/backend.h:
  * 102-110) as implemented by CUDABackend::attention
@@ -151,7 +155,7 @@ int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype
  * w_scale: fp32 [N]; bias: bf16 [N] or NULL; residual: bf16 [M, N] with row
  * stride ldr, or NULL (may alias y); y: y_dtype (SFB_BF16 or SFB_F32) [M, N]
  * with row stride ldy. act: 0 none, 1 GELU (tanh form, as the reference's
- * cuBLASLt GELU epilogue and the RDT-1B MLPs use). K % 64 == 0, N % 32 == 0.
+ * cuBLASLt GELU epilogue and the RDT-1B MLPs use), 2 SiLU (timestep MLP). K % 64 == 0, N % 32 == 0.
  * num_splits: split-K cluster size for small M (0 = automatic).
  * The result equals dequantise-then-GEMM up to fp32 summation order.
  */
@@ -159,6 +163,65 @@ int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w
                      const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                      int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
                      int32_t num_splits, void* stream);
+
+/* ── RDT-1B denoising runtime ──────────────────────────────────────────────────
+ * The model-level path around the kernels above, replacing for RDT-1B the
+ * reference's RDT1BModel::encode_condition / denoise_step
+ * (src/models/rdt1b/rdt1b.cpp:167-369), RDTBlock / SelfAttention /
+ * CrossAttention (dit_block.cu:198-387) and the CUDA-graph sampling loop of
+ * FlowMatchingSampler::sample (src/sampling/flow_matching.cpp:25-93), with a
+ * DPM-Solver++ (2M) sampler. Weights are seeded random values quantised to
+ * int8 per output channel (the reference loads checkpoints; none is available).
+ * All tensors are device memory; `sessions` independent robot sessions run
+ * batched (1 <= sessions <= max_sessions).
+ */
+typedef struct sfb_rdt1b_config {
+    int32_t num_layers;     /* 28 */
+    int32_t hidden;         /* 2048 (= heads · 64) */
+    int32_t heads;          /* 32 */
+    int32_t action_dim;     /* 128 */
+    int32_t horizon;        /* 64 action tokens */
+    int32_t state_dim;      /* 128 (must equal action_dim) */
+    int32_t lang_dim;       /* 4096 (T5-XXL features) */
+    int32_t img_dim;        /* 1152 (SigLIP features) */
+    int32_t max_lang_len;   /* 1024 */
+    int32_t img_len;        /* 4374 */
+    int32_t max_sessions;   /* batch capacity */
+    int32_t num_steps;      /* 5 DPM-Solver++ steps */
+    int32_t ctrl_freq;      /* 25 Hz */
+    float   weight_std;     /* 0.02, std of the random weights before quantisation */
+} sfb_rdt1b_config;
+
+int sfb_rdt1b_default_config(sfb_rdt1b_config* cfg);
+/* Allocates and initialises the model on the current device (setup-time
+ * cudaMalloc; nothing allocates afterwards). */
+int sfb_rdt1b_create(const sfb_rdt1b_config* cfg, uint64_t seed, void** handle);
+int sfb_rdt1b_destroy(void* handle);
+/* Per control tick: lang_tokens bf16 [sessions, max_lang_len, lang_dim],
+ * lang_len int32 [sessions] (valid language tokens; the rest are masked),
+ * img_tokens bf16 [sessions, img_len, img_dim], state bf16 [sessions,
+ * state_dim]. Runs the adaptors and fills every block's cross-attention K/V
+ * cache. */
+int sfb_rdt1b_encode(void* handle, int32_t sessions, const void* lang_tokens, const int32_t* lang_len,
+                     const void* img_tokens, const void* state, void* stream);
+/* One network evaluation: x_t fp32 [sessions, horizon, action_dim] at timestep
+ * t → x0 prediction fp32, same shape. */
+int sfb_rdt1b_forward(void* handle, int32_t sessions, const float* x_t, float t, float* x0_out,
+                      void* stream);
+/* Full sampling: noise fp32 [sessions, horizon, action_dim] → actions (same
+ * shape) after num_steps DPM-Solver++ steps. With use_graph != 0 the loop is
+ * captured into a CUDA graph on the first call for a given session count (that
+ * call runs eagerly, then captures; make it before any capture of your own) and
+ * replayed afterwards. */
+int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* actions,
+                     int32_t use_graph, void* stream);
+/* Device pointer, element count and dtype of a named parameter (names follow
+ * the reference checkpoint: "blocks.3.attn.qkv.weight_q", "...weight_scale",
+ * "...bias", "x_pos_embed", ...). */
+int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, int32_t* dtype);
+/* The sampler's timesteps and per-step update x ← a·x + b·x0 + c·x0_prev. */
+int sfb_rdt1b_schedule(void* handle, float* timesteps, float* coef_a, float* coef_b, float* coef_c,
+                       int32_t n);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -1,0 +1,173 @@
+"""CPU oracle of the RDT-1B denoising path (fp32, PyTorch on CPU).
+
+TEST INFRASTRUCTURE ONLY (tests/ and bench.py's CPU legs; never the product).
+
+A restatement of the reference's PyTorch alignment model
+(tests/alignment/test_rdt1b_alignment.py:73-210: RmsNorm, timestep embedder,
+adaptors, self/cross attention with per-head qk RMSNorm, RDT blocks with
+alternating language/image conditions, final layer) — the reference's own
+oracle for its C++ model — evaluated on the exact weights of a libsfb200 model
+(int8 weights dequantised as q·s). Two additions the reference's model lacks:
+the language key-padding mask (keys at or beyond lang_len are masked with
+-inf, the torch SDPA boolean-mask convention) and the DPM-Solver++ (2M)
+sampler, restated here independently of the C++ code from the published
+algorithm (Lu et al., "DPM-Solver++", 2022: data-prediction multistep solver)
+over the squaredcos_cap_v2 DDPM schedule (Nichol & Dhariwal, 2021).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+
+def dpm_schedule(num_steps: int, train_steps: int = 1000):
+    """(timesteps, a, b, c): step i maps x to a_i·x + b_i·x0_i + c_i·x0_{i-1}."""
+    def abar(t):
+        return math.cos((t + 0.008) / 1.008 * math.pi / 2) ** 2
+    betas = [min(1 - abar((i + 1) / train_steps) / abar(i / train_steps), 0.999)
+             for i in range(train_steps)]
+    alphas_cumprod = np.cumprod(1.0 - np.array(betas, dtype=np.float64))
+    ts = [int(round(x)) for x in np.linspace(0, train_steps - 1, num_steps + 1)[::-1][:-1]]
+    alpha = lambda t: math.sqrt(alphas_cumprod[t])
+    sigma = lambda t: math.sqrt(1 - alphas_cumprod[t])
+    lam = lambda t: math.log(alpha(t) / sigma(t))
+    a, b, c = [], [], []
+    for i in range(num_steps):
+        if i == num_steps - 1:                    # to noise level zero: the x0 estimate
+            a.append(0.0); b.append(1.0); c.append(0.0)
+            continue
+        s, t = ts[i], ts[i + 1]
+        h = lam(t) - lam(s)
+        first = -alpha(t) * (math.exp(-h) - 1.0)
+        if i == 0:                                # first order (DPM-Solver++ 1)
+            a.append(sigma(t) / sigma(s)); b.append(first); c.append(0.0)
+        else:                                     # second order multistep (2M)
+            r = (lam(s) - lam(ts[i - 1])) / h
+            a.append(sigma(t) / sigma(s)); b.append(first * (1 + 1 / (2 * r))); c.append(-first / (2 * r))
+    return ts, a, b, c
+
+
+def rms_norm(x, w, eps=1e-6):
+    return x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def sincos(t: float, dim: int = 256):
+    half = dim // 2
+    freq = torch.exp(-torch.arange(half, dtype=torch.float32) * math.log(10000) / half)
+    x = torch.tensor(float(t)) * freq
+    return torch.cat([x.cos(), x.sin()])
+
+
+class RefRDT:
+    """fp32 RDT-1B on CPU over a weight dict {name: float32 tensor}."""
+
+    def __init__(self, weights: dict, cfg):
+        self.w = weights
+        self.c = cfg
+
+    def lin(self, x, name, act=None):
+        y = x @ self.w[name + ".weight"].t() + self.w[name + ".bias"]
+        if act == "gelu":
+            y = F.gelu(y, approximate="tanh")
+        elif act == "silu":
+            y = F.silu(y)
+        return y
+
+    def encode(self, lang, img):
+        lang_c = self.lin(self.lin(lang, "lang_adaptor.0", "gelu"), "lang_adaptor.2")
+        lang_c = lang_c + self.w["lang_cond_pos_embed"][: lang.shape[1]]
+        img_c = self.lin(self.lin(img, "img_adaptor.0", "gelu"), "img_adaptor.2") + self.w["img_cond_pos_embed"]
+        return lang_c, img_c
+
+    def attn(self, q, k, v, H, key_len=None):
+        B, Sq, D = q.shape
+        Sk = k.shape[1]
+        q = q.view(B, Sq, H, 64).transpose(1, 2)
+        k = k.view(B, Sk, H, 64).transpose(1, 2)
+        v = v.view(B, Sk, H, 64).transpose(1, 2)
+        mask = None
+        if key_len is not None:
+            mask = (torch.arange(Sk)[None, :] < key_len[:, None])[:, None, None, :]
+        with torch.nn.attention.sdpa_kernel(torch.nn.attention.SDPBackend.MATH):
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+        return o.transpose(1, 2).reshape(B, Sq, D)
+
+    def forward(self, lang_c, img_c, lang_len, state, x_t, t):
+        c, w = self.c, self.w
+        B, T, A = x_t.shape
+        D, H = c.hidden, c.heads
+        traj = torch.cat([torch.cat([state[:, None, :], x_t], 1), torch.ones(B, T + 1, A)], 2)
+        seq = self.lin(self.lin(self.lin(traj, "state_adaptor.0", "gelu"), "state_adaptor.2", "gelu"),
+                       "state_adaptor.4")
+        temb = self.lin(self.lin(sincos(t), "t_embedder.mlp.0", "silu"), "t_embedder.mlp.2")
+        femb = self.lin(self.lin(sincos(c.ctrl_freq), "freq_embedder.mlp.0", "silu"), "freq_embedder.mlp.2")
+        x = torch.cat([temb.expand(B, 1, D), femb.expand(B, 1, D), seq], 1) + w["x_pos_embed"].view(-1, D)
+        for l in range(c.num_layers):
+            p = f"blocks.{l}."
+            h = rms_norm(x, w[p + "norm1.weight"])
+            qkv = self.lin(h, p + "attn.qkv").view(B, -1, 3, H, 64)
+            q = rms_norm(qkv[:, :, 0], w[p + "attn.q_norm.weight"]).reshape(B, -1, D)
+            k = rms_norm(qkv[:, :, 1], w[p + "attn.k_norm.weight"]).reshape(B, -1, D)
+            v = qkv[:, :, 2].reshape(B, -1, D)
+            x = x + self.lin(self.attn(q, k, v, H), p + "attn.proj")
+            cond, klen = (lang_c, lang_len) if l % 2 == 0 else (img_c, None)
+            h = rms_norm(x, w[p + "norm2.weight"])
+            q = rms_norm(self.lin(h, p + "cross_attn.q").view(B, -1, H, 64),
+                         w[p + "cross_attn.q_norm.weight"]).reshape(B, -1, D)
+            kv = self.lin(cond, p + "cross_attn.kv").view(B, -1, 2, H, 64)
+            k = rms_norm(kv[:, :, 0], w[p + "cross_attn.k_norm.weight"]).reshape(B, -1, D)
+            v = kv[:, :, 1].reshape(B, -1, D)
+            x = x + self.lin(self.attn(q, k, v, H, klen), p + "cross_attn.proj")
+            h = rms_norm(x, w[p + "norm3.weight"])
+            x = x + self.lin(self.lin(h, p + "ffn.fc1", "gelu"), p + "ffn.fc2")
+        h = rms_norm(x, w["final_layer.norm_final.weight"])
+        out = self.lin(self.lin(h, "final_layer.ffn_final.fc1", "gelu"), "final_layer.ffn_final.fc2")
+        return out[:, -T:]
+
+    def sample(self, lang_c, img_c, lang_len, state, noise):
+        ts, a, b, cc = dpm_schedule(self.c.num_steps)
+        x, x0_prev = noise.clone(), torch.zeros_like(noise)
+        for i, t in enumerate(ts):
+            x0 = self.forward(lang_c, img_c, lang_len, state, x, t)
+            x = a[i] * x + b[i] * x0 + cc[i] * x0_prev
+            x0_prev = x0
+        return x
+
+
+def load_weights(model, cfg) -> dict:
+    """Reads every parameter of a servoflow_b200.rdt1b.RDT1B into fp32 CPU tensors."""
+    D = cfg.hidden
+    w = {}
+
+    def lin(name, n, k):
+        q = model.param(name + ".weight_q").view(n, k).float().cpu()
+        s = model.param(name + ".weight_scale").float().cpu()
+        w[name + ".weight"] = q * s[:, None]
+        w[name + ".bias"] = model.param(name + ".bias").float().cpu()
+
+    def vec(name, shape):
+        w[name] = model.param(name).float().cpu().view(*shape)
+
+    lin("lang_adaptor.0", D, cfg.lang_dim); lin("lang_adaptor.2", D, D)
+    lin("img_adaptor.0", D, cfg.img_dim); lin("img_adaptor.2", D, D)
+    lin("state_adaptor.0", D, 2 * cfg.state_dim); lin("state_adaptor.2", D, D); lin("state_adaptor.4", D, D)
+    for e in ("t_embedder", "freq_embedder"):
+        lin(e + ".mlp.0", D, 256); lin(e + ".mlp.2", D, D)
+    vec("x_pos_embed", (cfg.horizon + 3, D))
+    vec("lang_cond_pos_embed", (cfg.max_lang_len, D))
+    vec("img_cond_pos_embed", (cfg.img_len, D))
+    for l in range(cfg.num_layers):
+        p = f"blocks.{l}."
+        for n in ("norm1", "norm2", "norm3"):
+            vec(p + n + ".weight", (D,))
+        lin(p + "attn.qkv", 3 * D, D); lin(p + "attn.proj", D, D)
+        vec(p + "attn.q_norm.weight", (64,)); vec(p + "attn.k_norm.weight", (64,))
+        lin(p + "cross_attn.q", D, D); lin(p + "cross_attn.kv", 2 * D, D); lin(p + "cross_attn.proj", D, D)
+        vec(p + "cross_attn.q_norm.weight", (64,)); vec(p + "cross_attn.k_norm.weight", (64,))
+        lin(p + "ffn.fc1", D, D); lin(p + "ffn.fc2", D, D)
+    vec("final_layer.norm_final.weight", (D,))
+    lin("final_layer.ffn_final.fc1", D, D); lin("final_layer.ffn_final.fc2", cfg.action_dim, D)
+    return w

@@ -152,6 +152,7 @@ void sfo_w8a16_linear(const float* x, const int8_t* q, const float* s, const flo
         for (int k = 0; k < K; ++k) acc += (double)x[(int64_t)m * K + k] * (double)q[(int64_t)n * K + k];
         double v = acc * (double)s[n] + (bias ? (double)bias[n] : 0.0);
         if (act == 1) v = 0.5 * v * (1.0 + tanh(0.7978845608028654 * (v + 0.044715 * v * v * v)));
+        else if (act == 2) v = v / (1.0 + exp(-v));
         if (residual) v += (double)residual[mn];
         y[mn] = (float)v;
     }

@@ -157,7 +157,7 @@ class B200Backend:
         if residual is not None and (residual.dtype != torch.bfloat16 or tuple(residual.shape) != (M, N)
                                      or residual.stride(1) != 1):
             raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "residual must be bf16 [M, N] row-major")
-        acts = {"none": 0, "gelu": 1}
+        acts = {"none": 0, "gelu": 1, "silu": 2}
         _capi.check(self._lib.sfb_w8a16_linear(
             x.data_ptr(), x.stride(0), w_q.data_ptr(), w_scale.data_ptr(),
             None if bias is None else bias.data_ptr(),

@@ -38,6 +38,13 @@ const char* sfb_version(void) { return "0.1.0 sm_100a"; }
 
 const char* sfb_last_error(void) { return sfb::last_error_buf(); }
 
+int sfb_copy_device(void* dst, const void* src, int64_t bytes) {
+    if ((dst == nullptr || src == nullptr) && bytes > 0) return SFB_ERR_INVALID;
+    cudaError_t e = cudaMemcpy(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault);
+    if (e != cudaSuccess) { sfb::record_cuda_error(e, "copy"); return SFB_ERR_CUDA; }
+    return SFB_OK;
+}
+
 int sfb_device_error(int* code, int reset) {
     if (code == nullptr) return SFB_ERR_INVALID;
     int v = 0;

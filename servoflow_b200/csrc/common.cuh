@@ -96,6 +96,7 @@ inline char* last_error_buf() {
 }
 inline void record_cuda_error(cudaError_t e, const char* where) {
     snprintf(last_error_buf(), 256, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+    (void)cudaGetLastError();   // reported here; do not leak into the next launch check
 }
 
 inline int launch_status() {

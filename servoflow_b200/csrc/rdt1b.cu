@@ -1,0 +1,574 @@
+// rdt1b.cu — the RDT-1B denoising runtime over the libsfb200 kernels: model
+// state, per-tick condition encoding with the cross-attention K/V cache, and
+// the DPM-Solver++ denoising loop captured once into a CUDA graph.
+//
+// Follows the reference model (src/models/rdt1b/dit_block.cu:198-387,
+// rdt1b.cpp:254-369; the PyTorch alignment model in
+// tests/alignment/test_rdt1b_alignment.py:73-210) with these changes:
+//   * weights are int8 per output channel (s_n = max|w_n| / 127) and every
+//     projection is one fused sfb_w8a16_linear call (dequant + GEMM + bias +
+//     GELU/SiLU + residual add);
+//   * the cross-attention K/V of both conditions are projected, k-normed and
+//     stored once per control tick (encode) instead of at every step and block
+//     (dit_block.cu:288-304); the cache buffer is the projection output itself
+//     and attention reads K/V from it through strides;
+//   * Q/K/V layouts: the QKV projection output [tokens, 3·D] is read in place
+//     by the attention kernel (BSHD strides), qk-norm runs in place, and the
+//     attention writes the O-projection input directly — no split/permute
+//     kernels (split_ops.cuh:62-255);
+//   * the language condition carries a key-padding length per session (the
+//     reference drops masks, attention.cu:30);
+//   * sessions are batched (B = number of robot sessions); the reference's
+//     denoise_step supports B = 1 only (rdt1b.cpp:268-270);
+//   * the sampler is DPM-Solver++ (2M) with x0 (sample) prediction over the
+//     squaredcos_cap_v2 DDPM schedule, as RDT-1B is configured
+//     (docs/RDT1B_ARCHITECTURE.md:217-223); the reference's C++ runtime has
+//     only Euler flow matching and DDIM (flow_matching.cpp:25-141).
+//
+// Weights are random (seeded, generated on the device); the same tensors are
+// readable through sfb_rdt1b_param so a test can run the CPU oracle on them.
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace sfb {
+
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream);
+int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
+                      const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
+                      int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
+                      int32_t num_splits, cudaStream_t stream);
+int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_t ldo, int rows,
+                    int D, float eps, cudaStream_t s);
+int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w, float eps,
+                         cudaStream_t s);
+
+namespace rdt {
+
+// ── device-side seeded initialisation ───────────────────────────────────────
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {   // SplitMix64 finaliser
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ float normal_at(uint64_t seed, uint64_t i) {
+    // Box-Muller on two uniform variates from a counter-based hash
+    const uint64_t a = mix64(seed ^ (i * 2 + 0x9e3779b97f4a7c15ull));
+    const uint64_t b = mix64(seed ^ (i * 2 + 1 + 0x7f4a7c159e3779b9ull));
+    const float u1 = (static_cast<float>(a >> 40) + 1.f) * (1.f / 16777217.f);
+    const float u2 = static_cast<float>(b >> 40) * (1.f / 16777216.f);
+    return sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+}
+__global__ void init_bf16_kernel(__nv_bfloat16* out, int64_t n, uint64_t seed, float mean, float std) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = __float2bfloat16_rn(mean + std * normal_at(seed, i));
+}
+// One block per output row: w ~ N(0, std²), s = max|w| / 127, q = round(w / s).
+__global__ void init_int8_rows_kernel(int8_t* q, float* s, int K, uint64_t seed, float std) {
+    const int r = blockIdx.x;
+    __shared__ float red[32];
+    float mx = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x)
+        mx = fmaxf(mx, fabsf(std * normal_at(seed, static_cast<uint64_t>(r) * K + k)));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        mx = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (threadIdx.x == 0) red[0] = mx;
+    }
+    __syncthreads();
+    const float sc = red[0] > 0.f ? red[0] / 127.f : 1.f;
+    if (threadIdx.x == 0) s[r] = sc;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float w = std * normal_at(seed, static_cast<uint64_t>(r) * K + k);
+        q[static_cast<int64_t>(r) * K + k] = static_cast<int8_t>(fminf(127.f, fmaxf(-127.f, rintf(w / sc))));
+    }
+}
+
+struct Linear {
+    int8_t* w = nullptr;
+    float* s = nullptr;
+    __nv_bfloat16* b = nullptr;
+    int N = 0, K = 0;
+};
+
+struct Block {
+    __nv_bfloat16 *norm1, *norm2, *norm3, *qn, *kn, *cqn, *ckn;
+    Linear qkv, proj, cq, ckv, cproj, fc1, fc2;
+};
+
+struct Model {
+    sfb_rdt1b_config c{};
+    int device = 0;
+    std::vector<void*> allocs;
+    std::map<std::string, std::pair<void*, std::pair<int64_t, int32_t>>> params;
+    uint64_t seed = 0, counter = 0;
+
+    Linear lang0, lang2, img0, img2, st0, st2, st4, t0, t2, f0, f2, fin1, fin2;
+    __nv_bfloat16 *x_pos, *lang_pos, *img_pos, *norm_final;
+    std::vector<Block> blocks;
+
+    // per-session state and cache
+    __nv_bfloat16 *state, *lang_c, *img_c;
+    int32_t* lang_len;
+    std::vector<__nv_bfloat16*> kv;
+    // step workspaces
+    __nv_bfloat16 *x, *xn, *qkv, *attn, *h, *ain, *ah1, *ah2, *seq, *tsc, *fsc, *th, *temb, *fh, *femb;
+    float *yfin, *xact, *x0prev;
+    // encode workspace
+    __nv_bfloat16* enc_h;
+    // DPM-Solver++ coefficients and timesteps
+    std::vector<float> ca, cb, cc, tsteps;
+    std::map<int, cudaGraphExec_t> graphs;
+    // the graph is captured and replayed on the model's own stream (capture is
+    // not possible on the legacy default stream a caller may be using)
+    cudaStream_t own = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+
+    int S() const { return c.horizon + 3; }
+};
+
+#define SFB_TRY(expr) do { int _rc = (expr); if (_rc != SFB_OK) return _rc; } while (0)
+
+static int dalloc(Model& m, void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) { record_cuda_error(e, "rdt1b allocation"); return SFB_ERR_CUDA; }
+    m.allocs.push_back(*p);
+    return SFB_OK;
+}
+
+static int new_bf16(Model& m, __nv_bfloat16** p, int64_t n, const char* name, float mean, float std) {
+    SFB_TRY(dalloc(m, reinterpret_cast<void**>(p), n * 2));
+    init_bf16_kernel<<<grid_for(n, 256), 256>>>(*p, n, m.seed + (++m.counter) * 0x1000193ull, mean, std);
+    if (name) m.params[name] = {*p, {n, SFB_BF16}};
+    return launch_status();
+}
+
+static int new_linear(Model& m, Linear& L, int N, int K, const std::string& name) {
+    L.N = N; L.K = K;
+    SFB_TRY(dalloc(m, reinterpret_cast<void**>(&L.w), static_cast<size_t>(N) * K));
+    SFB_TRY(dalloc(m, reinterpret_cast<void**>(&L.s), static_cast<size_t>(N) * 4));
+    init_int8_rows_kernel<<<N, 256>>>(L.w, L.s, K, m.seed + (++m.counter) * 0x1000193ull, m.c.weight_std);
+    SFB_TRY(launch_status());
+    m.params[name + ".weight_q"] = {L.w, {static_cast<int64_t>(N) * K, SFB_I8}};
+    m.params[name + ".weight_scale"] = {L.s, {N, SFB_F32}};
+    return new_bf16(m, &L.b, N, (name + ".bias").c_str(), 0.f, m.c.weight_std);
+}
+
+static int linear(const Linear& L, const __nv_bfloat16* x, int64_t ldx, int M, void* y, int64_t ldy,
+                  int act, const __nv_bfloat16* residual, int64_t ldr, cudaStream_t s, bool y_f32 = false) {
+    return w8a16_gemm_launch(x, ldx, L.w, L.s, L.b, residual, ldr, y, ldy, y_f32 ? SFB_F32 : SFB_BF16, M,
+                             L.N, L.K, act, 0, s);
+}
+
+// DPM-Solver++ (2M), x0 prediction, squaredcos_cap_v2 schedule over 1000
+// training steps, timesteps round(linspace(999, 0, n+1))[:-1], final target
+// noise level zero, first order on the first and last step.
+static void dpm_coefficients(Model& m) {
+    const int T = 1000, n = m.c.num_steps;
+    std::vector<double> ab(T);
+    auto abar = [](double t) {
+        const double v = cos((t + 0.008) / 1.008 * M_PI / 2.0);
+        return v * v;
+    };
+    double prod = 1.0;
+    for (int i = 0; i < T; ++i) {
+        const double beta = std::min(1.0 - abar((i + 1.0) / T) / abar(static_cast<double>(i) / T), 0.999);
+        prod *= 1.0 - beta;
+        ab[i] = prod;
+    }
+    std::vector<int> ts(n);
+    for (int i = 0; i < n; ++i) ts[i] = static_cast<int>(std::nearbyint(999.0 * (n - i) / n));
+    auto alpha = [&](int t) { return sqrt(ab[t]); };
+    auto sigma = [&](int t) { return sqrt(1.0 - ab[t]); };
+    auto lam = [&](int t) { return log(alpha(t)) - log(sigma(t)); };
+    m.ca.assign(n, 0.f); m.cb.assign(n, 0.f); m.cc.assign(n, 0.f); m.tsteps.assign(n, 0.f);
+    for (int i = 0; i < n; ++i) {
+        m.tsteps[i] = static_cast<float>(ts[i]);
+        if (i == n - 1) {                          // target noise level zero: x = x0
+            m.ca[i] = 0.f; m.cb[i] = 1.f; m.cc[i] = 0.f;
+            continue;
+        }
+        const int s = ts[i], t = ts[i + 1];
+        const double h = lam(t) - lam(s);
+        const double a = sigma(t) / sigma(s);
+        const double g = -alpha(t) * std::expm1(-h);   // −α_t (e^{−h} − 1)
+        if (i == 0) {
+            m.ca[i] = static_cast<float>(a); m.cb[i] = static_cast<float>(g); m.cc[i] = 0.f;
+        } else {
+            const double h0 = lam(s) - lam(ts[i - 1]);
+            const double r = h0 / h;
+            m.ca[i] = static_cast<float>(a);
+            m.cb[i] = static_cast<float>(g * (1.0 + 0.5 / r));
+            m.cc[i] = static_cast<float>(-g * 0.5 / r);
+        }
+    }
+}
+
+static int create(Model& m) {
+    const auto& c = m.c;
+    const int D = c.hidden, B = c.max_sessions, S = m.S();
+    const int A = c.action_dim;
+    SFB_TRY(new_linear(m, m.lang0, D, c.lang_dim, "lang_adaptor.0"));
+    SFB_TRY(new_linear(m, m.lang2, D, D, "lang_adaptor.2"));
+    SFB_TRY(new_linear(m, m.img0, D, c.img_dim, "img_adaptor.0"));
+    SFB_TRY(new_linear(m, m.img2, D, D, "img_adaptor.2"));
+    SFB_TRY(new_linear(m, m.st0, D, 2 * c.state_dim, "state_adaptor.0"));
+    SFB_TRY(new_linear(m, m.st2, D, D, "state_adaptor.2"));
+    SFB_TRY(new_linear(m, m.st4, D, D, "state_adaptor.4"));
+    SFB_TRY(new_linear(m, m.t0, D, 256, "t_embedder.mlp.0"));
+    SFB_TRY(new_linear(m, m.t2, D, D, "t_embedder.mlp.2"));
+    SFB_TRY(new_linear(m, m.f0, D, 256, "freq_embedder.mlp.0"));
+    SFB_TRY(new_linear(m, m.f2, D, D, "freq_embedder.mlp.2"));
+    SFB_TRY(new_bf16(m, &m.x_pos, static_cast<int64_t>(S) * D, "x_pos_embed", 0.f, c.weight_std));
+    SFB_TRY(new_bf16(m, &m.lang_pos, static_cast<int64_t>(c.max_lang_len) * D, "lang_cond_pos_embed", 0.f, c.weight_std));
+    SFB_TRY(new_bf16(m, &m.img_pos, static_cast<int64_t>(c.img_len) * D, "img_cond_pos_embed", 0.f, c.weight_std));
+    m.blocks.resize(c.num_layers);
+    for (int l = 0; l < c.num_layers; ++l) {
+        Block& bl = m.blocks[l];
+        const std::string p = "blocks." + std::to_string(l) + ".";
+        SFB_TRY(new_bf16(m, &bl.norm1, D, (p + "norm1.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_bf16(m, &bl.norm2, D, (p + "norm2.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_bf16(m, &bl.norm3, D, (p + "norm3.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_linear(m, bl.qkv, 3 * D, D, p + "attn.qkv"));
+        SFB_TRY(new_linear(m, bl.proj, D, D, p + "attn.proj"));
+        SFB_TRY(new_bf16(m, &bl.qn, 64, (p + "attn.q_norm.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_bf16(m, &bl.kn, 64, (p + "attn.k_norm.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_linear(m, bl.cq, D, D, p + "cross_attn.q"));
+        SFB_TRY(new_linear(m, bl.ckv, 2 * D, D, p + "cross_attn.kv"));
+        SFB_TRY(new_linear(m, bl.cproj, D, D, p + "cross_attn.proj"));
+        SFB_TRY(new_bf16(m, &bl.cqn, 64, (p + "cross_attn.q_norm.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_bf16(m, &bl.ckn, 64, (p + "cross_attn.k_norm.weight").c_str(), 1.f, 0.1f));
+        SFB_TRY(new_linear(m, bl.fc1, D, D, p + "ffn.fc1"));
+        SFB_TRY(new_linear(m, bl.fc2, D, D, p + "ffn.fc2"));
+    }
+    SFB_TRY(new_bf16(m, &m.norm_final, D, "final_layer.norm_final.weight", 1.f, 0.1f));
+    SFB_TRY(new_linear(m, m.fin1, D, D, "final_layer.ffn_final.fc1"));
+    SFB_TRY(new_linear(m, m.fin2, A, D, "final_layer.ffn_final.fc2"));
+
+    auto bf = [&](__nv_bfloat16** p, int64_t n) { return dalloc(m, reinterpret_cast<void**>(p), n * 2); };
+    auto f32 = [&](float** p, int64_t n) { return dalloc(m, reinterpret_cast<void**>(p), n * 4); };
+    const int64_t BS = static_cast<int64_t>(B) * S, BT1 = static_cast<int64_t>(B) * (c.horizon + 1);
+    SFB_TRY(bf(&m.state, static_cast<int64_t>(B) * c.state_dim));
+    SFB_TRY(bf(&m.lang_c, static_cast<int64_t>(B) * c.max_lang_len * D));
+    SFB_TRY(bf(&m.img_c, static_cast<int64_t>(B) * c.img_len * D));
+    SFB_TRY(dalloc(m, reinterpret_cast<void**>(&m.lang_len), static_cast<size_t>(B) * 4));
+    m.kv.resize(c.num_layers);
+    for (int l = 0; l < c.num_layers; ++l) {
+        const int Lk = (l % 2 == 0) ? c.max_lang_len : c.img_len;
+        SFB_TRY(bf(&m.kv[l], static_cast<int64_t>(B) * Lk * 2 * D));
+    }
+    SFB_TRY(bf(&m.x, BS * D)); SFB_TRY(bf(&m.xn, BS * D)); SFB_TRY(bf(&m.qkv, BS * 3 * D));
+    SFB_TRY(bf(&m.attn, BS * D)); SFB_TRY(bf(&m.h, BS * D));
+    SFB_TRY(bf(&m.ain, BT1 * 2 * c.state_dim)); SFB_TRY(bf(&m.ah1, BT1 * D)); SFB_TRY(bf(&m.ah2, BT1 * D));
+    SFB_TRY(bf(&m.seq, BT1 * D));
+    SFB_TRY(bf(&m.tsc, 256)); SFB_TRY(bf(&m.fsc, 256)); SFB_TRY(bf(&m.th, D)); SFB_TRY(bf(&m.temb, D));
+    SFB_TRY(bf(&m.fh, D)); SFB_TRY(bf(&m.femb, D));
+    SFB_TRY(f32(&m.yfin, BS * A));
+    SFB_TRY(f32(&m.xact, static_cast<int64_t>(B) * c.horizon * A));
+    SFB_TRY(f32(&m.x0prev, static_cast<int64_t>(B) * c.horizon * A));
+    const int64_t enc_rows = static_cast<int64_t>(B) * std::max(c.max_lang_len, c.img_len);
+    SFB_TRY(bf(&m.enc_h, enc_rows * D));
+    dpm_coefficients(m);
+    if (cudaStreamCreateWithFlags(&m.own, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&m.ev_in, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&m.ev_out, cudaEventDisableTiming) != cudaSuccess) {
+        record_cuda_error(cudaGetLastError(), "rdt1b stream");
+        return SFB_ERR_CUDA;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { record_cuda_error(e, "rdt1b init"); return SFB_ERR_CUDA; }
+    return SFB_OK;
+}
+
+static int attention(const Model& m, const __nv_bfloat16* q, int64_t q_sb, int64_t q_ss,
+                     const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_ss,
+                     __nv_bfloat16* out, int B, int Lq, int Lk, const int32_t* kv_len, cudaStream_t s) {
+    sfb_attn_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.q = q; a.k = k; a.v = v; a.out = out;
+    a.q_stride[0] = q_sb; a.q_stride[1] = 64; a.q_stride[2] = q_ss;
+    a.k_stride[0] = kv_sb; a.k_stride[1] = 64; a.k_stride[2] = kv_ss;
+    for (int i = 0; i < 3; ++i) a.v_stride[i] = a.k_stride[i];
+    a.out_stride[0] = static_cast<int64_t>(Lq) * m.c.hidden; a.out_stride[1] = 64;
+    a.out_stride[2] = m.c.hidden;
+    a.batch = B; a.heads = m.c.heads; a.heads_kv = m.c.heads; a.seq_q = Lq; a.seq_k = Lk;
+    a.head_dim = 64; a.dtype = SFB_BF16; a.kv_len = kv_len;
+    return attention_tc_launch(a, s);
+}
+
+// Condition encoding for one control tick (rdt1b.cpp:167-239 + the per-block
+// K/V projections of dit_block.cu:288-308, hoisted out of the step loop).
+static int encode(Model& m, int B, const void* lang, const int32_t* lang_len, const void* img,
+                  const void* state, cudaStream_t s) {
+    const auto& c = m.c;
+    const int D = c.hidden;
+    const float eps = 1e-6f;
+    auto cp = [&](void* dst, const void* src, size_t bytes) {
+        cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) { record_cuda_error(e, "rdt1b encode copy"); return SFB_ERR_CUDA; }
+        return SFB_OK;
+    };
+    SFB_TRY(cp(m.state, state, static_cast<size_t>(B) * c.state_dim * 2));
+    SFB_TRY(cp(m.lang_len, lang_len, static_cast<size_t>(B) * 4));
+    const int Ml = B * c.max_lang_len, Mi = B * c.img_len;
+    // adaptors: Linear → GELU → Linear (test_rdt1b_alignment.py:99-104)
+    SFB_TRY(linear(m.lang0, static_cast<const __nv_bfloat16*>(lang), c.lang_dim, Ml, m.enc_h, D, 1, nullptr, 0, s));
+    SFB_TRY(linear(m.lang2, m.enc_h, D, Ml, m.lang_c, D, 0, nullptr, 0, s));
+    rdt::add_rows_kernel<<<grid_for(static_cast<int64_t>(Ml) * D / 8, 256), 256, 0, s>>>(
+        m.lang_c, m.lang_pos, B, c.max_lang_len, D);
+    SFB_TRY(launch_status());
+    SFB_TRY(linear(m.img0, static_cast<const __nv_bfloat16*>(img), c.img_dim, Mi, m.enc_h, D, 1, nullptr, 0, s));
+    SFB_TRY(linear(m.img2, m.enc_h, D, Mi, m.img_c, D, 0, nullptr, 0, s));
+    rdt::add_rows_kernel<<<grid_for(static_cast<int64_t>(Mi) * D / 8, 256), 256, 0, s>>>(
+        m.img_c, m.img_pos, B, c.img_len, D);
+    SFB_TRY(launch_status());
+    // per-block cross-attention K/V cache: kv = cond·Wkvᵀ + b, K k-normed in place
+    for (int l = 0; l < c.num_layers; ++l) {
+        const bool lang_blk = (l % 2 == 0);
+        const int rows = lang_blk ? Ml : Mi;
+        SFB_TRY(linear(m.blocks[l].ckv, lang_blk ? m.lang_c : m.img_c, D, rows, m.kv[l], 2 * D, 0, nullptr, 0, s));
+        SFB_TRY(head_rms_norm_launch(m.kv[l], 2 * D, rows, c.heads, m.blocks[l].ckn, eps, s));
+    }
+    return SFB_OK;
+}
+
+// One denoising network evaluation (rdt1b.cpp:254-369, test_rdt1b_alignment.py:181-210)
+// on the current x_t (m.xact) at timestep t, leaving the x0 prediction in m.yfin.
+static int forward(Model& m, int B, float t, cudaStream_t s) {
+    const auto& c = m.c;
+    const int D = c.hidden, S = m.S(), T = c.horizon, A = c.action_dim;
+    const int M = B * S, Ma = B * (T + 1);
+    const float eps = 1e-6f;
+    // state adaptor on [state, x_t] with an all-ones action mask
+    rdt::adaptor_input_kernel<<<grid_for(static_cast<int64_t>(Ma) * 2 * A, 256), 256, 0, s>>>(
+        m.state, m.xact, m.ain, B, T, A);
+    SFB_TRY(launch_status());
+    SFB_TRY(linear(m.st0, m.ain, 2 * c.state_dim, Ma, m.ah1, D, 1, nullptr, 0, s));
+    SFB_TRY(linear(m.st2, m.ah1, D, Ma, m.ah2, D, 1, nullptr, 0, s));
+    SFB_TRY(linear(m.st4, m.ah2, D, Ma, m.seq, D, 0, nullptr, 0, s));
+    // timestep and control-frequency embeddings: sincos → Linear → SiLU → Linear
+    rdt::sincos_kernel<<<1, 128, 0, s>>>(t, 256, m.tsc);
+    rdt::sincos_kernel<<<1, 128, 0, s>>>(static_cast<float>(c.ctrl_freq), 256, m.fsc);
+    SFB_TRY(launch_status());
+    SFB_TRY(linear(m.t0, m.tsc, 256, 1, m.th, D, 2, nullptr, 0, s));
+    SFB_TRY(linear(m.t2, m.th, D, 1, m.temb, D, 0, nullptr, 0, s));
+    SFB_TRY(linear(m.f0, m.fsc, 256, 1, m.fh, D, 2, nullptr, 0, s));
+    SFB_TRY(linear(m.f2, m.fh, D, 1, m.femb, D, 0, nullptr, 0, s));
+    rdt::assemble_x_kernel<<<grid_for(static_cast<int64_t>(M) * D / 8, 256), 256, 0, s>>>(
+        m.temb, m.femb, m.seq, m.x_pos, m.x, B, S, D);
+    SFB_TRY(launch_status());
+
+    for (int l = 0; l < c.num_layers; ++l) {
+        const Block& bl = m.blocks[l];
+        // x = x + proj(attn(qk-norm(qkv(norm1(x)))))
+        SFB_TRY(rms_norm_launch(m.x, D, bl.norm1, m.xn, D, M, D, eps, s));
+        SFB_TRY(linear(bl.qkv, m.xn, D, M, m.qkv, 3 * D, 0, nullptr, 0, s));
+        SFB_TRY(head_rms_norm_launch(m.qkv, 3 * D, M, c.heads, bl.qn, eps, s));
+        SFB_TRY(head_rms_norm_launch(m.qkv + D, 3 * D, M, c.heads, bl.kn, eps, s));
+        SFB_TRY(attention(m, m.qkv, static_cast<int64_t>(S) * 3 * D, 3 * D, m.qkv + D, m.qkv + 2 * D,
+                          static_cast<int64_t>(S) * 3 * D, 3 * D, m.attn, B, S, S, nullptr, s));
+        SFB_TRY(linear(bl.proj, m.attn, D, M, m.x, D, 0, m.x, D, s));
+        // x = x + proj(cross_attn(qnorm(q(norm2(x))), K/V cache))
+        const bool lang_blk = (l % 2 == 0);
+        const int Lk = lang_blk ? c.max_lang_len : c.img_len;
+        SFB_TRY(rms_norm_launch(m.x, D, bl.norm2, m.xn, D, M, D, eps, s));
+        SFB_TRY(linear(bl.cq, m.xn, D, M, m.h, D, 0, nullptr, 0, s));
+        SFB_TRY(head_rms_norm_launch(m.h, D, M, c.heads, bl.cqn, eps, s));
+        SFB_TRY(attention(m, m.h, static_cast<int64_t>(S) * D, D, m.kv[l], m.kv[l] + D,
+                          static_cast<int64_t>(Lk) * 2 * D, 2 * D, m.attn, B, S, Lk,
+                          lang_blk ? m.lang_len : nullptr, s));
+        SFB_TRY(linear(bl.cproj, m.attn, D, M, m.x, D, 0, m.x, D, s));
+        // x = x + fc2(gelu(fc1(norm3(x))))
+        SFB_TRY(rms_norm_launch(m.x, D, bl.norm3, m.xn, D, M, D, eps, s));
+        SFB_TRY(linear(bl.fc1, m.xn, D, M, m.h, D, 1, nullptr, 0, s));
+        SFB_TRY(linear(bl.fc2, m.h, D, M, m.x, D, 0, m.x, D, s));
+    }
+    // final layer: norm → fc1 (GELU) → fc2, fp32 output [B·S, A]
+    SFB_TRY(rms_norm_launch(m.x, D, m.norm_final, m.xn, D, M, D, eps, s));
+    SFB_TRY(linear(m.fin1, m.xn, D, M, m.h, D, 1, nullptr, 0, s));
+    SFB_TRY(linear(m.fin2, m.h, D, M, m.yfin, A, 0, nullptr, 0, s, true));
+    return SFB_OK;
+}
+
+// The whole sampling loop on m.xact: num_steps network evaluations, each
+// followed by its DPM-Solver++ update.
+static int sample_loop(Model& m, int B, cudaStream_t s) {
+    const auto& c = m.c;
+    const int64_t n = static_cast<int64_t>(B) * c.horizon * c.action_dim;
+    for (int i = 0; i < c.num_steps; ++i) {
+        SFB_TRY(forward(m, B, m.tsteps[i], s));
+        rdt::dpm_update_kernel<<<grid_for(n, 256), 256, 0, s>>>(m.xact, m.yfin, m.x0prev, m.ca[i], m.cb[i],
+                                                                m.cc[i], B, c.horizon, c.action_dim, m.S());
+        SFB_TRY(launch_status());
+    }
+    return SFB_OK;
+}
+
+}  // namespace rdt
+}  // namespace sfb
+
+// ── C ABI ───────────────────────────────────────────────────────────────────
+using namespace sfb;
+
+extern "C" {
+
+int sfb_rdt1b_default_config(sfb_rdt1b_config* c) {
+    if (c == nullptr) return SFB_ERR_INVALID;
+    std::memset(c, 0, sizeof(*c));
+    // RDT1BConfig defaults (include/servoflow/models/rdt1b/config.h:28-57)
+    c->num_layers = 28; c->hidden = 2048; c->heads = 32; c->action_dim = 128; c->horizon = 64;
+    c->state_dim = 128; c->lang_dim = 4096; c->img_dim = 1152; c->max_lang_len = 1024;
+    c->img_len = 4374; c->max_sessions = 1; c->num_steps = 5; c->ctrl_freq = 25;
+    c->weight_std = 0.02f;
+    return SFB_OK;
+}
+
+int sfb_rdt1b_create(const sfb_rdt1b_config* cfg, uint64_t seed, void** handle) {
+    if (cfg == nullptr || handle == nullptr) return SFB_ERR_INVALID;
+    const auto& c = *cfg;
+    if (c.hidden != c.heads * 64 || c.hidden % 256 || c.num_layers < 1 || c.max_sessions < 1 ||
+        c.num_steps < 1 || c.num_steps > 64 || c.action_dim % 32 || c.lang_dim % 64 || c.img_dim % 64 ||
+        (2 * c.state_dim) % 64 || c.horizon < 1 || c.max_lang_len < 1 || c.img_len < 1 ||
+        2 * c.state_dim != 2 * c.action_dim)
+        return SFB_ERR_SHAPE;
+    if (!is_sm100(device_info())) return SFB_ERR_UNSUPPORTED;
+    auto* m = new (std::nothrow) rdt::Model();
+    if (m == nullptr) return SFB_ERR_CUDA;
+    m->c = c;
+    m->seed = seed;
+    cudaGetDevice(&m->device);
+    const int rc = rdt::create(*m);
+    if (rc != SFB_OK) {
+        for (void* ptr : m->allocs) cudaFree(ptr);
+        delete m;
+        return rc;
+    }
+    *handle = m;
+    return SFB_OK;
+}
+
+int sfb_rdt1b_destroy(void* handle) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr) return SFB_ERR_INVALID;
+    cudaDeviceSynchronize();
+    for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+    if (m->ev_in) cudaEventDestroy(m->ev_in);
+    if (m->ev_out) cudaEventDestroy(m->ev_out);
+    if (m->own) cudaStreamDestroy(m->own);
+    for (void* ptr : m->allocs) cudaFree(ptr);
+    delete m;
+    return SFB_OK;
+}
+
+int sfb_rdt1b_encode(void* handle, int32_t sessions, const void* lang_tokens, const int32_t* lang_len,
+                     const void* img_tokens, const void* state, void* stream) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || lang_tokens == nullptr || lang_len == nullptr || img_tokens == nullptr ||
+        state == nullptr)
+        return SFB_ERR_INVALID;
+    if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
+    return rdt::encode(*m, sessions, lang_tokens, lang_len, img_tokens, state,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int sfb_rdt1b_forward(void* handle, int32_t sessions, const float* x_t, float t, float* x0_out,
+                      void* stream) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || x_t == nullptr || x0_out == nullptr) return SFB_ERR_INVALID;
+    if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t bytes = static_cast<size_t>(sessions) * m->c.horizon * m->c.action_dim * 4;
+    if (cudaMemcpyAsync(m->xact, x_t, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) return SFB_ERR_CUDA;
+    SFB_TRY(rdt::forward(*m, sessions, t, s));
+    // x0 prediction: rows 3.. of each session's final-layer output
+    const int S = m->S(), T = m->c.horizon, A = m->c.action_dim;
+    cudaError_t e = cudaMemcpy2DAsync(x0_out, static_cast<size_t>(T) * A * 4,
+                                      m->yfin + static_cast<size_t>(S - T) * A, static_cast<size_t>(S) * A * 4,
+                                      static_cast<size_t>(T) * A * 4, sessions, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) { record_cuda_error(e, "rdt1b forward copy"); return SFB_ERR_CUDA; }
+    return SFB_OK;
+}
+
+int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* actions,
+                     int32_t use_graph, void* stream) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || noise == nullptr || actions == nullptr) return SFB_ERR_INVALID;
+    if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    // all work runs on the model's stream, ordered after the caller's prior work
+    cudaStream_t s = m->own;
+    if (cudaEventRecord(m->ev_in, caller) != cudaSuccess || cudaStreamWaitEvent(s, m->ev_in, 0) != cudaSuccess) {
+        record_cuda_error(cudaGetLastError(), "rdt1b sample ordering");
+        return SFB_ERR_CUDA;
+    }
+    const size_t bytes = static_cast<size_t>(sessions) * m->c.horizon * m->c.action_dim * 4;
+    if (cudaMemcpyAsync(m->xact, noise, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+        cudaMemsetAsync(m->x0prev, 0, bytes, s) != cudaSuccess) {
+        record_cuda_error(cudaGetLastError(), "rdt1b sample input");
+        return SFB_ERR_CUDA;
+    }
+    if (!use_graph) {
+        SFB_TRY(rdt::sample_loop(*m, sessions, s));
+    } else {
+        auto it = m->graphs.find(sessions);
+        if (it == m->graphs.end()) {
+            // first call for this session count: run eagerly (sets kernel
+            // attributes, produces this call's result), then capture the loop
+            SFB_TRY(rdt::sample_loop(*m, sessions, s));
+            cudaGraph_t g = nullptr;
+            cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+            if (e != cudaSuccess) { record_cuda_error(e, "begin capture"); return SFB_ERR_CUDA; }
+            const int rc = rdt::sample_loop(*m, sessions, s);
+            e = cudaStreamEndCapture(s, &g);
+            if (rc != SFB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+            if (e != cudaSuccess) { record_cuda_error(e, "end capture"); return SFB_ERR_CUDA; }
+            cudaGraphExec_t ge = nullptr;
+            e = cudaGraphInstantiate(&ge, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) { record_cuda_error(e, "graph instantiate"); return SFB_ERR_CUDA; }
+            m->graphs[sessions] = ge;
+        } else {
+            cudaError_t e = cudaGraphLaunch(it->second, s);
+            if (e != cudaSuccess) { record_cuda_error(e, "graph launch"); return SFB_ERR_CUDA; }
+        }
+    }
+    if (cudaMemcpyAsync(actions, m->xact, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+        cudaEventRecord(m->ev_out, s) != cudaSuccess || cudaStreamWaitEvent(caller, m->ev_out, 0) != cudaSuccess) {
+        record_cuda_error(cudaGetLastError(), "rdt1b sample output");
+        return SFB_ERR_CUDA;
+    }
+    return SFB_OK;
+}
+
+int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, int32_t* dtype) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || name == nullptr || ptr == nullptr || numel == nullptr || dtype == nullptr)
+        return SFB_ERR_INVALID;
+    auto it = m->params.find(name);
+    if (it == m->params.end()) return SFB_ERR_INVALID;
+    *ptr = it->second.first;
+    *numel = it->second.second.first;
+    *dtype = it->second.second.second;
+    return SFB_OK;
+}
+
+int sfb_rdt1b_schedule(void* handle, float* timesteps, float* coef_a, float* coef_b, float* coef_c,
+                       int32_t n) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || n != m->c.num_steps) return SFB_ERR_INVALID;
+    for (int i = 0; i < n; ++i) {
+        if (timesteps) timesteps[i] = m->tsteps[i];
+        if (coef_a) coef_a[i] = m->ca[i];
+        if (coef_b) coef_b[i] = m->cb[i];
+        if (coef_c) coef_c[i] = m->cc[i];
+    }
+    return SFB_OK;
+}
+
+}  // extern "C"

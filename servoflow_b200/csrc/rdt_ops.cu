@@ -1,0 +1,227 @@
+// rdt_ops.cu — the small kernels around the attention and projection kernels
+// in an RDT-1B denoising step (sm_100a). All are bandwidth- or latency-bound
+// elementwise / row-reduction kernels; none allocates.
+//
+//   rms_norm        x / sqrt(mean(x²) + eps) · w over rows of D (RmsNorm of
+//                   tests/alignment/test_rdt1b_alignment.py:73-80; the
+//                   reference's rms_norm_kernel_impl, src/backend/cuda/ops/
+//                   norm.cuh:89-122), fp32 math, bf16 in/out, warp per row.
+//   head_rms_norm   the same per 64-wide head, in place on a strided
+//                   [tokens, heads·64] block (the qk-norm of dit_block.cu:185-196,
+//                   applied where the projection wrote Q/K — no layout copy).
+//   sincos_embed    [cos(t·f_i), sin(t·f_i)], f_i = 10000^(−i/half)
+//                   (dit_block.cu:58-72).
+//   assemble_x      x = [t_emb, freq_emb, state_traj, action_traj] + x_pos_embed
+//                   per session (rdt1b.cpp:305-340).
+//   adaptor_input   cat([state | x_t], ones) per session, the state-adaptor input
+//                   (test_rdt1b_alignment.py:204-209).
+//   add_rows        cond += pos (condition position embeddings).
+//   dpm_update      x ← a·x + b·x0 + c·x0_prev (one DPM-Solver++ step; the
+//                   coefficients are computed on the host).
+#include "common.cuh"
+
+namespace sfb {
+namespace rdt {
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+
+// x, out: [rows, D] with row strides; w: [D]; D % 256 == 0, D <= 8192.
+__global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                int64_t ldo, int rows, int D, float eps) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const __nv_bfloat16* xr = x + warp * ldx;
+    float ss = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + eps);
+    __nv_bfloat16* orow = out + warp * ldo;
+    for (int c = lane * 8; c < D; c += 256) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+        const uint4 g = *reinterpret_cast<const uint4*>(w + c);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const __nv_bfloat162* gw = reinterpret_cast<const __nv_bfloat162*>(&g);
+        uint4 r;
+        __nv_bfloat162* ro = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]), gg = __bfloat1622float2(gw[i]);
+            // (x / rms) · w, the order of the reference's RmsNorm
+            ro[i] = __floats2bfloat162_rn(f.x * inv * gg.x, f.y * inv * gg.y);
+        }
+        *reinterpret_cast<uint4*>(orow + c) = r;
+    }
+}
+
+// In place: for each token row and each head h in [0, heads), the 64 values at
+// x[row·ld + h·64 ...] are RMS-normalised with weight w[64]. 8 threads per head.
+__global__ void head_rms_norm_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int rows, int heads,
+                                     const __nv_bfloat16* __restrict__ w, float eps) {
+    const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 3, sub = threadIdx.x & 7;
+    if (g >= rows * heads) return;
+    const int row = g / heads, h = g - row * heads;
+    __nv_bfloat16* p = x + row * ld + h * 64 + sub * 8;
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&u);
+    float f[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __bfloat1622float2(v[i]);
+        f[2 * i] = t.x; f[2 * i + 1] = t.y;
+        ss = fmaf(t.x, t.x, fmaf(t.y, t.y, ss));
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    const float inv = 1.f / sqrtf(ss / 64.f + eps);
+    const uint4 gu = *reinterpret_cast<const uint4*>(w + sub * 8);
+    const __nv_bfloat162* gw = reinterpret_cast<const __nv_bfloat162*>(&gu);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 gg = __bfloat1622float2(gw[i]);
+        v[i] = __floats2bfloat162_rn(f[2 * i] * inv * gg.x, f[2 * i + 1] * inv * gg.y);
+    }
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+// out[0:half] = cos(t·f_i), out[half:2half] = sin(t·f_i), f_i = exp(−ln(10000)·i/half)
+__global__ void sincos_kernel(float t, int dim, __nv_bfloat16* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int half = dim / 2;
+    if (i >= half) return;
+    const float freq = expf(-logf(10000.f) * static_cast<float>(i) / static_cast<float>(half));
+    const float a = t * freq;
+    out[i] = __float2bfloat16_rn(cosf(a));
+    out[half + i] = __float2bfloat16_rn(sinf(a));
+}
+
+// x[b, 0] = t_emb + pos[0]; x[b, 1] = f_emb + pos[1]; x[b, 2 + i] = seq[b, i] + pos[2 + i]
+__global__ void assemble_x_kernel(const __nv_bfloat16* __restrict__ t_emb,
+                                  const __nv_bfloat16* __restrict__ f_emb,
+                                  const __nv_bfloat16* __restrict__ seq,   // [B·(S−2), D]
+                                  const __nv_bfloat16* __restrict__ pos,   // [S, D]
+                                  __nv_bfloat16* __restrict__ x, int B, int S, int D) {
+    const int64_t n8 = static_cast<int64_t>(B) * S * D / 8;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = i * 8;
+        const int col = static_cast<int>(e % D);
+        const int64_t r = e / D;
+        const int b = static_cast<int>(r / S), s = static_cast<int>(r % S);
+        const __nv_bfloat16* src = s == 0 ? t_emb + col
+                                 : s == 1 ? f_emb + col
+                                          : seq + (static_cast<int64_t>(b) * (S - 2) + (s - 2)) * D + col;
+        const uint4 a = *reinterpret_cast<const uint4*>(src);
+        const uint4 p = *reinterpret_cast<const uint4*>(pos + static_cast<int64_t>(s) * D + col);
+        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&p);
+        uint4 o;
+        __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 fa = __bfloat1622float2(ha[k]), fp = __bfloat1622float2(hp[k]);
+            ho[k] = __floats2bfloat162_rn(fa.x + fp.x, fa.y + fp.y);
+        }
+        *reinterpret_cast<uint4*>(x + e) = o;
+    }
+}
+
+// out[b, 0] = [state[b], 1...1]; out[b, 1 + i] = [x_t[b, i], 1...1]   (A = action dim)
+__global__ void adaptor_input_kernel(const __nv_bfloat16* __restrict__ state,  // [B, A]
+                                     const float* __restrict__ x_t,            // [B, T, A]
+                                     __nv_bfloat16* __restrict__ out,          // [B·(T+1), 2A]
+                                     int B, int T, int A) {
+    const int64_t n = static_cast<int64_t>(B) * (T + 1) * 2 * A;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % (2 * A));
+        const int64_t r = i / (2 * A);
+        const int b = static_cast<int>(r / (T + 1)), s = static_cast<int>(r % (T + 1));
+        float v;
+        if (c >= A) v = 1.f;
+        else if (s == 0) v = bf(state[static_cast<int64_t>(b) * A + c]);
+        else v = x_t[(static_cast<int64_t>(b) * T + (s - 1)) * A + c];
+        out[i] = __float2bfloat16_rn(v);
+    }
+}
+
+// cond[b, s, :] += pos[s, :]   for s < S (rows of cond per session: S, row stride D)
+__global__ void add_rows_kernel(__nv_bfloat16* __restrict__ cond, const __nv_bfloat16* __restrict__ pos,
+                                int B, int S, int D) {
+    const int64_t n8 = static_cast<int64_t>(B) * S * D / 8;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = i * 8;
+        const int64_t s = (e / D) % S;
+        const int col = static_cast<int>(e % D);
+        uint4 a = *reinterpret_cast<const uint4*>(cond + e);
+        const uint4 p = *reinterpret_cast<const uint4*>(pos + s * D + col);
+        __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&a);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 fa = __bfloat1622float2(ha[k]), fp = __bfloat1622float2(hp[k]);
+            ha[k] = __floats2bfloat162_rn(fa.x + fp.x, fa.y + fp.y);
+        }
+        *reinterpret_cast<uint4*>(cond + e) = a;
+    }
+}
+
+// One DPM-Solver++ update over [B, T, A]: x0 rows are rows 3..3+T−1 of each
+// session's final-layer output [B, S, A] (fp32). x ← a·x + b·x0 + c·x0_prev,
+// then x0_prev ← x0.
+__global__ void dpm_update_kernel(float* __restrict__ x, const float* __restrict__ y_final,
+                                  float* __restrict__ x0_prev, float a, float bcoef, float c,
+                                  int B, int T, int A, int S) {
+    const int64_t n = static_cast<int64_t>(B) * T * A;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int col = static_cast<int>(i % A);
+        const int64_t r = i / A;
+        const int b = static_cast<int>(r / T), t = static_cast<int>(r % T);
+        const float x0 = y_final[(static_cast<int64_t>(b) * S + (S - T) + t) * A + col];
+        x[i] = a * x[i] + bcoef * x0 + c * x0_prev[i];
+        x0_prev[i] = x0;
+    }
+}
+
+inline unsigned grid_for(int64_t n, int threads) {
+    int64_t g = (n + threads - 1) / threads;
+    return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(g, 148 * 32)));
+}
+
+}  // namespace rdt
+
+int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_t ldo, int rows,
+                    int D, float eps, cudaStream_t s) {
+    if (D % 256 != 0 || (ldx % 8) || (ldo % 8)) return SFB_ERR_SHAPE;
+    if (rows <= 0) return SFB_OK;
+    const int warps_per_block = 4;
+    rdt::rms_norm_kernel<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+        static_cast<__nv_bfloat16*>(out), ldo, rows, D, eps);
+    return launch_status();
+}
+
+int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w, float eps,
+                         cudaStream_t s) {
+    if (ld % 8) return SFB_ERR_SHAPE;
+    if (rows <= 0 || heads <= 0) return SFB_OK;
+    const int64_t threads = static_cast<int64_t>(rows) * heads * 8;
+    rdt::head_rms_norm_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
+        static_cast<__nv_bfloat16*>(x), ld, rows, heads, static_cast<const __nv_bfloat16*>(w), eps);
+    return launch_status();
+}
+
+}  // namespace sfb

@@ -4,4 +4,6 @@
 #include "attn_simt.cu"
 #include "dequant.cu"
 #include "w8a16_gemm.cu"
+#include "rdt_ops.cu"
+#include "rdt1b.cu"
 #include "capi.cu"

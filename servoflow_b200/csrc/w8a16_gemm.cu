@@ -5,7 +5,7 @@
 //
 // X: bf16 activations [M, K] (row stride ldx); Wq: int8 weights [N, K]
 // (row-major, one row per output channel, contiguous); s: fp32 per-output-
-// channel scales; bias: optional bf16 [N]; act: none or GELU (tanh form);
+// channel scales; bias: optional bf16 [N]; act: none, GELU (tanh form) or SiLU;
 // R: optional bf16 residual [M, N] (may alias Y); Y: bf16 or fp32 [M, N].
 //
 // It replaces the reference's two-step path — dequantise the whole weight
@@ -46,7 +46,7 @@ struct W8Params {
     int32_t        bn;            // MMA N (tokens per CTA), multiple of 32, <= 256
     int32_t        kchunks;       // K / 64
     int32_t        splits;        // cluster size along grid.x
-    int32_t        act;           // 0 none, 1 GELU (tanh)
+    int32_t        act;           // 0 none, 1 GELU (tanh), 2 SiLU
     int32_t        y_f32;         // 1: fp32 output
 };
 
@@ -206,6 +206,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     auto finish = [&](float acc, int m) {
         float y = fmaf(acc, sc, bi);
         if (p.act == 1) y = gelu_tanh(y);
+        else if (p.act == 2) y = y / (1.f + expf(-y));          // SiLU
         if (p.residual)
             y += __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[m * p.ldr + nrow]);
         if (p.y_f32) static_cast<float*>(p.y)[m * p.ldy + nrow] = y;
@@ -293,7 +294,7 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     if (M == 0) return SFB_OK;
     if (K % 64 != 0 || N % 32 != 0) return SFB_ERR_SHAPE;
     if (y_dtype != SFB_BF16 && y_dtype != SFB_F32) return SFB_ERR_DTYPE;
-    if (act != 0 && act != 1) return SFB_ERR_INVALID;
+    if (act < 0 || act > 2) return SFB_ERR_INVALID;
     auto aligned16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
     if (!aligned16(x) || !aligned16(w) || (ldx * 2) % 16 != 0) return SFB_ERR_ALIGN;
     if (residual != nullptr && ldr < N) return SFB_ERR_SHAPE;

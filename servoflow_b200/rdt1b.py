@@ -1,0 +1,120 @@
+"""Python handle on the RDT-1B denoising runtime of libsfb200 (C ABI
+sfb_rdt1b_*). torch tensors supply device memory and streams only."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _capi
+
+
+class RDT1BConfig(ctypes.Structure):
+    """Mirror of ``sfb_rdt1b_config`` (include/sfb200.h)."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "num_layers", "hidden", "heads", "action_dim", "horizon", "state_dim", "lang_dim", "img_dim",
+        "max_lang_len", "img_len", "max_sessions", "num_steps", "ctrl_freq")] + [
+        ("weight_std", ctypes.c_float)]
+
+
+def _declare(lib):
+    c = ctypes
+    if getattr(lib, "_rdt_declared", False):
+        return
+    lib.sfb_rdt1b_default_config.argtypes = [c.POINTER(RDT1BConfig)]
+    lib.sfb_rdt1b_create.argtypes = [c.POINTER(RDT1BConfig), c.c_uint64, c.POINTER(c.c_void_p)]
+    lib.sfb_rdt1b_destroy.argtypes = [c.c_void_p]
+    lib.sfb_rdt1b_encode.argtypes = [c.c_void_p, c.c_int32, c.c_void_p, c.c_void_p, c.c_void_p,
+                                     c.c_void_p, c.c_void_p]
+    lib.sfb_rdt1b_forward.argtypes = [c.c_void_p, c.c_int32, c.c_void_p, c.c_float, c.c_void_p,
+                                      c.c_void_p]
+    lib.sfb_rdt1b_sample.argtypes = [c.c_void_p, c.c_int32, c.c_void_p, c.c_void_p, c.c_int32,
+                                     c.c_void_p]
+    lib.sfb_rdt1b_param.argtypes = [c.c_void_p, c.c_char_p, c.POINTER(c.c_void_p),
+                                    c.POINTER(c.c_int64), c.POINTER(c.c_int32)]
+    lib.sfb_rdt1b_schedule.argtypes = [c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p,
+                                       c.c_int32]
+    for f in ("default_config", "create", "destroy", "encode", "forward", "sample", "param",
+              "schedule"):
+        getattr(lib, "sfb_rdt1b_" + f).restype = c.c_int
+    lib._rdt_declared = True
+
+
+def default_config(**overrides) -> RDT1BConfig:
+    lib = _capi.lib()
+    _declare(lib)
+    cfg = RDT1BConfig()
+    _capi.check(lib.sfb_rdt1b_default_config(ctypes.byref(cfg)), "default_config")
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+def _sh(stream):
+    return torch.cuda.current_stream().cuda_stream if stream is None else int(stream.cuda_stream)
+
+
+class RDT1B:
+    """Model handle: encode() once per control tick, sample() per chunk."""
+
+    _DT = {_capi.SFB_BF16: torch.bfloat16, _capi.SFB_F32: torch.float32, _capi.SFB_I8: torch.int8}
+
+    def __init__(self, cfg: RDT1BConfig, seed: int = 0):
+        self.lib = _capi.lib()
+        _declare(self.lib)
+        self.cfg = cfg
+        h = ctypes.c_void_p()
+        _capi.check(self.lib.sfb_rdt1b_create(ctypes.byref(cfg), seed, ctypes.byref(h)), "rdt1b create")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.sfb_rdt1b_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode(self, lang, lang_len, img, state, stream=None):
+        B = lang.shape[0]
+        _capi.check(self.lib.sfb_rdt1b_encode(self.h, B, lang.data_ptr(), lang_len.data_ptr(),
+                                              img.data_ptr(), state.data_ptr(), _sh(stream)),
+                    "rdt1b encode")
+
+    def forward(self, x_t, t: float, out, stream=None):
+        _capi.check(self.lib.sfb_rdt1b_forward(self.h, x_t.shape[0], x_t.data_ptr(), float(t),
+                                               out.data_ptr(), _sh(stream)), "rdt1b forward")
+
+    def sample(self, noise, out, use_graph=True, stream=None):
+        _capi.check(self.lib.sfb_rdt1b_sample(self.h, noise.shape[0], noise.data_ptr(), out.data_ptr(),
+                                              1 if use_graph else 0, _sh(stream)), "rdt1b sample")
+
+    def param(self, name: str) -> torch.Tensor:
+        """A copy (on the GPU) of a model parameter."""
+        ptr, n, dt = ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_int32()
+        _capi.check(self.lib.sfb_rdt1b_param(self.h, name.encode(), ctypes.byref(ptr), ctypes.byref(n),
+                                             ctypes.byref(dt)), f"param {name}")
+        out = torch.empty(n.value, dtype=self._DT[dt.value], device="cuda")
+        torch.cuda.synchronize()
+        _copy_d2d(out.data_ptr(), ptr.value, n.value * out.element_size())
+        return out
+
+    def schedule(self):
+        n = self.cfg.num_steps
+        arrs = [(ctypes.c_float * n)() for _ in range(4)]
+        _capi.check(self.lib.sfb_rdt1b_schedule(self.h, *[ctypes.cast(a, ctypes.c_void_p) for a in arrs], n),
+                    "schedule")
+        return [list(a) for a in arrs]
+
+
+def _copy_d2d(dst: int, src: int, nbytes: int) -> None:
+    lib = _capi.lib()
+    if not hasattr(lib, "_copy_declared"):
+        lib.sfb_copy_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
+        lib.sfb_copy_device.restype = ctypes.c_int
+        lib._copy_declared = True
+    _capi.check(lib.sfb_copy_device(dst, src, nbytes), "copy")

@@ -1,0 +1,96 @@
+"""GPU tests of the RDT-1B denoising runtime against the CPU oracle
+(oracle/rdt1b_ref.py), at full width (hidden 2048, 32 heads) with 2 blocks and
+shortened condition lengths so the fp32 CPU oracle stays fast.
+
+Criteria: the reference's own alignment bar for a bf16 model
+(tests/alignment/test_rdt1b_alignment.py:426): max |ours − oracle| < 0.05 and
+cosine similarity > 0.9999.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import rdt1b_ref
+from servoflow_b200.rdt1b import RDT1B, default_config
+
+pytestmark = pytest.mark.gpu
+
+
+def close(ours, ref):
+    a = ours.float().cpu().reshape(-1).double()
+    b = ref.float().reshape(-1).double()
+    max_abs = (a - b).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(a[None], b[None]).item()
+    return max_abs, cos
+
+
+@pytest.fixture(scope="module")
+def setup(gpu):
+    cfg = default_config(num_layers=2, max_lang_len=64, img_len=256, max_sessions=2)
+    model = RDT1B(cfg, seed=1234)
+    g = torch.Generator().manual_seed(42)
+    B = 2
+    lang = torch.randn(B, cfg.max_lang_len, cfg.lang_dim, generator=g).bfloat16()
+    img = torch.randn(B, cfg.img_len, cfg.img_dim, generator=g).bfloat16()
+    state = torch.randn(B, cfg.state_dim, generator=g).bfloat16()
+    lens = torch.tensor([40, 64], dtype=torch.int32)
+    noise = torch.randn(B, cfg.horizon, cfg.action_dim, generator=g)
+    dev = gpu
+    model.encode(lang.to(dev), lens.to(dev), img.to(dev), state.to(dev))
+    torch.cuda.synchronize()
+    ref = rdt1b_ref.RefRDT(rdt1b_ref.load_weights(model, cfg), cfg)
+    lang_c, img_c = ref.encode(lang.float(), img.float())
+    yield dict(cfg=cfg, model=model, ref=ref, lang=lang, img=img, state=state, lens=lens, noise=noise,
+               lang_c=lang_c, img_c=img_c, dev=dev)
+    model.close()
+
+
+def test_single_network_evaluation(setup):
+    s = setup
+    out = torch.empty(2, s["cfg"].horizon, s["cfg"].action_dim, device=s["dev"])
+    s["model"].forward(s["noise"].to(s["dev"]), 999.0, out)
+    torch.cuda.synchronize()
+    ref = s["ref"].forward(s["lang_c"], s["img_c"], s["lens"], s["state"].float(), s["noise"], 999)
+    max_abs, cos = close(out, ref)
+    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+
+
+def test_schedule_matches_oracle(setup):
+    ts, a, b, c = setup["model"].schedule()
+    rts, ra, rb, rc = rdt1b_ref.dpm_schedule(setup["cfg"].num_steps)
+    assert ts == [float(t) for t in rts]
+    for x, y in ((a, ra), (b, rb), (c, rc)):
+        assert np.allclose(x, y, rtol=1e-6, atol=1e-7)
+
+
+def test_sampling_graph_matches_oracle_and_replays(setup):
+    s = setup
+    noise = s["noise"].to(s["dev"])
+    out1 = torch.empty_like(noise)
+    out2 = torch.empty_like(noise)
+    out3 = torch.empty_like(noise)
+    s["model"].sample(noise, out1, use_graph=False)      # eager
+    s["model"].sample(noise, out2, use_graph=True)       # eager first call, then capture
+    s["model"].sample(noise, out3, use_graph=True)       # graph replay
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2) and torch.equal(out2, out3)
+    ref = s["ref"].sample(s["lang_c"], s["img_c"], s["lens"], s["state"].float(), s["noise"])
+    max_abs, cos = close(out3, ref)
+    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+
+
+def test_masked_language_tokens_do_not_matter(setup):
+    s = setup
+    lang2 = s["lang"].clone()
+    lang2[0, 40:] = torch.randn(24, s["cfg"].lang_dim).bfloat16() * 5    # beyond lang_len[0]
+    m = s["model"]
+    noise = s["noise"].to(s["dev"])
+    a = torch.empty_like(noise)
+    b = torch.empty_like(noise)
+    m.forward(noise, 599.0, a)
+    m.encode(lang2.to(s["dev"]), s["lens"].to(s["dev"]), s["img"].to(s["dev"]), s["state"].to(s["dev"]))
+    m.forward(noise, 599.0, b)
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], b[0])
+    m.encode(s["lang"].to(s["dev"]), s["lens"].to(s["dev"]), s["img"].to(s["dev"]), s["state"].to(s["dev"]))
+    torch.cuda.synchronize()

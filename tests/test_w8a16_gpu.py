@@ -41,7 +41,7 @@ def check(be, M, N, K, seed, dev, act="none", bias=True, residual=False, splits=
     ref = oracle.w8a16_linear(x.float().cpu().numpy(), q.cpu().numpy(), s.cpu().numpy(),
                               None if b is None else b.float().cpu().numpy(),
                               None if r is None else r.float().cpu().numpy(),
-                              act=1 if act == "gelu" else 0)
+                              act={"none": 0, "gelu": 1, "silu": 2}[act])
     out = y.float().cpu().numpy()
     if f32:
         tol = 1e-4 * np.maximum(np.abs(ref), 1.0)
@@ -68,6 +68,10 @@ def test_rdt_step_shapes(be, gpu, N):
 
 def test_gelu_and_residual(be, gpu):
     check(be, 67, 2048, 2048, 5, gpu, act="gelu", residual=True)
+
+
+def test_silu_single_token(be, gpu):
+    check(be, 1, 2048, 256, 6, gpu, act="silu")
 
 
 @pytest.mark.parametrize("M", [1, 16, 32, 33, 100, 128, 255, 256, 300, 600])
