@@ -156,7 +156,7 @@ int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype
  * stride ldr, or NULL (may alias y); y: y_dtype (SFB_BF16 or SFB_F32) [M, N]
  * with row stride ldy. act: 0 none, 1 GELU (tanh form, as the reference's
  * cuBLASLt GELU epilogue and the RDT-1B MLPs use), 2 SiLU (timestep MLP). K % 64 == 0, N % 32 == 0.
- * num_splits: split-K cluster size for small M (0 = automatic).
+ * num_splits: split-K cluster size for M <= 128: 1, 2, 4 or 8 (0 = automatic).
  * The result equals dequantise-then-GEMM up to fp32 summation order.
  */
 int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,

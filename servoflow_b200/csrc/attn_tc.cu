@@ -194,15 +194,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int rows  = min(128, p.Lq - q0);
     const int groups = (rows + 31) >> 5;            // active 32-row windows per group
 
-    // Key range of this (batch, q-tile), then this CTA's share of its tiles.
-    int kend = p.Lk;
-    if (p.kv_len != nullptr) kend = min(kend, max(0, p.kv_len[b]));
-    if (p.causal) kend = min(kend, q0 + rows);
-    const int ntiles  = (kend + kTileKeys - 1) / kTileKeys;
-    const int tbase   = ntiles / p.splits;
-    const int trem    = ntiles - tbase * p.splits;
-    const int t_begin = split * tbase + min(split, trem);
-    const int ntl     = tbase + (split < trem ? 1 : 0);
 
     SFB_T(0);
 #ifdef SFB_TRACE
@@ -235,7 +226,19 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem = *tmem_holder;
+    pdl_trigger();                       // TMEM is held: the next kernel may start
+    pdl_wait();                          // Q/K/V, key lengths and the output belong to earlier kernels
     SFB_T(1);
+
+    // Key range of this (batch, q-tile), then this CTA's share of its tiles.
+    int kend = p.Lk;
+    if (p.kv_len != nullptr) kend = min(kend, max(0, p.kv_len[b]));
+    if (p.causal) kend = min(kend, q0 + rows);
+    const int ntiles  = (kend + kTileKeys - 1) / kTileKeys;
+    const int tbase   = ntiles / p.splits;
+    const int trem    = ntiles - tbase * p.splits;
+    const int t_begin = split * tbase + min(split, trem);
+    const int ntl     = tbase + (split < trem ? 1 : 0);
 
     bool ok = true;
     auto wait = [&](int bar, uint32_t parity) {
@@ -654,7 +657,7 @@ int choose_attn_splits(int units, int ntiles_max, int num_sms) {
     return s;
 }
 
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream) {
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl) {
     const int eb = 2;
     const CUtensorMapDataType dt =
         a.dtype == SFB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -717,13 +720,13 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream) {
     cfg.blockDim = dim3(attn_tc::kThreads, 1, 1);
     cfg.dynamicSmemBytes = attn_tc::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = p.splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1 + pdl_attr(&attr[1], pdl);
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, p);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();

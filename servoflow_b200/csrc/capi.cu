@@ -4,12 +4,12 @@
 #include "common.cuh"
 
 namespace sfb {
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream);
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl);
 int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream);
 int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                       int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
-                      int32_t num_splits, cudaStream_t stream);
+                      int32_t num_splits, cudaStream_t stream, bool pdl);
 int dequantize_int8_launch(const int8_t* in, const void* scale, int32_t scale_dtype,
                            int64_t scale_numel, void* out, int32_t out_dtype, int64_t rows,
                            int64_t cols, cudaStream_t stream);
@@ -71,7 +71,7 @@ int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
     if (!sfb::is_sm100(dev)) return SFB_ERR_UNSUPPORTED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool tc = (a->dtype == SFB_F16 || a->dtype == SFB_BF16) && a->head_dim == 64;
-    return tc ? sfb::attention_tc_launch(*a, s) : sfb::attention_simt_launch(*a, s);
+    return tc ? sfb::attention_tc_launch(*a, s, false) : sfb::attention_simt_launch(*a, s);
 }
 
 int sfb_attention_bhsd(const void* q, const void* k, const void* v, void* out, int32_t batch,
@@ -104,7 +104,7 @@ int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w
                      int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
                      int32_t num_splits, void* stream) {
     return sfb::w8a16_gemm_launch(x, ldx, w, w_scale, bias, residual, ldr, y, ldy, y_dtype, M, N, K,
-                                  act, num_splits, static_cast<cudaStream_t>(stream));
+                                  act, num_splits, static_cast<cudaStream_t>(stream), false);
 }
 
 }  // extern "C"

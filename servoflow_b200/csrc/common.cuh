@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -97,6 +98,76 @@ inline char* last_error_buf() {
 inline void record_cuda_error(cudaError_t e, const char* where) {
     snprintf(last_error_buf(), 256, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
     (void)cudaGetLastError();   // reported here; do not leak into the next launch check
+}
+
+// Every kernel of the library prefers the maximal shared-memory carveout, so
+// that alternating between the big tcgen05 kernels (~225 KB of shared memory)
+// and the small row kernels never forces an L1/shared reconfiguration of the
+// SMs between launches. Applied once per kernel and device.
+template <typename K>
+inline void prefer_max_shared(K kernel) {
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!done[dev & 63]) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             static_cast<int>(cudaSharedmemCarveoutMaxShared));
+        (void)cudaGetLastError();
+        done[dev & 63] = true;
+    }
+}
+
+// ── programmatic dependent launch (model path only) ───────────────────────
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel of the stream is still running. It must execute
+// pdl_wait() before it reads or writes any memory that earlier kernels write
+// or read (it returns once they have completed and their writes are
+// visible); everything before that touches only its own shared memory,
+// TMEM and constant weights. pdl_trigger() lets the next kernel be scheduled;
+// kernels that allocate TMEM call it only after their allocation, so a later
+// kernel never holds TMEM an earlier one waits for. Both are no-ops in a
+// kernel launched without the attribute. The C-ABI entry points launch
+// without it; SFB_PDL=0 turns it off for the model as well.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("SFB_PDL");
+        return !(e != nullptr && e[0] == '0');
+    }();
+    return on;
+}
+
+// Fills the launch attribute for programmatic stream serialization; returns
+// the number of attributes written (0 or 1).
+inline int pdl_attr(cudaLaunchAttribute* at, bool pdl) {
+    if (!pdl || !pdl_enabled()) return 0;
+    at->id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at->val.programmaticStreamSerializationAllowed = 1;
+    return 1;
+}
+
+// Launches a plain (non-cluster) kernel, optionally with programmatic
+// dependent launch; returns an SFB status.
+template <typename... KArgs, typename... Args>
+inline int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                         bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    cfg.numAttrs = pdl_attr(at, pdl);
+    cfg.attrs = at;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        record_cuda_error(e, "kernel launch");
+        return SFB_ERR_LAUNCH;
+    }
+    return SFB_OK;
 }
 
 inline int launch_status() {

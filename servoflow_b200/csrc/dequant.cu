@@ -66,6 +66,7 @@ int launch(const int8_t* in, const void* scale, bool per_channel, void* out, int
     int64_t blocks = (work + threads - 1) / threads;
     blocks = std::min<int64_t>(blocks, static_cast<int64_t>(std::max(dev.num_sms, 1)) * 16);
     blocks = std::max<int64_t>(blocks, 1);
+    prefer_max_shared(dequant_int8_kernel<S, O>);
     dequant_int8_kernel<S, O><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
         in, static_cast<const S*>(scale), per_channel, static_cast<O*>(out), rows, cols, vec_ok);
     return launch_status();

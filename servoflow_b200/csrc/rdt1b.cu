@@ -35,11 +35,11 @@
 
 namespace sfb {
 
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream);
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl);
 int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                       int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
-                      int32_t num_splits, cudaStream_t stream);
+                      int32_t num_splits, cudaStream_t stream, bool pdl);
 int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_t ldo, int rows,
                     int D, float eps, cudaStream_t s);
 int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w, float eps,
@@ -163,7 +163,7 @@ static int new_linear(Model& m, Linear& L, int N, int K, const std::string& name
 static int linear(const Linear& L, const __nv_bfloat16* x, int64_t ldx, int M, void* y, int64_t ldy,
                   int act, const __nv_bfloat16* residual, int64_t ldr, cudaStream_t s, bool y_f32 = false) {
     return w8a16_gemm_launch(x, ldx, L.w, L.s, L.b, residual, ldr, y, ldy, y_f32 ? SFB_F32 : SFB_BF16, M,
-                             L.N, L.K, act, 0, s);
+                             L.N, L.K, act, 0, s, true);
 }
 
 // DPM-Solver++ (2M), x0 prediction, squaredcos_cap_v2 schedule over 1000
@@ -299,7 +299,7 @@ static int attention(const Model& m, const __nv_bfloat16* q, int64_t q_sb, int64
     a.out_stride[2] = m.c.hidden;
     a.batch = B; a.heads = m.c.heads; a.heads_kv = m.c.heads; a.seq_q = Lq; a.seq_k = Lk;
     a.head_dim = 64; a.dtype = SFB_BF16; a.kv_len = kv_len;
-    return attention_tc_launch(a, s);
+    return attention_tc_launch(a, s, true);
 }
 
 // Condition encoding for one control tick (rdt1b.cpp:167-239 + the per-block
@@ -320,14 +320,13 @@ static int encode(Model& m, int B, const void* lang, const int32_t* lang_len, co
     // adaptors: Linear → GELU → Linear (test_rdt1b_alignment.py:99-104)
     SFB_TRY(linear(m.lang0, static_cast<const __nv_bfloat16*>(lang), c.lang_dim, Ml, m.enc_h, D, 1, nullptr, 0, s));
     SFB_TRY(linear(m.lang2, m.enc_h, D, Ml, m.lang_c, D, 0, nullptr, 0, s));
-    rdt::add_rows_kernel<<<grid_for(static_cast<int64_t>(Ml) * D / 8, 256), 256, 0, s>>>(
-        m.lang_c, m.lang_pos, B, c.max_lang_len, D);
-    SFB_TRY(launch_status());
+    prefer_max_shared(rdt::add_rows_kernel);
+    SFB_TRY(launch_kernel(rdt::add_rows_kernel, grid_for(static_cast<int64_t>(Ml) * D / 8, 256), 256, 0, s, true,
+        m.lang_c, m.lang_pos, B, c.max_lang_len, D));
     SFB_TRY(linear(m.img0, static_cast<const __nv_bfloat16*>(img), c.img_dim, Mi, m.enc_h, D, 1, nullptr, 0, s));
     SFB_TRY(linear(m.img2, m.enc_h, D, Mi, m.img_c, D, 0, nullptr, 0, s));
-    rdt::add_rows_kernel<<<grid_for(static_cast<int64_t>(Mi) * D / 8, 256), 256, 0, s>>>(
-        m.img_c, m.img_pos, B, c.img_len, D);
-    SFB_TRY(launch_status());
+    SFB_TRY(launch_kernel(rdt::add_rows_kernel, grid_for(static_cast<int64_t>(Mi) * D / 8, 256), 256, 0, s, true,
+        m.img_c, m.img_pos, B, c.img_len, D));
     // per-block cross-attention K/V cache: kv = cond·Wkvᵀ + b, K k-normed in place
     for (int l = 0; l < c.num_layers; ++l) {
         const bool lang_blk = (l % 2 == 0);
@@ -346,23 +345,24 @@ static int forward(Model& m, int B, float t, cudaStream_t s) {
     const int M = B * S, Ma = B * (T + 1);
     const float eps = 1e-6f;
     // state adaptor on [state, x_t] with an all-ones action mask
-    rdt::adaptor_input_kernel<<<grid_for(static_cast<int64_t>(Ma) * 2 * A, 256), 256, 0, s>>>(
-        m.state, m.xact, m.ain, B, T, A);
-    SFB_TRY(launch_status());
+    prefer_max_shared(rdt::adaptor_input_kernel);
+    prefer_max_shared(rdt::sincos_kernel);
+    prefer_max_shared(rdt::assemble_x_kernel);
+    prefer_max_shared(rdt::dpm_update_kernel);
+    SFB_TRY(launch_kernel(rdt::adaptor_input_kernel, grid_for(static_cast<int64_t>(Ma) * 2 * A, 256), 256, 0, s, true,
+        m.state, m.xact, m.ain, B, T, A));
     SFB_TRY(linear(m.st0, m.ain, 2 * c.state_dim, Ma, m.ah1, D, 1, nullptr, 0, s));
     SFB_TRY(linear(m.st2, m.ah1, D, Ma, m.ah2, D, 1, nullptr, 0, s));
     SFB_TRY(linear(m.st4, m.ah2, D, Ma, m.seq, D, 0, nullptr, 0, s));
     // timestep and control-frequency embeddings: sincos → Linear → SiLU → Linear
-    rdt::sincos_kernel<<<1, 128, 0, s>>>(t, 256, m.tsc);
-    rdt::sincos_kernel<<<1, 128, 0, s>>>(static_cast<float>(c.ctrl_freq), 256, m.fsc);
-    SFB_TRY(launch_status());
+    SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, t, 256, m.tsc));
+    SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, static_cast<float>(c.ctrl_freq), 256, m.fsc));
     SFB_TRY(linear(m.t0, m.tsc, 256, 1, m.th, D, 2, nullptr, 0, s));
     SFB_TRY(linear(m.t2, m.th, D, 1, m.temb, D, 0, nullptr, 0, s));
     SFB_TRY(linear(m.f0, m.fsc, 256, 1, m.fh, D, 2, nullptr, 0, s));
     SFB_TRY(linear(m.f2, m.fh, D, 1, m.femb, D, 0, nullptr, 0, s));
-    rdt::assemble_x_kernel<<<grid_for(static_cast<int64_t>(M) * D / 8, 256), 256, 0, s>>>(
-        m.temb, m.femb, m.seq, m.x_pos, m.x, B, S, D);
-    SFB_TRY(launch_status());
+    SFB_TRY(launch_kernel(rdt::assemble_x_kernel, grid_for(static_cast<int64_t>(M) * D / 8, 256), 256, 0, s, true,
+        m.temb, m.femb, m.seq, m.x_pos, m.x, B, S, D));
 
     for (int l = 0; l < c.num_layers; ++l) {
         const Block& bl = m.blocks[l];
@@ -403,9 +403,8 @@ static int sample_loop(Model& m, int B, cudaStream_t s) {
     const int64_t n = static_cast<int64_t>(B) * c.horizon * c.action_dim;
     for (int i = 0; i < c.num_steps; ++i) {
         SFB_TRY(forward(m, B, m.tsteps[i], s));
-        rdt::dpm_update_kernel<<<grid_for(n, 256), 256, 0, s>>>(m.xact, m.yfin, m.x0prev, m.ca[i], m.cb[i],
-                                                                m.cc[i], B, c.horizon, c.action_dim, m.S());
-        SFB_TRY(launch_status());
+        SFB_TRY(launch_kernel(rdt::dpm_update_kernel, grid_for(n, 256), 256, 0, s, true,
+            m.xact, m.yfin, m.x0prev, m.ca[i], m.cb[i], m.cc[i], B, c.horizon, c.action_dim, m.S()));
     }
     return SFB_OK;
 }

@@ -29,6 +29,8 @@ __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162f
 __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                 int64_t ldo, int rows, int D, float eps) {
+    pdl_trigger();
+    pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     const __nv_bfloat16* xr = x + warp * ldx;
@@ -67,6 +69,8 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
 // x[row·ld + h·64 ...] are RMS-normalised with weight w[64]. 8 threads per head.
 __global__ void head_rms_norm_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int rows, int heads,
                                      const __nv_bfloat16* __restrict__ w, float eps) {
+    pdl_trigger();
+    pdl_wait();
     const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 3, sub = threadIdx.x & 7;
     if (g >= rows * heads) return;
     const int row = g / heads, h = g - row * heads;
@@ -97,6 +101,8 @@ __global__ void head_rms_norm_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, 
 
 // out[0:half] = cos(t·f_i), out[half:2half] = sin(t·f_i), f_i = exp(−ln(10000)·i/half)
 __global__ void sincos_kernel(float t, int dim, __nv_bfloat16* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int half = dim / 2;
     if (i >= half) return;
@@ -112,6 +118,8 @@ __global__ void assemble_x_kernel(const __nv_bfloat16* __restrict__ t_emb,
                                   const __nv_bfloat16* __restrict__ seq,   // [B·(S−2), D]
                                   const __nv_bfloat16* __restrict__ pos,   // [S, D]
                                   __nv_bfloat16* __restrict__ x, int B, int S, int D) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t n8 = static_cast<int64_t>(B) * S * D / 8;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -142,6 +150,8 @@ __global__ void adaptor_input_kernel(const __nv_bfloat16* __restrict__ state,  /
                                      const float* __restrict__ x_t,            // [B, T, A]
                                      __nv_bfloat16* __restrict__ out,          // [B·(T+1), 2A]
                                      int B, int T, int A) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t n = static_cast<int64_t>(B) * (T + 1) * 2 * A;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -159,6 +169,8 @@ __global__ void adaptor_input_kernel(const __nv_bfloat16* __restrict__ state,  /
 // cond[b, s, :] += pos[s, :]   for s < S (rows of cond per session: S, row stride D)
 __global__ void add_rows_kernel(__nv_bfloat16* __restrict__ cond, const __nv_bfloat16* __restrict__ pos,
                                 int B, int S, int D) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t n8 = static_cast<int64_t>(B) * S * D / 8;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -184,6 +196,8 @@ __global__ void add_rows_kernel(__nv_bfloat16* __restrict__ cond, const __nv_bfl
 __global__ void dpm_update_kernel(float* __restrict__ x, const float* __restrict__ y_final,
                                   float* __restrict__ x0_prev, float a, float bcoef, float c,
                                   int B, int T, int A, int S) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t n = static_cast<int64_t>(B) * T * A;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -208,10 +222,11 @@ int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_
     if (D % 256 != 0 || (ldx % 8) || (ldo % 8)) return SFB_ERR_SHAPE;
     if (rows <= 0) return SFB_OK;
     const int warps_per_block = 4;
-    rdt::rms_norm_kernel<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
-        static_cast<__nv_bfloat16*>(out), ldo, rows, D, eps);
-    return launch_status();
+    prefer_max_shared(rdt::rms_norm_kernel);
+    return launch_kernel(rdt::rms_norm_kernel, (rows + warps_per_block - 1) / warps_per_block,
+                         32 * warps_per_block, 0, s, true, static_cast<const __nv_bfloat16*>(x), ldx,
+                         static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), ldo, rows,
+                         D, eps);
 }
 
 int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w, float eps,
@@ -219,9 +234,10 @@ int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w
     if (ld % 8) return SFB_ERR_SHAPE;
     if (rows <= 0 || heads <= 0) return SFB_OK;
     const int64_t threads = static_cast<int64_t>(rows) * heads * 8;
-    rdt::head_rms_norm_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
-        static_cast<__nv_bfloat16*>(x), ld, rows, heads, static_cast<const __nv_bfloat16*>(w), eps);
-    return launch_status();
+    prefer_max_shared(rdt::head_rms_norm_kernel);
+    return launch_kernel(rdt::head_rms_norm_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, s,
+                         true, static_cast<__nv_bfloat16*>(x), ld, rows, heads,
+                         static_cast<const __nv_bfloat16*>(w), eps);
 }
 
 }  // namespace sfb

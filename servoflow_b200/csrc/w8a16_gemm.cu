@@ -19,12 +19,13 @@
 //   * Swap-AB: weight rows are the MMA M dimension (128 per CTA) and tokens
 //     the MMA N dimension (N = tokens rounded up to 32, at most 256 per CTA),
 //     so a 67-token denoising step does not pad an M=128 tile.
-//   * Warp roles per CTA (6 warps): warp 0 issues TMA (int8 weight tile
+//   * Warp roles per CTA (10 warps): warp 0 issues TMA (int8 weight tile
 //     [128 × 64] without swizzle, bf16 activation tile [N × 64] with 128-byte
 //     swizzle), warp 1 issues tcgen05.mma from one elected lane of a
-//     converged warp, warps 2..5 convert each int8 tile into a bf16 SW128
+//     converged warp, warps 2..9 convert each int8 tile into a bf16 SW128
 //     operand tile (exactly: bytes re-biased into fp32 with a byte permute,
-//     one FADD, top 16 bits kept) and afterwards run the epilogue.
+//     one FADD, top 16 bits kept) and afterwards run the epilogue, staged
+//     through shared memory so that Y is written in 16-byte vectors.
 //   * Split-K over a thread-block cluster when M is small: each CTA
 //     accumulates a K range in TMEM, pushes its fp32 partial into the owning
 //     CTA's shared memory (owner = a block of token columns) with remote
@@ -48,30 +49,55 @@ struct W8Params {
     int32_t        splits;        // cluster size along grid.x
     int32_t        act;           // 0 none, 1 GELU (tanh), 2 SiLU
     int32_t        y_f32;         // 1: fp32 output
+    int32_t        stages;        // pipeline depth, kRingBytes / stage bytes, at most kMaxStages
+#ifdef SFB_TRACE
+    unsigned long long* trace;
+#endif
 };
 
 namespace w8 {
 
-constexpr int kThreads  = 6 * 32;
-constexpr int kStages   = 4;
+#ifdef SFB_TRACE
+#define W8_T(slot, i) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) \
+        p.trace[(slot) * 64 + (i)] = clock64(); } while (0)
+#else
+#define W8_T(slot, i) do { } while (0)
+#endif
+
+constexpr int kThreads  = 10 * 32;        // TMA, MMA, 8 converter/epilogue warps
+constexpr int kConvWarps = 8;
+constexpr int kStageStride = 36;           // floats per row of an epilogue staging block
+constexpr int kMaxStages = 8;
 constexpr int kWBytes   = 128 * 64;            // int8 weight tile
 constexpr int kWbBytes  = 128 * 128;           // bf16 weight tile (SW128)
-constexpr int kXBytes   = 256 * 128;           // bf16 activation tile, up to 256 rows
-constexpr int kOffX     = 0;
-constexpr int kOffWb    = kOffX + kStages * kXBytes;
-constexpr int kOffW     = kOffWb + kStages * kWbBytes;
-constexpr int kOffBar   = kOffW + kStages * kWBytes;
-constexpr int kOffTmem  = kOffBar + 8 * 24;
+// One ring area split into `stages` X tiles (bn · 128 B, bn <= 256), then as
+// many bf16 and int8 weight tiles; the depth follows the token tile: 4 stages
+// at bn = 256, 6 at 96, 8 at 64 and below.
+constexpr int kRingBytes = 224 * 1024;
+constexpr int kOffBar   = kRingBytes;
+constexpr int kOffTmem  = kOffBar + 8 * (4 * kMaxStages + 2);
 constexpr int kSmemUsed = kOffTmem + 16;
 constexpr int kSmemBytes = kSmemUsed + 1024;
-// Split-K merge buffer (only when splits > 1, bn <= 128) reuses the X ring:
-// [C sources][128 rows][ceil(bn/C) + 1 columns] fp32 <= 128 · 160 · 4 bytes.
+// Split-K merge (only when splits > 1, bn <= 128) reuses the ring, idle by
+// then: a staging area [C owners][bn tokens][128/C + pad] at offset 0 and a
+// receive area [C sources][bn][128/C] at kOffRecv, each fp32 and at most
+// 64 KB + 512 B.
+constexpr int kOffRecv  = 65536 + 1024;
+static_assert(kOffRecv + 65536 <= kRingBytes, "merge areas fit the ring");
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
-__host__ __device__ constexpr int bar_full(int s)  { return s; }                 // W int8 + X landed
-__host__ __device__ constexpr int bar_conv(int s)  { return kStages + s; }       // W bf16 ready
-__host__ __device__ constexpr int bar_empty(int s) { return 2 * kStages + s; }   // stage consumed by MMA
-constexpr int kBarAcc = 3 * kStages;                                             // accumulator done
+__host__ __device__ constexpr int stage_bytes(int bn) { return kWBytes + kWbBytes + bn * 128; }
+__host__ __device__ constexpr int num_stages(int bn) {
+    return kRingBytes / stage_bytes(bn) < kMaxStages ? kRingBytes / stage_bytes(bn) : kMaxStages;
+}
+static_assert(num_stages(256) >= 4, "four stages at the widest token tile");
+
+__host__ __device__ constexpr int bar_full_w(int s) { return s; }                    // W int8 landed
+__host__ __device__ constexpr int bar_full_x(int s) { return kMaxStages + s; }       // X landed
+__host__ __device__ constexpr int bar_conv(int s)  { return 2 * kMaxStages + s; }    // W bf16 ready
+__host__ __device__ constexpr int bar_empty(int s) { return 3 * kMaxStages + s; }    // stage consumed by MMA
+constexpr int kBarAcc = 4 * kMaxStages;                                              // accumulator done
+constexpr int kBarMerge = 4 * kMaxStages + 1;                                        // split-K partials landed
 
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;   // sqrt(2/pi), GELU tanh form
@@ -88,9 +114,11 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffTmem);
-    auto sX  = [&](int s) { return smem + kOffX + s * kXBytes; };
-    auto sWb = [&](int s) { return smem + kOffWb + s * kWbBytes; };
-    auto sW  = [&](int s) { return smem + kOffW + s * kWBytes; };
+    const int nst = p.stages;
+    const int xtile = p.bn * 128;
+    auto sX  = [&](int s) { return smem + s * xtile; };
+    auto sWb = [&](int s) { return smem + nst * xtile + s * kWbBytes; };
+    auto sW  = [&](int s) { return smem + nst * (xtile + kWbBytes) + s * kWBytes; };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x;
@@ -101,13 +129,21 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     const int c_begin = split * cbase + min(split, crem);
     const int nch = cbase + (split < crem ? 1 : 0);
 
+#ifdef SFB_TRACE
+    const uint64_t cta_t0 = ptx::global_timer_ns();
+#endif
     if (tid == 32) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&bars[bar_full(s)], 1);
-            mbar_init(&bars[bar_conv(s)], 4);
+        for (int s = 0; s < nst; ++s) {
+            mbar_init(&bars[bar_full_w(s)], 1);
+            mbar_init(&bars[bar_full_x(s)], 1);
+            mbar_init(&bars[bar_conv(s)], kConvWarps / 2);
             mbar_init(&bars[bar_empty(s)], 1);
         }
         mbar_init(&bars[kBarAcc], 1);
+        mbar_init(&bars[kBarMerge], 1);
+        if (p.splits > 1)   // partials of the other C-1 CTAs land here by bulk copy
+            mbar_arrive_expect_tx(&bars[kBarMerge],
+                                  static_cast<uint32_t>((p.splits - 1) * p.bn * (128 / p.splits) * 4));
         fence_mbarrier_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
@@ -120,6 +156,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem = *tmem_holder;
+    pdl_trigger();                                     // TMEM is held: the next kernel may start
 
     bool ok = true;
     auto wait = [&](int bar, uint32_t parity) {
@@ -129,14 +166,29 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 
     if (warp == 0) {
         // ── TMA producer ────────────────────────────────────────────────────
+        // The int8 weights of the first stages are constant and are fetched
+        // before waiting for the previous kernel; activations after.
+        const int pre = min(nch, nst);
+        if (elect_one()) {
+            for (int c = 0; c < pre; ++c) {
+                mbar_arrive_expect_tx(&bars[bar_full_w(c)], kWBytes);
+                tma_load_2d(sW(c), &tmW, &bars[bar_full_w(c)], (c_begin + c) * 64, n0);
+            }
+        }
+        __syncwarp();
+        pdl_wait();
         for (int c = 0; c < nch; ++c) {
-            const int s = c % kStages;
-            if (c >= kStages) wait(bar_empty(s), ((c / kStages) - 1) & 1);
+            const int s = c % nst;
+            if (c >= nst) wait(bar_empty(s), ((c / nst) - 1) & 1);
             if (elect_one()) {
-                mbar_arrive_expect_tx(&bars[bar_full(s)], kWBytes + xbytes);
                 const int k0 = (c_begin + c) * 64;
-                tma_load_2d(sW(s), &tmW, &bars[bar_full(s)], k0, n0);
-                tma_load_2d(sX(s), &tmX, &bars[bar_full(s)], k0, m0);
+                if (c >= nst) {
+                    mbar_arrive_expect_tx(&bars[bar_full_w(s)], kWBytes);
+                    tma_load_2d(sW(s), &tmW, &bars[bar_full_w(s)], k0, n0);
+                }
+                mbar_arrive_expect_tx(&bars[bar_full_x(s)], xbytes);
+                tma_load_2d(sX(s), &tmX, &bars[bar_full_x(s)], k0, m0);
+                W8_T(0, c);
             }
             __syncwarp();
         }
@@ -144,11 +196,13 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         // ── MMA issuer ──────────────────────────────────────────────────────
         const uint32_t idesc = idesc_f16(128, static_cast<uint32_t>(p.bn), 1, 0, 0);
         for (int c = 0; c < nch; ++c) {
-            const int s = c % kStages;
-            wait(bar_conv(s), (c / kStages) & 1);
+            const int s = c % nst;
+            wait(bar_conv(s), (c / nst) & 1);
+            wait(bar_full_x(s), (c / nst) & 1);
             tc_fence_after_sync();
             const uint32_t aw = smem_u32(sWb(s)), ax = smem_u32(sX(s));
             if (elect_one()) {
+                W8_T(3, c);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     mma_f16_ss(tmem, smem_desc_sw128(aw + kk * 32, 16, 1024),
@@ -161,21 +215,30 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         }
     } else {
         // ── converters: int8 [128 × 64] → bf16 SW128 [128 × 64] ──────────────
-        const int ct = tid - 64;                       // 0..127
-        for (int c = 0; c < nch; ++c) {
-            const int s = c % kStages;
-            wait(bar_full(s), (c / kStages) & 1);
+        // Two groups of four warps take alternate chunks, so the conversion
+        // latency of one chunk overlaps the next.
+        const int grp = (warp - 2) >> 2;
+        const int ct = tid - 64 - grp * 128;           // 0..127
+        for (int c = grp; c < nch; c += 2) {
+            const int s = c % nst;
+            wait(bar_full_w(s), (c / nst) & 1);
+            if (ct == 0) W8_T(1, c);
             const uint8_t* src = sW(s);
             uint8_t* dst = sWb(s);
-#pragma unroll 2
-            for (int it = 0; it < 8; ++it) {
+            uint2 raw[8];
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {           // all loads first: independent
                 const int unit = it * 128 + ct;        // (row, 8-element chunk)
+                raw[it] = *reinterpret_cast<const uint2*>(src + (unit >> 3) * 64 + (unit & 7) * 8);
+            }
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int unit = it * 128 + ct;
                 const int r = unit >> 3, ch = unit & 7;
-                const uint2 raw = *reinterpret_cast<const uint2*>(src + r * 64 + ch * 8);
                 uint32_t o[4];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint32_t x = (h ? raw.y : raw.x) ^ 0x80808080u;   // q + 128, unsigned
+                    const uint32_t x = (h ? raw[it].y : raw[it].x) ^ 0x80808080u;   // q + 128, unsigned
                     // 0x4B0000bb = 2^23 + bb as fp32; minus (2^23 + 128) gives q exactly
                     const float f0 = __uint_as_float(ptx::prmt(x, 0x4B000000u, 0x7440u)) - 8388736.f;
                     const float f1 = __uint_as_float(ptx::prmt(x, 0x4B000000u, 0x7441u)) - 8388736.f;
@@ -190,12 +253,14 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[bar_conv(s)]);
+            if (ct == 0) W8_T(2, c);
         }
     }
 
-    // ── epilogue (warps 2..5: TMEM lane window = warp % 4) ───────────────────
+    // ── epilogue (warps 2..9: TMEM lane window = warp % 4, column half hh) ───
     const bool epi = warp >= 2;
     const int win = warp & 3;
+    const int hh = (warp - 2) >> 2;                    // 0: warps 2..5, 1: warps 6..9
     const int nrow = n0 + win * 32 + lane;             // output channel of this thread
     const uint32_t lane_off = static_cast<uint32_t>(win * 32) << 16;
     float sc = 0.f, bi = 0.f;
@@ -203,77 +268,191 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         sc = p.w_scale[nrow];
         if (p.bias) bi = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[nrow]);
     }
-    auto finish = [&](float acc, int m) {
-        float y = fmaf(acc, sc, bi);
-        if (p.act == 1) y = gelu_tanh(y);
-        else if (p.act == 2) y = y / (1.f + expf(-y));          // SiLU
-        if (p.residual)
-            y += __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[m * p.ldr + nrow]);
-        if (p.y_f32) static_cast<float*>(p.y)[m * p.ldy + nrow] = y;
-        else static_cast<__nv_bfloat16*>(p.y)[m * p.ldy + nrow] = __float2bfloat16_rn(y);
+    auto act = [&](float y) {
+        if (p.act == 1) return gelu_tanh(y);
+        if (p.act == 2) return y / (1.f + expf(-y));    // SiLU
+        return y;
     };
+    if (tid == 64) W8_T(4, 0);
+    pdl_wait();                                        // before the residual read and the output write
     if (epi && nch > 0) {
         wait(kBarAcc, 0);
         tc_fence_after_sync();
     }
+    if (tid == 64) W8_T(4, 1);
     const int mvalid = min(p.bn, p.M - m0);
     if (p.splits == 1) {
+        // Each warp takes 32-column blocks c0 = 32·hh, 32·hh + 64, ...: TMEM →
+        // act(acc·s + b) staged as fp32 [32 tokens][32 channels] in shared memory
+        // (the bf16 weight ring, idle now), then written as 16-byte vectors of 8
+        // channels per token row, with the residual added in the same pass.
         if (epi) {
+            float* stg = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * kStageStride;
+            const int nb = n0 + win * 32;               // first channel of this warp
 #pragma unroll 1
-            for (int c0 = 0; c0 < p.bn; c0 += 32) {
+            for (int c0 = 32 * hh; c0 < p.bn; c0 += 64) {
                 float v[32];
                 if (nch > 0) { tmem_ld32(tmem + lane_off + c0, v); tmem_ld_wait(); }
                 else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = 0.f;
                 }
-                if (nrow < p.N && ok) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (c0 + i < mvalid) finish(v[i], m0 + c0 + i);
+                for (int i = 0; i < 32; ++i) stg[i * kStageStride + lane] = act(fmaf(v[i], sc, bi));
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int r = j * 8 + (lane >> 2), seg = (lane & 3) * 8;   // token row, 8 channels
+                    const int m = m0 + c0 + r, n = nb + seg;
+                    if (c0 + r < mvalid && n < p.N && ok) {
+                        const float4 a = *reinterpret_cast<const float4*>(stg + r * kStageStride + seg);
+                        const float4 b = *reinterpret_cast<const float4*>(stg + r * kStageStride + seg + 4);
+                        float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                        if (p.residual) {
+                            const uint4 rr = *reinterpret_cast<const uint4*>(
+                                static_cast<const __nv_bfloat16*>(p.residual) + m * p.ldr + n);
+                            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const float2 f = __bfloat1622float2(r2[k]);
+                                y[2 * k] += f.x; y[2 * k + 1] += f.y;
+                            }
+                        }
+                        if (p.y_f32) {
+                            float* dst = static_cast<float*>(p.y) + m * p.ldy + n;
+                            *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+                            *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+                        } else {
+                            uint4 o;
+                            __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(y[2 * k], y[2 * k + 1]);
+                            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n) = o;
+                        }
+                    }
                 }
+                __syncwarp();
             }
         }
     } else {
-        // Split-K merge: CTA r owns token columns [bn·r/C, bn·(r+1)/C). Every CTA
-        // pushes its partial rows of each owner's columns into that owner's
-        // buffer [C sources][128 rows][cols]; one cluster barrier publishes them.
-        const int C = p.splits;
-        const int cs = (p.bn + C - 1) / C + 1;         // merge slice stride (floats)
-        float* buf = reinterpret_cast<float*>(smem + kOffX);
-        cluster_sync();   // every CTA's MMAs are done and its X ring is free
+        // Split-K merge. CTA r owns channel rows [r·R, (r+1)·R) of the tile,
+        // R = 128 / C. Every CTA stages its fp32 partial as C contiguous
+        // owner slices [bn tokens][R channels] (padded by R floats between
+        // slices so the per-lane stores hit distinct banks), then one thread
+        // bulk-copies slice r into CTA r's receive area, signalling r's merge
+        // barrier. The owner sums its own slice and the C - 1 received ones,
+        // applies scale/bias/activation/residual and writes 16-byte vectors of
+        // 8 channels per token.
+        const int C = p.splits, R = 128 / C;
+        const int slice = p.bn * R;
+        float* stg = reinterpret_cast<float*>(smem);
+        float* rcv = reinterpret_cast<float*>(smem + kOffRecv);
+        const int segs = R / 8;                         // 8-channel segments per owned row
+        const int nunits = mvalid * segs;
+        constexpr int kMaxIt = 4;                       // (128 tokens · 8 segs) / 256 threads
+        uint4 rres[kMaxIt];
         if (epi) {
+            // Staged values carry the channel scale and (from CTA 0 only) the bias,
+            // so the owner's pass is a plain sum.
+            const float bsplit = split == 0 ? bi : 0.f;
             const int row = win * 32 + lane;
-#pragma unroll 1
-            for (int c0 = 0; c0 < p.bn; c0 += 32) {
-                float v[32];
-                if (nch > 0) { tmem_ld32(tmem + lane_off + c0, v); tmem_ld_wait(); }
-                else {
+            const int owner = row / R, slot = row - owner * R;
+            float* d = stg + owner * (slice + R) + slot;
+            float v[2][32];
+            const int c0a = 32 * hh, c0b = 32 * hh + 64;
+            if (nch > 0) {
+                if (c0a < p.bn) tmem_ld32(tmem + lane_off + c0a, v[0]);
+                if (c0b < p.bn) tmem_ld32(tmem + lane_off + c0b, v[1]);
+                tmem_ld_wait();
+            } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = 0.f;
-                }
+                for (int i = 0; i < 32; ++i) { v[0][i] = 0.f; v[1][i] = 0.f; }
+            }
+            if (c0a < p.bn) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = c0 + i;
-                    const int owner = (col * C) / p.bn;
-                    const int lo = (p.bn * owner + C - 1) / C;
-                    const uint32_t a = smem_u32(buf + (split * 128 + row) * cs + (col - lo));
-                    dsmem_st_f32(dsmem_map(a, owner), v[i]);
-                }
+                for (int i = 0; i < 32; ++i) d[(c0a + i) * R] = fmaf(v[0][i], sc, bsplit);
+            }
+            if (c0b < p.bn) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) d[(c0b + i) * R] = fmaf(v[1][i], sc, bsplit);
+            }
+            fence_proxy_async_smem();
+            // the residual rows this thread adds in the owner pass, loaded early
+            const int nb = n0 + split * R;
+#pragma unroll
+            for (int it = 0; it < kMaxIt; ++it) {
+                const int u = tid - 64 + it * kConvWarps * 32;
+                const int mm = u / segs, n = nb + (u - mm * segs) * 8;
+                rres[it] = make_uint4(0u, 0u, 0u, 0u);
+                if (p.residual && u < nunits && n < p.N)
+                    rres[it] = *reinterpret_cast<const uint4*>(
+                        static_cast<const __nv_bfloat16*>(p.residual) + (m0 + mm) * p.ldr + n);
             }
         }
+        if (tid == 64) W8_T(4, 3);
+        // every CTA's MMAs are done (its X ring is free) and its slices are staged
         cluster_sync();
-        if (epi && nrow < p.N && ok) {
-            const int row = win * 32 + lane;
-            const int lo = (p.bn * split + C - 1) / C, hi = (p.bn * (split + 1) + C - 1) / C;
-            for (int col = lo; col < hi && col < mvalid; ++col) {
-                float acc = 0.f;
-                for (int r = 0; r < C; ++r) acc += buf[(r * 128 + row) * cs + (col - lo)];
-                finish(acc, m0 + col);
+        if (tid == 64) {
+            for (int j = 1; j < C; ++j) {
+                const int o = (split + j) % C;
+                bulk_copy_to_cluster(dsmem_map(smem_u32(rcv + split * slice), o),
+                                     smem_u32(stg + o * (slice + R)), static_cast<uint32_t>(slice * 4),
+                                     dsmem_map(smem_u32(&bars[kBarMerge]), o));
             }
         }
+        if (tid == 64) W8_T(4, 4);
+        if (epi) wait(kBarMerge, 0);
+        if (tid == 64) W8_T(4, 5);
+        if (epi) {
+            const int nb = n0 + split * R;                 // first channel owned here
+#pragma unroll
+            for (int it = 0; it < kMaxIt; ++it) {
+                const int u = tid - 64 + it * kConvWarps * 32;
+                const int mm = u / segs, seg = (u - mm * segs) * 8;
+                const int n = nb + seg, m = m0 + mm;
+                if (u >= nunits || n >= p.N || !ok) continue;
+                float y[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) y[k] = 0.f;
+#pragma unroll 1
+                for (int r = 0; r < C; ++r) {
+                    const float* src = (r == split ? stg + r * (slice + R) : rcv + r * slice) + mm * R + seg;
+                    const float4 a4 = *reinterpret_cast<const float4*>(src);
+                    const float4 b4 = *reinterpret_cast<const float4*>(src + 4);
+                    y[0] += a4.x; y[1] += a4.y; y[2] += a4.z; y[3] += a4.w;
+                    y[4] += b4.x; y[5] += b4.y; y[6] += b4.z; y[7] += b4.w;
+                }
+                const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rres[it]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = __bfloat1622float2(r2[k]);   // zero without a residual
+                    y[2 * k] = act(y[2 * k]) + f.x;
+                    y[2 * k + 1] = act(y[2 * k + 1]) + f.y;
+                }
+                if (p.y_f32) {
+                    float* dst = static_cast<float*>(p.y) + m * p.ldy + n;
+                    *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+                    *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+                } else {
+                    uint4 o;
+                    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(y[2 * k], y[2 * k + 1]);
+                    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.y) + m * p.ldy + n) = o;
+                }
+            }
+        }
+        if (tid == 64) W8_T(4, 6);
+        cluster_sync();   // no CTA leaves while a peer's copy may still touch its shared memory
     }
 
+    if (tid == 64) W8_T(4, 2);
+#ifdef SFB_TRACE
+    if (p.trace && tid == 64) {
+        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        if (cta < 1024) { p.trace[1024 + 2 * cta] = cta_t0; p.trace[1025 + 2 * cta] = ptx::global_timer_ns(); }
+    }
+#endif
     if (!ok) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
     tc_fence_before_sync();
     __syncthreads();
@@ -285,10 +464,51 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 
 }  // namespace w8
 
+#ifdef SFB_TRACE
+static unsigned long long* g_w8_trace = nullptr;
+extern "C" void sfb_debug_set_w8_trace(void* p) { g_w8_trace = static_cast<unsigned long long*>(p); }
+#endif
+
+// Clusters of `size` CTAs of the GEMM kernel that can be resident at once
+// (cached per device and size; 0 when the query fails).
+static int w8_max_clusters(const DeviceInfo& dev, int size) {
+    static int cache[64][17] = {};
+    int& slot = cache[dev.ordinal & 63][size & 15];
+    if (slot != 0) return slot;
+    if (cudaFuncSetAttribute(w8::w8a16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             w8::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(w8::w8a16_gemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                             1) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size, 1, 1);
+    cfg.blockDim = dim3(w8::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = w8::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, w8::w8a16_gemm_kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+#ifdef SFB_TRACE
+    fprintf(stderr, "w8a16: cluster size %d -> %d resident clusters\n", size, n);
+#endif
+    slot = n;
+    return n;
+}
+
 int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                       int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
-                      int32_t num_splits, cudaStream_t stream) {
+                      int32_t num_splits, cudaStream_t stream, bool pdl) {
     if (x == nullptr || w == nullptr || w_scale == nullptr || y == nullptr) return SFB_ERR_INVALID;
     if (M < 0 || N <= 0 || K <= 0) return SFB_ERR_SHAPE;
     if (M == 0) return SFB_OK;
@@ -312,16 +532,21 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     const int ntile = (N + 127) / 128, mtile = (M + p.bn - 1) / p.bn;
     int splits = num_splits;
     if (splits <= 0) {
+        // Split K across a cluster only when the tiles alone leave most SMs
+        // idle, and only as far as every cluster still fits in one wave: at one
+        // CTA per SM the GPCs hold fewer 8-CTA clusters than SMs / 8, and a
+        // cluster left over for a second wave doubles the kernel's time.
         splits = 1;
-        if (p.bn <= 128) {
-            const int units = ntile * mtile;
-            splits = std::max(1, dev.num_sms / std::max(units, 1));
-            splits = std::min(splits, 8);
-            splits = std::min(splits, std::max(1, p.kchunks / 2));
-        }
+        const int units = ntile * mtile;
+        while (p.bn <= 128 && splits < 8 && units * splits * 2 <= dev.num_sms &&
+               p.kchunks / (splits * 2) >= 2 && units <= w8_max_clusters(dev, splits * 2))
+            splits *= 2;
     }
+    if (splits != 1 && splits != 2 && splits != 4 && splits != 8 && splits != 16) return SFB_ERR_INVALID;
     if (splits > 1 && p.bn > 128) return SFB_ERR_INVALID;
-    p.splits = std::min(std::min(splits, 16), p.kchunks);
+    if (splits > p.kchunks) return SFB_ERR_INVALID;
+    p.splits = splits;
+    p.stages = w8::num_stages(p.bn);
 
     CUtensorMap mx, mw;
     {
@@ -355,18 +580,21 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
         }
         attr_done[dev.ordinal & 63] = true;
     }
+#ifdef SFB_TRACE
+    p.trace = g_w8_trace;
+#endif
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.splits, ntile, mtile);
     cfg.blockDim = dim3(w8::kThreads, 1, 1);
     cfg.dynamicSmemBytes = w8::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = p.splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1 + pdl_attr(&attr[1], pdl);
     cudaError_t e = cudaLaunchKernelEx(&cfg, w8::w8a16_gemm_kernel, mx, mw, p);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
