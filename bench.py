@@ -1,22 +1,40 @@
 #!/usr/bin/env python3
-"""Benchmark of the B200 attention path (one JSON line on rank 0).
+"""Benchmark of the B200 RDT-1B denoising path (one JSON line on rank 0).
 
-Workload (default): RDT-1B image cross-attention, batch 1,
-32 heads, head_dim 64, Lq = 67, Lk = 4374, bf16; the K/V cache is resident
-(projected once per control tick, reused by every denoising step), so one
-step = one attention call on fresh Q. L2 is flushed (256 MiB write) before
-every timed call, so every call streams K/V from HBM.
+Headline workload (config 4): the full RDT-1B DiT denoise at batch 1 — 28
+blocks, hidden 2048, 32 heads, int8 per-channel weights, self-attention over
+the 67 action-chunk tokens, cross-attention alternating between the masked
+language condition (1024 keys) and the image condition (4374 keys), 5
+DPM-Solver++ steps replayed as one CUDA graph. One step = one full 5-step
+denoise of one session's action chunk (64 x 128 fp32 noise) with the control
+tick's condition K/V cache resident. The working set streamed per denoise
+(7.9 GB of int8 weights and cached K/V) is ~60x the 126 MB L2, so no flush
+is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (torchrun, one process per GPU): independent robot sessions are
-sharded one per GPU with no collective on the hot path (weak scaling); the
-only collectives are the barrier and the max-over-ranks of the timings.
---impl reference times the reference's attention semantics on the host CPU:
-the reference has no CPU attention (only a CUDA backend registers,
-src/backend/cuda/cuda_backend.cu:613-622), so this runs the C/OpenMP
-restatement in oracle/ on all host threads, a bounded sample of heads per
-step scaled to a full call.
+Reported beside the headline:
+  e2e       the same denoise through the public call with host buffers:
+            pinned host noise in, pinned host actions out, copies inside the
+            timed region (RDT1B.sample_host -> sfb_rdt1b_sample).
+  roofline  the dominant kernel, the int8-weight linear layer
+            (w8a16_gemm_kernel): all 168 block projections of one network
+            evaluation launched back to back through sfb_w8a16_linear with
+            the model's weights (M = 67 tokens), algorithmic bytes
+            (int8 W + scale + bias + X + Y [+ residual]) / event-timed
+            duration per launch, against the measured HBM copy bandwidth.
+  attention the image cross-attention kernel alone (config 2: Lq 67, Lk 4374,
+            L2 flushed before every call), GB/s and TFLOP/s vs the peaks.
+  cpu_baseline / --impl reference
+            the CPU oracle of the same network (oracle/rdt1b_ref.py, torch
+            fp32 on all host threads) on a bounded sample of blocks per step,
+            scaled to 28 blocks x 5 steps. The reference has no CPU path
+            (only its CUDA backend registers), so this restatement stands in.
+
+Multi-GPU (torchrun, one process per GPU): each rank serves its own session
+(own weights, K/V cache and graph) with no collective on the hot path (weak
+scaling); the only collectives are barriers and the max over ranks of the
+timings.
 """
 from __future__ import annotations
 
@@ -24,9 +42,9 @@ import argparse
 import json
 import os
 import re
-import subprocess
 import sys
 import time
+from types import SimpleNamespace
 
 import numpy as np
 
@@ -34,7 +52,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "RDT-1B denoise p50 latency (ms, B=1); attention TFLOP/s & GB/s vs B200 peak"
-B, H, D, LQ, LK = 1, 32, 64, 67, 4374
+# RDT-1B shapes (reference config.h)
+HIDDEN, HEADS, LAYERS, HORIZON, ACTION, LANG_LEN, IMG_LEN, STEPS = 2048, 32, 28, 64, 128, 1024, 4374, 5
+TOKENS = HORIZON + 3
 FLUSH_BYTES = 256 << 20
 
 
@@ -47,17 +67,9 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def alg_bytes(elem=2):
-    return elem * (2 * B * H * LQ * D + 2 * B * H * LK * D)
-
-
-def alg_flops():
-    return 4.0 * B * H * LQ * LK * D
-
-
-def profiled_traffic():
-    """DRAM bytes per launch from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "attn_fwd_tc_image_xattn.md")
+def profiled_traffic(name):
+    """DRAM bytes per launch from a committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(p):
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
@@ -122,85 +134,191 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(sm), "source": "NVML, 5 ms polling"}
 
 
-def dist_setup(args):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return world, rank, local
 
 
+# ── CPU oracle timing (cpu_baseline and --impl reference) ─────────────────────
+class CpuDenoiseSample:
+    """The CPU oracle network (oracle/rdt1b_ref.py) on the host cores: one
+    language block and one image block with their cross K/V cached (as the
+    per-tick cache does), timed one block at a time; a block's time scaled by
+    28 blocks x 5 steps gives the denoise estimate. The adaptors, embedders
+    and final layer (<1% of the FLOPs) are left out of the sample."""
+
+    def __init__(self, threads, seed=0):
+        import torch
+        from oracle.rdt1b_ref import RefRDT, random_block_weights
+        self.torch = torch
+        torch.set_num_threads(threads)
+        self.threads = torch.get_num_threads()
+        cfg = SimpleNamespace(hidden=HIDDEN, heads=HEADS, num_layers=2)
+        self.ref = RefRDT(random_block_weights(cfg, [0, 1], seed=seed), cfg)
+        g = torch.Generator().manual_seed(seed)
+        lang_c = torch.randn(1, LANG_LEN, HIDDEN, generator=g)
+        img_c = torch.randn(1, IMG_LEN, HIDDEN, generator=g)
+        self.lang_len = torch.randint(8, LANG_LEN + 1, (1,), generator=g)
+        with torch.inference_mode():
+            self.kv = [self.ref.cross_kv(l, lang_c, img_c) for l in (0, 1)]
+        self.x = torch.randn(1, TOKENS, HIDDEN, generator=g)
+
+    def block(self, l):
+        """Seconds for block l (0: language, 1: image) on the current x."""
+        with self.torch.inference_mode():
+            t0 = time.perf_counter()
+            self.x = self.ref.block(self.x, l, *self.kv[l], self.lang_len)
+            return time.perf_counter() - t0
+
+    def denoise_ms(self, t_lang, t_img):
+        return (t_lang + t_img) / 2 * LAYERS * STEPS * 1e3
+
+    def baseline(self, budget_s):
+        """cpu_baseline object: pairs of blocks until the time budget is spent."""
+        self.block(0); self.block(1)                  # warm-up
+        est = []
+        t_end = time.perf_counter() + budget_s
+        while time.perf_counter() < t_end or not est:
+            est.append(self.denoise_ms(self.block(0), self.block(1)))
+        return {"value": float(np.median(est)), "unit": "ms", "cores": self.threads, "kind": "port",
+                "sample": f"{len(est)} (language block + image block) pairs, fp32 torch on "
+                          f"{self.threads} threads, cross K/V cached; block time scaled x{LAYERS * STEPS} "
+                          "to 28 blocks x 5 steps (oracle/rdt1b_ref.py)"}
+
+
 def run_reference(args, world, rank):
-    """Oracle port of the reference attention on the host CPU (rank 0 only)."""
+    """The CPU oracle of the denoise on the host CPU (rank 0 only)."""
     if rank != 0:
         return
-    from oracle import oracle
-    oracle.build()
-    cores = oracle.num_threads()
-    rng = np.random.default_rng(0)
-    q = rng.standard_normal((B, H, LQ, D), dtype=np.float32)
-    k = rng.standard_normal((B, H, LK, D), dtype=np.float32)
-    v = rng.standard_normal((B, H, LK, D), dtype=np.float32)
-    # size the per-step sample so the whole run stays within ~2 minutes
-    t0 = time.perf_counter()
-    oracle.attention(q[:, :1], k[:, :1], v[:, :1])
-    per_head = time.perf_counter() - t0
-    budget = 100.0 / max(1, args.steps + args.warmup)
-    heads = int(max(1, min(H, budget // max(per_head, 1e-6))))
-    for _ in range(args.warmup):
-        oracle.attention(q[:, :heads], k[:, :heads], v[:, :heads])
+    threads = os.cpu_count() or 1
+    s = CpuDenoiseSample(threads)
+    budget = 150.0                                  # seconds for warm-up + timed steps
+    t_start = time.perf_counter()
+    for i in range(args.warmup):
+        s.block(i % 2)
     ts = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        oracle.attention(q[:, :heads], k[:, :heads], v[:, :heads])
-        ts.append((time.perf_counter() - t0) * H / heads * 1e3)
+    for i in range(args.steps):                     # one block per step, alternating kinds
+        if ts and time.perf_counter() - t_start > budget:
+            break
+        ts.append(s.block(i % 2) * LAYERS * STEPS * 1e3)
     p50 = float(np.median(ts))
     line = {
         "impl": "reference", "metric": METRIC, "value": p50, "unit": "ms", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.mean(ts)),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "image cross-attention (config 2): B=1 H=32 D=64 Lq=67 Lk=4374",
-                   "parallelism": "host CPU, OpenMP"},
-        "cpu_baseline": {"value": p50, "unit": "ms", "cores": cores, "kind": "port",
-                         "sample": f"{heads} of {H} heads per step, time scaled x{H / heads:.1f} "
-                                   "to a full call; fp64 online softmax (oracle/sfo_oracle.c)"},
+        "steps": args.steps, "steps_measured": len(ts), "warmup": args.warmup,
+        "ms_per_step": float(np.mean(ts)), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded",
+        "config": {"workload": "config 4: RDT-1B 5-step denoise, B=1 (28 blocks, hidden 2048, 32 heads, "
+                               "lang 1024 masked / image 4374 cross-attention, cross K/V cached)",
+                   "parallelism": f"host CPU, torch fp32, {s.threads} threads"},
+        "cpu_baseline": {"value": p50, "unit": "ms", "cores": s.threads, "kind": "port",
+                         "sample": f"one RDT block per step (language and image alternating), "
+                                   f"time scaled x{LAYERS * STEPS} to 28 blocks x 5 steps; "
+                                   "oracle/rdt1b_ref.py (the reference has no CPU backend)"},
         "e2e": {"value": p50, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_sample():
-    from oracle import oracle
-    oracle.build()
-    rng = np.random.default_rng(0)
-    heads = 4
-    q = rng.standard_normal((B, heads, LQ, D), dtype=np.float32)
-    k = rng.standard_normal((B, heads, LK, D), dtype=np.float32)
-    v = rng.standard_normal((B, heads, LK, D), dtype=np.float32)
+# ── GPU arm ───────────────────────────────────────────────────────────────────
+def block_gemms(model):
+    """(name, N, K, act, has_residual) of the 168 block projections of one
+    network evaluation, in launch order."""
+    out = []
+    for l in range(LAYERS):
+        p = f"blocks.{l}."
+        out += [(p + "attn.qkv", 3 * HIDDEN, HIDDEN, 0, False), (p + "attn.proj", HIDDEN, HIDDEN, 0, True),
+                (p + "cross_attn.q", HIDDEN, HIDDEN, 0, False),
+                (p + "cross_attn.proj", HIDDEN, HIDDEN, 0, True),
+                (p + "ffn.fc1", HIDDEN, HIDDEN, 1, False), (p + "ffn.fc2", HIDDEN, HIDDEN, 0, True)]
+    return out
+
+
+def gemm_roofline(model, dev, reps):
+    """Event-timed duration per launch of the block projections, launched back
+    to back through the C ABI with the model's weights (HBM-resident, 0.96 GB
+    per pass, so every launch streams its weights from HBM)."""
+    import torch
+    from servoflow_b200 import _capi
+    capi = _capi.lib()
+    M = TOKENS
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(M, HIDDEN, generator=g) * 0.5).bfloat16().to(dev)
+    res = (torch.randn(M, HIDDEN, generator=g) * 0.5).bfloat16().to(dev)
+    y = torch.empty(M, 3 * HIDDEN, dtype=torch.bfloat16, device=dev)
+    sh = torch.cuda.current_stream().cuda_stream
+    calls, nbytes = [], 0
+    for name, N, K, act, has_res in block_gemms(model):
+        wq = model.param_ptr(name + ".weight_q")[0]
+        ws = model.param_ptr(name + ".weight_scale")[0]
+        wb = model.param_ptr(name + ".bias")[0]
+        calls.append((wq, ws, wb, res.data_ptr() if has_res else None, N, K, act))
+        nbytes += N * K + N * 4 + N * 2 + M * K * 2 + M * N * 2 + (M * N * 2 if has_res else 0)
+
+    def run():
+        for wq, ws, wb, rp, N, K, act in calls:
+            rc = capi.sfb_w8a16_linear(x.data_ptr(), K, wq, ws, wb, rp, HIDDEN if rp else 0,
+                                       y.data_ptr(), N, 2, M, N, K, act, 0, sh)
+            if rc:
+                raise _capi.SfbError(rc, "w8a16_linear")
+
+    run()
+    torch.cuda.synchronize()
     ts = []
-    t_end = time.perf_counter() + 10.0
-    while time.perf_counter() < t_end or len(ts) < 3:
-        t0 = time.perf_counter()
-        oracle.attention(q, k, v)
-        ts.append((time.perf_counter() - t0) * H / heads * 1e3)
-        if len(ts) >= 50:
-            break
-    return {"value": float(np.median(ts)), "unit": "ms", "cores": oracle.num_threads(),
-            "kind": "port",
-            "sample": f"{len(ts)} calls on {heads} of {H} heads, time scaled x{H // heads} to a "
-                      "full config-2 call; fp64 online softmax, OpenMP (oracle/sfo_oracle.c)"}
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(); run(); e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e-3)
+    per_launch = float(np.median(ts)) / len(calls)
+    return nbytes / len(calls), per_launch, len(calls) * (reps + 1)
+
+
+def attention_roofline(be, dev, reps):
+    """Image cross-attention (config 2) alone: L2 flushed before every call."""
+    import ctypes
+    import torch
+    from servoflow_b200 import _capi
+    from servoflow_b200.backend import attention_args
+    capi = _capi.lib()
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn(1, HEADS, TOKENS, 64, generator=g).bfloat16().to(dev)
+    k = torch.randn(1, HEADS, IMG_LEN, 64, generator=g).bfloat16().to(dev)
+    v = torch.randn(1, HEADS, IMG_LEN, 64, generator=g).bfloat16().to(dev)
+    out = torch.empty_like(q)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    cargs = attention_args(q, k, v, out)
+    pargs = ctypes.byref(cargs)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    for _ in range(5):
+        _capi.check(capi.sfb_attention_fwd(pargs, sh), "attention")
+    torch.cuda.synchronize()
+    st = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    en = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    for i in range(reps):
+        flush.zero_()
+        st[i].record(stream)
+        _capi.check(capi.sfb_attention_fwd(pargs, sh), "attention")
+        en[i].record(stream)
+    torch.cuda.synchronize()
+    ms = np.array([a.elapsed_time(b) for a, b in zip(st, en)])
+    nbytes = 2 * (2 * HEADS * TOKENS * 64 + 2 * HEADS * IMG_LEN * 64)
+    flops = 4.0 * HEADS * TOKENS * IMG_LEN * 64
+    return nbytes, flops, float(np.median(ms)), float(np.mean(ms)), reps + 5
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    world, rank, local = dist_setup(args)
+    world, rank, local = dist_setup()
 
     if args.impl == "reference":
         run_reference(args, world, rank)
@@ -217,33 +335,29 @@ def main():
 
     from servoflow_b200 import build
     build.build_library()
-    import ctypes
-    from servoflow_b200 import _capi
-    from servoflow_b200.backend import B200Backend, attention_args
+    from servoflow_b200.backend import B200Backend
+    from servoflow_b200.rdt1b import RDT1B, default_config
     be = B200Backend(dev.index)
-    capi = _capi.lib()
 
-    # one robot session per GPU (sessions are independent: seed by rank)
-    g = torch.Generator().manual_seed(1000 + rank)
-    q = torch.randn(B, H, LQ, D, generator=g).bfloat16().to(dev)
-    k = torch.randn(B, H, LK, D, generator=g).bfloat16().to(dev)
-    v = torch.randn(B, H, LK, D, generator=g).bfloat16().to(dev)
-    out = torch.empty_like(q)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    # one robot session per GPU: its own weights, condition and noise (seeded by rank)
+    model = RDT1B(default_config(max_sessions=1), seed=1000 + rank)
+    g = torch.Generator().manual_seed(2000 + rank)
+    lang = torch.randn(1, LANG_LEN, 4096, generator=g).bfloat16().to(dev)
+    lang_len = torch.randint(8, LANG_LEN + 1, (1,), generator=g, dtype=torch.int32).to(dev)
+    img = torch.randn(1, IMG_LEN, 1152, generator=g).bfloat16().to(dev)
+    state = torch.randn(1, 128, generator=g).bfloat16().to(dev)
+    noise_h = torch.randn(1, HORIZON, ACTION, generator=g).pin_memory()
+    act_h = torch.empty_like(noise_h).pin_memory()
+    noise = noise_h.to(dev)
+    actions = torch.empty_like(noise)
     stream = torch.cuda.current_stream()
-    sh = stream.cuda_stream
-    cargs = attention_args(q, k, v, out)         # sfb_attn_args, built once
-    pargs = ctypes.byref(cargs)
 
-    def attn():
-        rc = capi.sfb_attention_fwd(pargs, sh)
-        if rc:
-            raise _capi.SfbError(rc, "attention")
-
-    for _ in range(args.warmup):
-        attn()
+    model.encode(lang, lang_len, img, state)
+    for _ in range(args.warmup):                       # the first call captures the graph
+        model.sample(noise, actions)
     torch.cuda.synchronize()
     assert be.device_error() == 0
+    kernels_per_step = model.graph_kernels(1)
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -254,79 +368,103 @@ def main():
         torch.cuda.synchronize()
         t_wall = time.perf_counter()
         for i in range(args.steps):
-            flush.zero_()
             starts[i].record(stream)
-            attn()
+            model.sample(noise, actions)
             ends[i].record(stream)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         t_wall = time.perf_counter() - t_wall
 
-        # end to end through the public API: pinned host Q in, host O out
-        q_host = q.cpu().pin_memory()
-        o_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        q_dev = torch.empty_like(q)
-        args_e2e = attention_args(q_dev, k, v, out)
-        pe = ctypes.byref(args_e2e)
-        e_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        e_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        for i in range(args.warmup):
-            q_dev.copy_(q_host, non_blocking=True)
-            _capi.check(capi.sfb_attention_fwd(pe, sh), "attention")
-            o_host.copy_(out, non_blocking=True)
+        # end to end through the public call: pinned host noise in, host actions out
+        for _ in range(3):
+            model.sample_host(noise_h, act_h)
         torch.cuda.synchronize()
+        e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         for i in range(args.steps):
-            flush.zero_()
-            e_start[i].record(stream)
-            q_dev.copy_(q_host, non_blocking=True)
-            _capi.check(capi.sfb_attention_fwd(pe, sh), "attention")
-            o_host.copy_(out, non_blocking=True)
-            e_end[i].record(stream)
+            e_st[i].record(stream)
+            model.sample_host(noise_h, act_h)
+            e_en[i].record(stream)
         torch.cuda.synchronize()
+
+        # a full control tick: condition encode (adaptors + 28 cross K/V projections) + denoise
+        n_tick = min(args.steps, 20)
+        t_st = [torch.cuda.Event(enable_timing=True) for _ in range(n_tick)]
+        t_en = [torch.cuda.Event(enable_timing=True) for _ in range(n_tick)]
+        for i in range(n_tick):
+            t_st[i].record(stream)
+            model.encode(lang, lang_len, img, state)
+            model.sample(noise, actions)
+            t_en[i].record(stream)
+        torch.cuda.synchronize()
+    assert be.device_error() == 0
+    assert torch.isfinite(act_h).all()
+
+    gemm_bytes, gemm_s, gemm_launches = gemm_roofline(model, dev, reps=5)
+    at_bytes, at_flops, at_p50, at_mean, at_launches = attention_roofline(be, dev, reps=200)
     assert be.device_error() == 0
 
     ms = np.array([s.elapsed_time(e) for s, e in zip(starts, ends)])
-    e2e_ms = np.array([s.elapsed_time(e) for s, e in zip(e_start, e_end)])
-    stats = torch.tensor([np.median(ms), np.mean(ms), np.percentile(ms, 99), np.median(e2e_ms)],
+    e2e_ms = np.array([s.elapsed_time(e) for s, e in zip(e_st, e_en)])
+    tick_ms = np.array([s.elapsed_time(e) for s, e in zip(t_st, t_en)])
+    stats = torch.tensor([np.median(ms), np.mean(ms), np.percentile(ms, 99), np.median(e2e_ms),
+                          np.median(tick_ms), gemm_s, at_p50, at_mean],
                          dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    p50, mean, p99, e2e_p50 = stats.tolist()
+    p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_p50, at_mean = stats.tolist()
 
     if rank == 0:
         hbm, tflops, kind = peaks()
-        nbytes, flops = alg_bytes(), alg_flops()
-        achieved = nbytes / (mean * 1e-3) / 1e9
-        traffic = profiled_traffic()
+        gemm_gbs = gemm_bytes / gemm_s / 1e9
+        at_gbs = at_bytes / (at_mean * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": p50, "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": mean, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic N(0,1), seeded per session",
-            "config": {"workload": "image cross-attention (config 2): B=1 H=32 D=64 Lq=67 Lk=4374, "
-                                   "K/V cache resident, one call per step",
-                       "global_batch": world, "seq_len": LK,
-                       "l2": "flushed before every timed step (256 MiB write)",
+            "data": "synthetic: random-init int8 weights, N(0,1) conditions and noise, seeded per session",
+            "config": {"workload": "config 4: full RDT-1B denoise, B=1 session per GPU, 28 blocks, hidden "
+                                   "2048, 32 heads, lang 1024 (masked) / image 4374 cross-attention, "
+                                   "5 DPM-Solver++ steps in one CUDA graph, condition K/V cache resident",
+                       "global_batch": world, "seq_len": TOKENS,
+                       "l2": "not flushed: each denoise streams 7.9 GB (int8 weights + cached K/V), "
+                             "~60x the 126 MB L2",
                        "parallelism": f"{world} independent session(s), one per GPU, no collective"},
             "p99_ms": p99,
-            "throughput": {"value": world * 1e3 / mean, "unit": "attention calls/s (all GPUs)"},
-            "tflops": flops / (mean * 1e-3) / 1e12,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": traffic,
+            "throughput": {"value": world * 1e3 / mean, "unit": "denoises/s (all GPUs)",
+                           "actions_per_s": world * 1e3 / mean * HORIZON},
+            "tick_ms": {"value": tick_p50, "unit": "ms",
+                        "what": "encode (adaptors + 28 cross K/V projections) + denoise, device inputs"},
+            "roofline": {"bound": "hbm", "achieved": gemm_gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": gemm_gbs / hbm,
+                         "traffic": profiled_traffic("w8a16_gemm_rdt1b_block.md"),
                          "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                         "alg_bytes_per_launch": nbytes, "kernel": "attn_fwd_tc_kernel<bf16>"},
-            "e2e": {"value": e2e_p50, "unit": "ms", "h2d_bytes_per_step": q.numel() * 2,
-                    "d2h_bytes_per_step": out.numel() * 2,
-                    "path": "B200Backend.attention (C ABI sfb_attention_fwd), pinned host Q -> "
-                            "device, O -> pinned host, K/V cache resident"},
-            "gpu_launches": args.steps * 2 * world,
-            "gpu_launches_note": "attn_fwd_tc_kernel launches: K device-timed + K end-to-end, per GPU",
+                         "kernel": "w8a16_gemm_kernel (int8-weight linear), dominant by time",
+                         "alg_bytes_per_launch": gemm_bytes, "us_per_launch": gemm_s * 1e6,
+                         "how": "168 block projections (M=67) back to back via sfb_w8a16_linear, "
+                                "model weights, CUDA events, max over ranks"},
+            "attention": {"kernel": "attn_fwd_tc_kernel<bf16>, image cross-attention (config 2)",
+                          "p50_us": at_p50 * 1e3, "mean_us": at_mean * 1e3,
+                          "achieved_gbs": at_gbs, "frac_hbm": at_gbs / hbm,
+                          "tflops": at_flops / (at_mean * 1e-3) / 1e12,
+                          "frac_tensor": at_flops / (at_mean * 1e-3) / 1e12 / tflops,
+                          "alg_bytes_per_launch": at_bytes,
+                          "traffic": profiled_traffic("attn_fwd_tc_image_xattn.md"),
+                          "l2": "flushed before every call"},
+            "e2e": {"value": e2e_p50, "unit": "ms", "h2d_bytes_per_step": noise_h.numel() * 4,
+                    "d2h_bytes_per_step": act_h.numel() * 4,
+                    "path": "RDT1B.sample_host -> sfb_rdt1b_sample: pinned host noise -> device, "
+                            "graph replay, actions -> pinned host, all inside the timed region"},
+            "gpu_launches": kernels_per_step * args.steps,
+            "gpu_launches_note": f"{kernels_per_step} kernels per denoise graph x {args.steps} timed steps "
+                                 f"(counted from the captured graph's kernel nodes); the e2e, tick and "
+                                 f"roofline passes add more",
             "clocks": sampler.summary(),
             "wall_s_device_loop": t_wall,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_sample()
+            line["cpu_baseline"] = CpuDenoiseSample(os.cpu_count() or 1).baseline(15.0)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

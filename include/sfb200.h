@@ -209,12 +209,18 @@ int sfb_rdt1b_encode(void* handle, int32_t sessions, const void* lang_tokens, co
 int sfb_rdt1b_forward(void* handle, int32_t sessions, const float* x_t, float t, float* x0_out,
                       void* stream);
 /* Full sampling: noise fp32 [sessions, horizon, action_dim] → actions (same
- * shape) after num_steps DPM-Solver++ steps. With use_graph != 0 the loop is
+ * shape) after num_steps DPM-Solver++ steps. noise and actions may be device
+ * pointers or host pointers (pinned host memory keeps the copies
+ * asynchronous); the call returns once the work is queued on `stream`. With use_graph != 0 the loop is
  * captured into a CUDA graph on the first call for a given session count (that
  * call runs eagerly, then captures; make it before any capture of your own) and
  * replayed afterwards. */
 int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* actions,
                      int32_t use_graph, void* stream);
+/* Kernel launches in the captured sampling graph for `sessions` (known after
+ * the first use_graph call for that session count). Diagnostic; no
+ * counterpart in the reference. */
+int sfb_rdt1b_graph_kernels(void* handle, int32_t sessions, int64_t* kernels);
 /* Device pointer, element count and dtype of a named parameter (names follow
  * the reference checkpoint: "blocks.3.attn.qkv.weight_q", "...weight_scale",
  * "...bias", "x_pos_embed", ...). */

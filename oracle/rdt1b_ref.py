@@ -106,26 +106,41 @@ class RefRDT:
         femb = self.lin(self.lin(sincos(c.ctrl_freq), "freq_embedder.mlp.0", "silu"), "freq_embedder.mlp.2")
         x = torch.cat([temb.expand(B, 1, D), femb.expand(B, 1, D), seq], 1) + w["x_pos_embed"].view(-1, D)
         for l in range(c.num_layers):
-            p = f"blocks.{l}."
-            h = rms_norm(x, w[p + "norm1.weight"])
-            qkv = self.lin(h, p + "attn.qkv").view(B, -1, 3, H, 64)
-            q = rms_norm(qkv[:, :, 0], w[p + "attn.q_norm.weight"]).reshape(B, -1, D)
-            k = rms_norm(qkv[:, :, 1], w[p + "attn.k_norm.weight"]).reshape(B, -1, D)
-            v = qkv[:, :, 2].reshape(B, -1, D)
-            x = x + self.lin(self.attn(q, k, v, H), p + "attn.proj")
-            cond, klen = (lang_c, lang_len) if l % 2 == 0 else (img_c, None)
-            h = rms_norm(x, w[p + "norm2.weight"])
-            q = rms_norm(self.lin(h, p + "cross_attn.q").view(B, -1, H, 64),
-                         w[p + "cross_attn.q_norm.weight"]).reshape(B, -1, D)
-            kv = self.lin(cond, p + "cross_attn.kv").view(B, -1, 2, H, 64)
-            k = rms_norm(kv[:, :, 0], w[p + "cross_attn.k_norm.weight"]).reshape(B, -1, D)
-            v = kv[:, :, 1].reshape(B, -1, D)
-            x = x + self.lin(self.attn(q, k, v, H, klen), p + "cross_attn.proj")
-            h = rms_norm(x, w[p + "norm3.weight"])
-            x = x + self.lin(self.lin(h, p + "ffn.fc1", "gelu"), p + "ffn.fc2")
+            k, v = self.cross_kv(l, lang_c, img_c)
+            x = self.block(x, l, k, v, lang_len)
         h = rms_norm(x, w["final_layer.norm_final.weight"])
         out = self.lin(self.lin(h, "final_layer.ffn_final.fc1", "gelu"), "final_layer.ffn_final.fc2")
         return out[:, -T:]
+
+    def cross_kv(self, l, lang_c, img_c):
+        """Block l's cross-attention K (k-normed) and V over its condition
+        (language for even blocks, image for odd; dit_block.cu:288-308)."""
+        c, w = self.c, self.w
+        p = f"blocks.{l}."
+        cond = lang_c if l % 2 == 0 else img_c
+        B, D = cond.shape[0], c.hidden
+        kv = self.lin(cond, p + "cross_attn.kv").view(B, -1, 2, c.heads, 64)
+        k = rms_norm(kv[:, :, 0], w[p + "cross_attn.k_norm.weight"]).reshape(B, -1, D)
+        return k, kv[:, :, 1].reshape(B, -1, D)
+
+    def block(self, x, l, k, v, lang_len):
+        """RDT block l (dit_block.cu:349-387) on x [B, S, D] with the block's
+        cross-attention K/V; language blocks mask keys at or beyond lang_len."""
+        c, w = self.c, self.w
+        B, D, H = x.shape[0], c.hidden, c.heads
+        p = f"blocks.{l}."
+        h = rms_norm(x, w[p + "norm1.weight"])
+        qkv = self.lin(h, p + "attn.qkv").view(B, -1, 3, H, 64)
+        q = rms_norm(qkv[:, :, 0], w[p + "attn.q_norm.weight"]).reshape(B, -1, D)
+        kk = rms_norm(qkv[:, :, 1], w[p + "attn.k_norm.weight"]).reshape(B, -1, D)
+        vv = qkv[:, :, 2].reshape(B, -1, D)
+        x = x + self.lin(self.attn(q, kk, vv, H), p + "attn.proj")
+        h = rms_norm(x, w[p + "norm2.weight"])
+        q = rms_norm(self.lin(h, p + "cross_attn.q").view(B, -1, H, 64),
+                     w[p + "cross_attn.q_norm.weight"]).reshape(B, -1, D)
+        x = x + self.lin(self.attn(q, k, v, H, lang_len if l % 2 == 0 else None), p + "cross_attn.proj")
+        h = rms_norm(x, w[p + "norm3.weight"])
+        return x + self.lin(self.lin(h, p + "ffn.fc1", "gelu"), p + "ffn.fc2")
 
     def sample(self, lang_c, img_c, lang_len, state, noise):
         ts, a, b, cc = dpm_schedule(self.c.num_steps)
@@ -170,4 +185,27 @@ def load_weights(model, cfg) -> dict:
         lin(p + "ffn.fc1", D, D); lin(p + "ffn.fc2", D, D)
     vec("final_layer.norm_final.weight", (D,))
     lin("final_layer.ffn_final.fc1", D, D); lin("final_layer.ffn_final.fc2", cfg.action_dim, D)
+    return w
+
+
+def random_block_weights(cfg, layers, seed: int = 0, std: float = 0.02) -> dict:
+    """fp32 weights N(0, std) for the listed blocks only (the CPU timing sample;
+    the values do not matter for timing, the shapes are RDT-1B's)."""
+    g = torch.Generator().manual_seed(seed)
+    D = cfg.hidden
+    w = {}
+
+    def lin(name, n, k):
+        w[name + ".weight"] = torch.randn(n, k, generator=g) * std
+        w[name + ".bias"] = torch.randn(n, generator=g) * std
+
+    for l in layers:
+        p = f"blocks.{l}."
+        for n in ("norm1", "norm2", "norm3"):
+            w[p + n + ".weight"] = 1 + torch.randn(D, generator=g) * std
+        lin(p + "attn.qkv", 3 * D, D); lin(p + "attn.proj", D, D)
+        lin(p + "cross_attn.q", D, D); lin(p + "cross_attn.kv", 2 * D, D); lin(p + "cross_attn.proj", D, D)
+        for n in ("attn.q_norm", "attn.k_norm", "cross_attn.q_norm", "cross_attn.k_norm"):
+            w[p + n + ".weight"] = 1 + torch.randn(64, generator=g) * std
+        lin(p + "ffn.fc1", D, D); lin(p + "ffn.fc2", D, D)
     return w

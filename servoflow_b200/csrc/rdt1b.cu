@@ -125,6 +125,7 @@ struct Model {
     // DPM-Solver++ coefficients and timesteps
     std::vector<float> ca, cb, cc, tsteps;
     std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, int64_t> graph_kernels;     // kernel nodes of each captured graph
     // the graph is captured and replayed on the model's own stream (capture is
     // not possible on the legacy default stream a caller may be using)
     cudaStream_t own = nullptr;
@@ -507,7 +508,8 @@ int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* 
         return SFB_ERR_CUDA;
     }
     const size_t bytes = static_cast<size_t>(sessions) * m->c.horizon * m->c.action_dim * 4;
-    if (cudaMemcpyAsync(m->xact, noise, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+    // noise and actions may live on the device or in (preferably pinned) host memory
+    if (cudaMemcpyAsync(m->xact, noise, bytes, cudaMemcpyDefault, s) != cudaSuccess ||
         cudaMemsetAsync(m->x0prev, 0, bytes, s) != cudaSuccess) {
         record_cuda_error(cudaGetLastError(), "rdt1b sample input");
         return SFB_ERR_CUDA;
@@ -527,6 +529,17 @@ int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* 
             e = cudaStreamEndCapture(s, &g);
             if (rc != SFB_OK) { if (g) cudaGraphDestroy(g); return rc; }
             if (e != cudaSuccess) { record_cuda_error(e, "end capture"); return SFB_ERR_CUDA; }
+            size_t nn = 0;
+            int64_t nk = 0;
+            if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn > 0) {
+                std::vector<cudaGraphNode_t> nodes(nn);
+                if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+                    for (size_t i = 0; i < nn; ++i) {
+                        cudaGraphNodeType ty;
+                        if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++nk;
+                    }
+            }
+            m->graph_kernels[sessions] = nk;
             cudaGraphExec_t ge = nullptr;
             e = cudaGraphInstantiate(&ge, g, 0);
             cudaGraphDestroy(g);
@@ -537,7 +550,7 @@ int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* 
             if (e != cudaSuccess) { record_cuda_error(e, "graph launch"); return SFB_ERR_CUDA; }
         }
     }
-    if (cudaMemcpyAsync(actions, m->xact, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+    if (cudaMemcpyAsync(actions, m->xact, bytes, cudaMemcpyDefault, s) != cudaSuccess ||
         cudaEventRecord(m->ev_out, s) != cudaSuccess || cudaStreamWaitEvent(caller, m->ev_out, 0) != cudaSuccess) {
         record_cuda_error(cudaGetLastError(), "rdt1b sample output");
         return SFB_ERR_CUDA;
@@ -554,6 +567,15 @@ int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, 
     *ptr = it->second.first;
     *numel = it->second.second.first;
     *dtype = it->second.second.second;
+    return SFB_OK;
+}
+
+int sfb_rdt1b_graph_kernels(void* handle, int32_t sessions, int64_t* kernels) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || kernels == nullptr) return SFB_ERR_INVALID;
+    auto it = m->graph_kernels.find(sessions);
+    if (it == m->graph_kernels.end()) return SFB_ERR_INVALID;
+    *kernels = it->second;
     return SFB_OK;
 }
 

@@ -35,8 +35,9 @@ def _declare(lib):
                                     c.POINTER(c.c_int64), c.POINTER(c.c_int32)]
     lib.sfb_rdt1b_schedule.argtypes = [c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p,
                                        c.c_int32]
+    lib.sfb_rdt1b_graph_kernels.argtypes = [c.c_void_p, c.c_int32, c.POINTER(c.c_int64)]
     for f in ("default_config", "create", "destroy", "encode", "forward", "sample", "param",
-              "schedule"):
+              "schedule", "graph_kernels"):
         getattr(lib, "sfb_rdt1b_" + f).restype = c.c_int
     lib._rdt_declared = True
 
@@ -92,6 +93,26 @@ class RDT1B:
     def sample(self, noise, out, use_graph=True, stream=None):
         _capi.check(self.lib.sfb_rdt1b_sample(self.h, noise.shape[0], noise.data_ptr(), out.data_ptr(),
                                               1 if use_graph else 0, _sh(stream)), "rdt1b sample")
+
+    def sample_host(self, noise, out, stream=None):
+        """sample() from host noise into host actions (pinned CPU tensors keep
+        the copies asynchronous); the copies run inside the same call."""
+        assert not noise.is_cuda and not out.is_cuda
+        _capi.check(self.lib.sfb_rdt1b_sample(self.h, noise.shape[0], noise.data_ptr(), out.data_ptr(),
+                                              1, _sh(stream)), "rdt1b sample")
+
+    def graph_kernels(self, sessions: int = 1) -> int:
+        """Kernel launches in the captured sampling graph for `sessions`."""
+        n = ctypes.c_int64()
+        _capi.check(self.lib.sfb_rdt1b_graph_kernels(self.h, sessions, ctypes.byref(n)), "graph_kernels")
+        return n.value
+
+    def param_ptr(self, name: str):
+        """(device pointer, element count, SFB dtype code) of a parameter, no copy."""
+        ptr, n, dt = ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_int32()
+        _capi.check(self.lib.sfb_rdt1b_param(self.h, name.encode(), ctypes.byref(ptr), ctypes.byref(n),
+                                             ctypes.byref(dt)), f"param {name}")
+        return ptr.value, n.value, dt.value
 
     def param(self, name: str) -> torch.Tensor:
         """A copy (on the GPU) of a model parameter."""
