@@ -69,6 +69,7 @@ struct AttnTcParams {
     int64_t  mask_sb;
 #ifdef SFB_TRACE
     unsigned long long* trace;
+    int dbg_skip;                    // timing experiments only: return at once
 #endif
 };
 
@@ -195,6 +196,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int groups = (rows + 31) >> 5;            // active 32-row windows per group
 
 
+#ifdef SFB_TRACE
+    if (p.dbg_skip) { pdl_trigger(); pdl_wait(); return; }
+#endif
     SFB_T(0);
 #ifdef SFB_TRACE
     const uint64_t cta_t0 = ptx::global_timer_ns();
@@ -646,6 +650,8 @@ static int make_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 #ifdef SFB_TRACE
 static unsigned long long* g_trace_ptr = nullptr;
 extern "C" void sfb_debug_set_trace(void* p) { g_trace_ptr = static_cast<unsigned long long*>(p); }
+static int g_attn_skip = 0;
+extern "C" void sfb_debug_set_attn_skip(int s) { g_attn_skip = s; }
 #endif
 
 // Cluster size along Lk: as many splits as keep every CTA co-resident in one
@@ -692,6 +698,7 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl) {
     p.mask_sb = a.key_mask_stride_b;
 #ifdef SFB_TRACE
     p.trace = g_trace_ptr;
+    p.dbg_skip = g_attn_skip;
 #endif
     const int units = a.batch * a.heads * p.qtiles;
     const int ntiles_max = (a.seq_k + 127) / 128;

@@ -117,6 +117,9 @@ inline void prefer_max_shared(K kernel) {
     }
 }
 
+// Returns the status of `expr` from the enclosing function unless it is SFB_OK.
+#define SFB_TRY(expr) do { int _rc = (expr); if (_rc != SFB_OK) return _rc; } while (0)
+
 // ── programmatic dependent launch (model path only) ───────────────────────
 // A kernel launched with programmatic stream serialization may start while
 // the previous kernel of the stream is still running. It must execute

@@ -134,7 +134,6 @@ struct Model {
     int S() const { return c.horizon + 3; }
 };
 
-#define SFB_TRY(expr) do { int _rc = (expr); if (_rc != SFB_OK) return _rc; } while (0)
 
 static int dalloc(Model& m, void** p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes);

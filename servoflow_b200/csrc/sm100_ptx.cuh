@@ -90,6 +90,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// Same contract as mbar_wait, polling with the non-blocking probe: the
+// waiting warp resumes within a few cycles of the phase completing (a
+// blocking try_wait can sleep for hundreds of cycles past it).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
+                                               uint64_t timeout_ns = 1000000000ull) {
+    if (mbar_test(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_test(bar, parity)) return true;
+        if ((it & 255u) == 255u && global_timer_ns() - t0 > timeout_ns) return false;
+    }
+}
+
 // ── TMA (tensor tile loads, no multicast) ───────────────────────────────────
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -112,6 +125,15 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         " [%0], [%1, {%3, %4}], [%2];"
         ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
           "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// Untiled bulk copy global → this CTA's shared memory (both addresses 16-byte
+// aligned, bytes a multiple of 16), completion as transaction bytes.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
 

@@ -35,6 +35,10 @@
 #include "common.cuh"
 #include "sm100_ptx.cuh"
 
+#include <mutex>
+#include <utility>
+#include <vector>
+
 namespace sfb {
 
 struct W8Params {
@@ -47,7 +51,6 @@ struct W8Params {
     int32_t        bn;            // MMA N (tokens per CTA), multiple of 32, <= 256
     int32_t        kchunks;       // K / 64
     int32_t        splits;        // cluster size along grid.x
-    int32_t        act;           // 0 none, 1 GELU (tanh), 2 SiLU
     int32_t        y_f32;         // 1: fp32 output
     int32_t        stages;        // pipeline depth, kRingBytes / stage bytes, at most kMaxStages
 #ifdef SFB_TRACE
@@ -104,6 +107,9 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.f + tanhf(k0 * fmaf(k1 * x * x, x, x)));
 }
 
+// kAct: 0 none, 1 GELU (tanh), 2 SiLU; kSplit: K split across a cluster.
+// Each instantiation carries only its own epilogue path.
+template <int kAct, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmW,
@@ -141,7 +147,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         }
         mbar_init(&bars[kBarAcc], 1);
         mbar_init(&bars[kBarMerge], 1);
-        if (p.splits > 1)   // partials of the other C-1 CTAs land here by bulk copy
+        if (kSplit)         // partials of the other C-1 CTAs land here by bulk copy
             mbar_arrive_expect_tx(&bars[kBarMerge],
                                   static_cast<uint32_t>((p.splits - 1) * p.bn * (128 / p.splits) * 4));
         fence_mbarrier_init();
@@ -268,10 +274,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         sc = p.w_scale[nrow];
         if (p.bias) bi = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[nrow]);
     }
-    auto act = [&](float y) {
-        if (p.act == 1) return gelu_tanh(y);
-        if (p.act == 2) return y / (1.f + expf(-y));    // SiLU
-        return y;
+    auto act = [](float y) {
+        if constexpr (kAct == 1) return gelu_tanh(y);
+        else if constexpr (kAct == 2) return y / (1.f + expf(-y));    // SiLU
+        else return y;
     };
     if (tid == 64) W8_T(4, 0);
     pdl_wait();                                        // before the residual read and the output write
@@ -281,7 +287,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     }
     if (tid == 64) W8_T(4, 1);
     const int mvalid = min(p.bn, p.M - m0);
-    if (p.splits == 1) {
+    if constexpr (!kSplit) {
         // Each warp takes 32-column blocks c0 = 32·hh, 32·hh + 64, ...: TMEM →
         // act(acc·s + b) staged as fp32 [32 tokens][32 channels] in shared memory
         // (the bf16 weight ring, idle now), then written as 16-byte vectors of 8
@@ -462,6 +468,16 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     }
 }
 
+using KernFn = void (*)(CUtensorMap, CUtensorMap, W8Params);
+
+inline KernFn pick(int act, bool split) {
+    static const KernFn t[3][2] = {
+        {w8a16_gemm_kernel<0, false>, w8a16_gemm_kernel<0, true>},
+        {w8a16_gemm_kernel<1, false>, w8a16_gemm_kernel<1, true>},
+        {w8a16_gemm_kernel<2, false>, w8a16_gemm_kernel<2, true>}};
+    return t[act][split ? 1 : 0];
+}
+
 }  // namespace w8
 
 #ifdef SFB_TRACE
@@ -475,9 +491,10 @@ static int w8_max_clusters(const DeviceInfo& dev, int size) {
     static int cache[64][17] = {};
     int& slot = cache[dev.ordinal & 63][size & 15];
     if (slot != 0) return slot;
-    if (cudaFuncSetAttribute(w8::w8a16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const w8::KernFn kern = w8::pick(0, true);        // the variants share their resource use
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              w8::kSmemBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(w8::w8a16_gemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed,
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed,
                              1) != cudaSuccess) {
         (void)cudaGetLastError();
         return 0;
@@ -494,7 +511,7 @@ static int w8_max_clusters(const DeviceInfo& dev, int size) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, w8::w8a16_gemm_kernel, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         return 0;
     }
@@ -525,7 +542,7 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     W8Params p{};
     p.w_scale = w_scale; p.bias = bias; p.residual = residual; p.y = y;
     p.ldy = ldy; p.ldr = ldr; p.M = M; p.N = N; p.K = K;
-    p.act = act; p.y_f32 = y_dtype == SFB_F32 ? 1 : 0;
+    p.y_f32 = y_dtype == SFB_F32 ? 1 : 0;
     p.kchunks = K / 64;
     // tokens per CTA: round up to 32, at most 256
     p.bn = M >= 256 ? 256 : ((M + 31) / 32) * 32;
@@ -567,18 +584,24 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
                                    dims, str, box, es, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc != SFB_OK) return rc;
     }
-    static bool attr_done[64] = {};
-    if (!attr_done[dev.ordinal & 63]) {
-        cudaError_t e1 = cudaFuncSetAttribute(w8::w8a16_gemm_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, w8::kSmemBytes);
-        cudaError_t e2 = cudaFuncSetAttribute(w8::w8a16_gemm_kernel,
-                                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e1 != cudaSuccess || e2 != cudaSuccess) {
-            (void)cudaGetLastError();
-            record_cuda_error(e1 != cudaSuccess ? e1 : e2, "w8a16 kernel attributes");
-            return SFB_ERR_CUDA;
+    const w8::KernFn kern = w8::pick(act, p.splits > 1);
+    {
+        static std::mutex mu;
+        static std::vector<std::pair<int, w8::KernFn>> done;
+        std::lock_guard<std::mutex> lock(mu);
+        bool have = false;
+        for (const auto& d : done) have = have || (d.first == dev.ordinal && d.second == kern);
+        if (!have) {
+            cudaError_t e1 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  w8::kSmemBytes);
+            cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e1 != cudaSuccess || e2 != cudaSuccess) {
+                (void)cudaGetLastError();
+                record_cuda_error(e1 != cudaSuccess ? e1 : e2, "w8a16 kernel attributes");
+                return SFB_ERR_CUDA;
+            }
+            done.emplace_back(dev.ordinal, kern);
         }
-        attr_done[dev.ordinal & 63] = true;
     }
 #ifdef SFB_TRACE
     p.trace = g_w8_trace;
@@ -595,7 +618,7 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1 + pdl_attr(&attr[1], pdl);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, w8::w8a16_gemm_kernel, mx, mw, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, p);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
         record_cuda_error(e, "w8a16 gemm launch");
