@@ -86,7 +86,8 @@ int sfb_copy_device(void* dst, const void* src, int64_t bytes);
  *   produce NaN).
  * - heads % heads_kv == 0 (grouped K/V heads, as flash_attn::mha_fwd's H_k).
  * - dtype: SFB_BF16 / SFB_F16 (tcgen05 tensor-core kernel, head_dim 64) or
- *   SFB_F32 (SIMT kernel, head_dim <= 128). q, k, v, out share the dtype.
+ *   SFB_F32 (SIMT kernel, head_dim <= 128). q, k, v, out share the dtype,
+ *   except that v_dtype = SFB_F16 with dtype SFB_BF16 takes V in fp16.
  * - Tensor-core path: softmax in fp32; the probabilities and V enter the P·V
  *   product as fp16 (bf16 V is converted exactly in shared memory). bf16 V
  *   entries beyond the fp16 range (|v| > 65504) are not supported: the kernel
@@ -116,6 +117,8 @@ typedef struct sfb_attn_args {
     /* Number of key splits merged inside one thread-block cluster
      * (0 = choose automatically, else 1..16). Tuning knob only. */
     int32_t num_splits;
+    int32_t v_dtype;        /* 0: V has `dtype`; SFB_F16 with dtype SFB_BF16: V is already
+                               fp16 (a cache stored in the P·V operand type: no conversion) */
 } sfb_attn_args;
 
 int sfb_attention_fwd(const sfb_attn_args* args, void* stream);

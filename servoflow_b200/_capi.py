@@ -53,6 +53,7 @@ class AttnArgs(ctypes.Structure):
         ("key_mask", ctypes.c_void_p),
         ("key_mask_stride_b", ctypes.c_int64),
         ("num_splits", ctypes.c_int32),
+        ("v_dtype", ctypes.c_int32),
     ]
 
 

@@ -64,7 +64,8 @@ def attention_args(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, out: torch
             raise _capi.SfbError(_capi.SFB_ERR_SHAPE, f"{n} must be 4-D")
         if t.stride(3) != 1:
             raise _capi.SfbError(_capi.SFB_ERR_SHAPE, f"{n}: head_dim must be contiguous")
-    if not (Q.dtype == K.dtype == V.dtype == out.dtype):
+    v_f16 = Q.dtype == torch.bfloat16 and V.dtype == torch.float16
+    if not (Q.dtype == K.dtype == out.dtype and (V.dtype == Q.dtype or v_f16)):
         raise _capi.SfbError(_capi.SFB_ERR_DTYPE, "Q/K/V/out dtypes differ")
     if layout == "bhsd":
         bi, hi, si = 0, 1, 2
@@ -85,6 +86,7 @@ def attention_args(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, out: torch
     a.is_causal = 1 if is_causal else 0
     a.scale = float(scale)
     a.num_splits = int(num_splits)
+    a.v_dtype = _capi.SFB_F16 if v_f16 else 0
     a.kv_len = None
     a.key_mask = None
     if mask is not None:

@@ -67,6 +67,7 @@ struct AttnTcParams {
     const int32_t* kv_len;
     const uint8_t* key_mask;
     int64_t  mask_sb;
+    int32_t  v_f16;                  // bf16 Q/K with V already in fp16: no in-kernel conversion
 #ifdef SFB_TRACE
     unsigned long long* trace;
     int dbg_skip;                    // timing experiments only: return at once
@@ -173,6 +174,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     using HO = HalfOps<T>;
     constexpr bool kConvV = std::is_same<T, __nv_bfloat16>::value;   // bf16 V needs an fp16 copy
     constexpr uint32_t kFmtQK = kConvV ? 1u : 0u;
+    const bool conv_v = kConvV && !p.v_f16;          // bf16 V converted to fp16 here
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -349,12 +351,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 #ifdef SFB_TRACE
                 if (nP < nS) {
                     if (!seen_p && mbar_test(&bars[bar_p(nP % kBufs)], (nP / kBufs) & 1)) seen_p = clock64();
-                    if (!seen_v && mbar_test(&bars[kConvV ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
+                    if (!seen_v && mbar_test(&bars[conv_v ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
                                              (nP / kStages) & 1)) seen_v = clock64();
                 }
 #endif
                 if (nP < nS && mbar_test(&bars[bar_p(nP % kBufs)], (nP / kBufs) & 1) &&
-                    mbar_test(&bars[kConvV ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
+                    mbar_test(&bars[conv_v ? bar_vc(nP % kStages) : bar_v(nP % kStages)],
                               (nP / kStages) & 1)) {
 #ifdef SFB_TRACE
                     const long long tb0 = clock64();
@@ -380,7 +382,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 }
             }
         }
-    } else if (kConvV && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
+    } else if (conv_v && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
         // ── V conversion warps: bf16 → fp16 in place (same swizzled layout) ──
         const int ct = (warp - kConvWarp0) * 32 + lane;
         uint32_t bad = 0;
@@ -663,7 +665,7 @@ int choose_attn_splits(int units, int ntiles_max, int num_sms) {
     return s;
 }
 
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl) {
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl, bool v_f16) {
     const int eb = 2;
     const CUtensorMapDataType dt =
         a.dtype == SFB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -681,7 +683,8 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl) {
                           a.q_stride[0], eb, 64, 128)) != SFB_OK) return rc;
     if ((rc = make_map_4d(&mk, a.k, dt, 64, a.seq_k, a.heads_kv, a.batch, a.k_stride[2], a.k_stride[1],
                           a.k_stride[0], eb, 64, 128)) != SFB_OK) return rc;
-    if ((rc = make_map_4d(&mv, a.v, dt, 64, a.seq_k, a.heads_kv, a.batch, a.v_stride[2], a.v_stride[1],
+    if (v_f16 && a.dtype != SFB_BF16) return SFB_ERR_DTYPE;
+    if ((rc = make_map_4d(&mv, a.v, v_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : dt, 64, a.seq_k, a.heads_kv, a.batch, a.v_stride[2], a.v_stride[1],
                           a.v_stride[0], eb, 64, 128)) != SFB_OK) return rc;
 
     const DeviceInfo& dev = device_info();
@@ -696,6 +699,7 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl) {
     p.kv_len = a.kv_len;
     p.key_mask = a.key_mask;
     p.mask_sb = a.key_mask_stride_b;
+    p.v_f16 = v_f16 ? 1 : 0;
 #ifdef SFB_TRACE
     p.trace = g_trace_ptr;
     p.dbg_skip = g_attn_skip;

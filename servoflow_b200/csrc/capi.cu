@@ -4,7 +4,7 @@
 #include "common.cuh"
 
 namespace sfb {
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl);
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl, bool v_f16);
 int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream);
 int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
@@ -66,12 +66,16 @@ int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
     if (a->heads % a->heads_kv != 0) return SFB_ERR_SHAPE;
     if (a->dtype != SFB_F32 && a->dtype != SFB_F16 && a->dtype != SFB_BF16) return SFB_ERR_DTYPE;
     if (a->num_splits < 0 || a->num_splits > 16) return SFB_ERR_INVALID;
+    if (a->v_dtype != 0 && a->v_dtype != a->dtype && !(a->v_dtype == SFB_F16 && a->dtype == SFB_BF16))
+        return SFB_ERR_DTYPE;
     if (a->batch == 0 || a->seq_q == 0) return SFB_OK;
     const sfb::DeviceInfo& dev = sfb::device_info();
     if (!sfb::is_sm100(dev)) return SFB_ERR_UNSUPPORTED;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool tc = (a->dtype == SFB_F16 || a->dtype == SFB_BF16) && a->head_dim == 64;
-    return tc ? sfb::attention_tc_launch(*a, s, false) : sfb::attention_simt_launch(*a, s);
+    const bool v_f16 = a->v_dtype == SFB_F16 && a->dtype == SFB_BF16;
+    if (v_f16 && !tc) return SFB_ERR_DTYPE;
+    return tc ? sfb::attention_tc_launch(*a, s, false, v_f16) : sfb::attention_simt_launch(*a, s);
 }
 
 int sfb_attention_bhsd(const void* q, const void* k, const void* v, void* out, int32_t batch,

@@ -18,6 +18,9 @@
 //   add_rows        cond += pos (condition position embeddings).
 //   dpm_update      x ← a·x + b·x0 + c·x0_prev (one DPM-Solver++ step; the
 //                   coefficients are computed on the host).
+//   bf16_to_f16     in place on the cross-attention V cache once per control
+//                   tick, so every denoising step reads V in the P·V operand
+//                   type (exact for |v| <= 65504, else SFB_ERR_RANGE).
 #include "common.cuh"
 
 namespace sfb {
@@ -210,6 +213,33 @@ __global__ void dpm_update_kernel(float* __restrict__ x, const float* __restrict
     }
 }
 
+// In place on a strided [rows, cols] block (cols % 8 == 0): bf16 → fp16, exact
+// for |v| <= 65504 (fp16 has more mantissa bits); larger magnitudes set
+// SFB_ERR_RANGE in the device error flag.
+__global__ void bf16_to_f16_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int rows, int cols) {
+    pdl_trigger();
+    pdl_wait();
+    const int per_row = cols / 8;
+    const int64_t n = static_cast<int64_t>(rows) * per_row;
+    bool bad = false;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / per_row, c = (i - r * per_row) * 8;
+        uint4* p = reinterpret_cast<uint4*>(x + r * ld + c);
+        uint4 u = *p;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float lo = __uint_as_float(w[e] << 16), hi = __uint_as_float(w[e] & 0xffff0000u);
+            bad |= (fabsf(lo) > 65504.f) | (fabsf(hi) > 65504.f);
+            const __half2 h = __floats2half2_rn(lo, hi);
+            w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        *p = u;
+    }
+    if (bad) atomicExch(&g_sfb_device_error, SFB_ERR_RANGE);
+}
+
 inline unsigned grid_for(int64_t n, int threads) {
     int64_t g = (n + threads - 1) / threads;
     return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(g, 148 * 32)));
@@ -238,6 +268,14 @@ int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w
     return launch_kernel(rdt::head_rms_norm_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, s,
                          true, static_cast<__nv_bfloat16*>(x), ld, rows, heads,
                          static_cast<const __nv_bfloat16*>(w), eps);
+}
+
+int bf16_to_f16_launch(void* x, int64_t ld, int rows, int cols, cudaStream_t s) {
+    if (cols % 8 || ld % 8) return SFB_ERR_SHAPE;
+    if (rows <= 0) return SFB_OK;
+    prefer_max_shared(rdt::bf16_to_f16_kernel);
+    return launch_kernel(rdt::bf16_to_f16_kernel, rdt::grid_for(static_cast<int64_t>(rows) * cols / 8, 256), 256,
+                         0, s, true, static_cast<__nv_bfloat16*>(x), ld, rows, cols);
 }
 
 }  // namespace sfb

@@ -94,6 +94,20 @@ def test_config2_image_cross_attention(be, gpu):
     assert torch.equal(out2, run(be, q, k, v))
 
 
+@pytest.mark.parametrize("Lk,B,masked", [(4374, 1, False), (1024, 4, True)])
+def test_fp16_v_cache(be, gpu, Lk, B, masked):
+    # bf16 Q/K with the V cache already in fp16 (how the model stores it):
+    # same result as bf16 V converted inside the kernel
+    q, k, v = make(B, 32, 32, 67, Lk, 64, torch.bfloat16, 5, gpu)
+    v16 = v.to(torch.float16)
+    lens = torch.randint(8, Lk + 1, (B,), generator=torch.Generator().manual_seed(6), dtype=torch.int32)
+    kw = {"mask": lens.to(gpu)} if masked else {}
+    ref = oracle_of(q, k, v16, **({"kv_len": lens.numpy()} if masked else {}))
+    out = run(be, q, k, v16, **kw)
+    check_close(out, ref, torch.bfloat16)
+    assert torch.equal(out, run(be, q, k, v, **kw))
+
+
 def test_config3_language_cross_attention_masked(be, gpu):
     B, Lk = 16, 1024
     q, k, v = make(B, 32, 32, 67, Lk, 64, torch.bfloat16, 3, gpu)
