@@ -459,8 +459,9 @@ def main():
                     "d2h_bytes_per_step": act_h.numel() * 4,
                     "path": "RDT1B.sample_host -> sfb_rdt1b_sample: pinned host noise -> device, "
                             "graph replay, actions -> pinned host, all inside the timed region"},
-            "gpu_launches": kernels_per_step * args.steps,
+            "gpu_launches": kernels_per_step * args.steps * world,
             "gpu_launches_note": f"{kernels_per_step} kernels per denoise graph x {args.steps} timed steps "
+                                 f"x {world} GPU(s) "
                                  f"(counted from the captured graph's kernel nodes); the e2e, tick and "
                                  f"roofline passes add more",
             "clocks": sampler.summary(),
