@@ -68,6 +68,9 @@ struct AttnTcParams {
     const uint8_t* key_mask;
     int64_t  mask_sb;
     int32_t  v_f16;                  // bf16 Q/K with V already in fp16: no in-kernel conversion
+    const __nv_bfloat16* qn_w;       // per-head RMSNorm weight [64] applied to Q rows, or null
+    const __nv_bfloat16* kn_w;       // the same for K rows, or null
+    float    norm_eps;
 #ifdef SFB_TRACE
     unsigned long long* trace;
     int dbg_skip;                    // timing experiments only: return at once
@@ -101,7 +104,7 @@ constexpr int kOffStage  = kOffQ + kTileBytes;              // [kStages] × (K, 
 constexpr int kOffMerge  = kOffStage + kStages * 2 * kTileBytes;
 constexpr int kMergeBytes = kMergeRows * (2 * kOStride + 2) * 4;
 constexpr int kOffBar    = kOffMerge + kMergeBytes;
-constexpr int kOffTmem   = kOffBar + 8 * 32;
+constexpr int kOffTmem   = kOffBar + 8 * 40;
 constexpr int kOffRed    = kOffTmem + 16;                   // float [2 groups][m|l][128]
 constexpr int kSmemUsed  = kOffRed + 2 * 2 * 128 * 4;
 constexpr int kSmemBytes = kSmemUsed + 1024;                // + alignment slack
@@ -118,8 +121,45 @@ __host__ __device__ constexpr int bar_s(int u) { return 1 + 3 * kStages + u; }  
 __host__ __device__ constexpr int bar_p(int u) { return 1 + 3 * kStages + kBufs + u; }       // P_j written
 __host__ __device__ constexpr int bar_o(int u) { return 1 + 3 * kStages + 2 * kBufs + u; }   // PV_j done
 __host__ __device__ constexpr int bar_og(int g) { return 1 + 3 * kStages + 3 * kBufs + g; }  // group's PV done
-constexpr int kNumBars = 3 + 3 * kStages + 3 * kBufs;
-static_assert(kNumBars <= 32, "barrier area");
+constexpr int kBarQn = 3 + 3 * kStages + 3 * kBufs;                                        // Q rows normalised
+__host__ __device__ constexpr int bar_kn(int s) { return kBarQn + 1 + s; }                  // K rows normalised
+constexpr int kNumBars = kBarQn + 1 + kStages;
+static_assert(kNumBars <= 40, "barrier area");
+
+// RMS-normalises row r (64 bf16) of a 128-byte-swizzled [128 × 64] tile in
+// place: x · 1/sqrt(mean(x²) + eps) · w, fp32 math, bf16 result. The sum of
+// squares is formed as 8 per-chunk partials combined pairwise, the order of
+// the standalone per-head RMSNorm kernel, so both give identical bits.
+__device__ __forceinline__ void norm_row_sw128(uint8_t* tile, int r, const __nv_bfloat16* w, float eps) {
+    uint4 c[8];
+    float part[8];
+#pragma unroll
+    for (int lc = 0; lc < 8; ++lc) {                // logical 16-byte chunk lc sits at lc ^ (r & 7)
+        c[lc] = *reinterpret_cast<const uint4*>(tile + r * 128 + ((lc ^ (r & 7)) << 4));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&c[lc]);
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+        }
+        part[lc] = ss;
+    }
+    const float ss = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+    const float inv = 1.f / sqrtf(ss / 64.f + eps);
+#pragma unroll
+    for (int lc = 0; lc < 8; ++lc) {
+        const uint4 gu = *reinterpret_cast<const uint4*>(w + lc * 8);
+        const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&gu);
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&c[lc]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]), gg = __bfloat1622float2(g[i]);
+            h[i] = __floats2bfloat162_rn(f.x * inv * gg.x, f.y * inv * gg.y);
+        }
+        *reinterpret_cast<uint4*>(tile + r * 128 + ((lc ^ (r & 7)) << 4)) = c[lc];
+    }
+}
 
 template <typename T> struct HalfOps;
 template <> struct HalfOps<__nv_bfloat16> {
@@ -219,6 +259,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         }
         mbar_init(&bars[bar_og(0)], 1);
         mbar_init(&bars[bar_og(1)], 1);
+        mbar_init(&bars[kBarQn], 4);
+        for (int s = 0; s < kStages; ++s) mbar_init(&bars[bar_kn(s)], kConvWarps);
         fence_mbarrier_init();
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -255,6 +297,18 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int grp = (warp >> 2) & 1;     // softmax group (tile parity)
     const int row = win * 32 + lane;
     float m_ref = -INFINITY, l_run = 0.f;
+
+    // qk-RMSNorm fused into the load (dit_block.cu:185-196 applies it as a
+    // separate pass): warps 0..3 normalise the landed Q tile in place, one
+    // row per thread, before the first Q·Kᵀ; the K tiles are done by the
+    // V-conversion warps below.
+    if (p.qn_w != nullptr && warp < 4 && ntl > 0) {
+        wait(kBarQ, 0);
+        norm_row_sw128(sQ, row, p.qn_w, p.norm_eps);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kBarQn]);
+    }
 
     if (warp == kCtrlWarp) {
         // ── control warp: TMA + MMA issue ───────────────────────────────────
@@ -313,7 +367,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             __syncwarp();
             int nL = min(kStages, ntl);                // tiles whose K/V load is issued
             for (int t = 0; t < nL; ++t) issue_kv(t);
-            wait(kBarQ, 0);
+            wait(p.qn_w ? kBarQn : kBarQ, 0);
             // Event loop. P·V completions are retired in issue order, so every
             // parity probe is at most one phase behind its barrier.
             int nS = 0, nP = 0, pv_done = 0;
@@ -334,7 +388,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 while (nL < ntl && nL - kStages < pv_done) { issue_kv(nL); ++nL; progress = true; }
                 // S/P buffer of tile j is free once P·V of tile j - kBufs is done
                 if (nS < ntl && (nS < kBufs || nS - kBufs < pv_done) &&
-                    mbar_test(&bars[bar_k(nS % kStages)], (nS / kStages) & 1)) {
+                    mbar_test(&bars[p.kn_w ? bar_kn(nS % kStages) : bar_k(nS % kStages)], (nS / kStages) & 1)) {
 #ifdef SFB_TRACE
                     const long long ts0 = clock64();
 #endif
@@ -382,12 +436,22 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 }
             }
         }
-    } else if (conv_v && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
-        // ── V conversion warps: bf16 → fp16 in place (same swizzled layout) ──
+    } else if ((conv_v || p.kn_w != nullptr) && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
+        // ── K-norm / V conversion warps: K rows RMS-normalised in place, bf16 V
+        //    converted to fp16 in place (same swizzled layouts) ──
         const int ct = (warp - kConvWarp0) * 32 + lane;
         uint32_t bad = 0;
         for (int t = 0; t < ntl; ++t) {
             const int s = t % kStages;
+            if (p.kn_w != nullptr) {
+                wait(bar_k(s), (t / kStages) & 1);
+                for (int r = ct; r < kTileKeys; r += kConvWarps * 32)
+                    norm_row_sw128(sK(s), r, p.kn_w, p.norm_eps);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[bar_kn(s)]);
+            }
+            if (!conv_v) continue;
             wait(bar_v(s), (t / kStages) & 1);
             uint4* v4 = reinterpret_cast<uint4*>(sV(s));
 #pragma unroll 2
@@ -665,7 +729,8 @@ int choose_attn_splits(int units, int ntiles_max, int num_sms) {
     return s;
 }
 
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl, bool v_f16) {
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnOpts& o) {
+    const bool pdl = o.pdl, v_f16 = o.v_f16;
     const int eb = 2;
     const CUtensorMapDataType dt =
         a.dtype == SFB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -700,6 +765,10 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl, b
     p.key_mask = a.key_mask;
     p.mask_sb = a.key_mask_stride_b;
     p.v_f16 = v_f16 ? 1 : 0;
+    p.qn_w = static_cast<const __nv_bfloat16*>(o.qn_w);
+    p.kn_w = static_cast<const __nv_bfloat16*>(o.kn_w);
+    p.norm_eps = o.norm_eps;
+    if ((o.qn_w || o.kn_w) && (a.dtype != SFB_BF16 || a.head_dim != 64)) return SFB_ERR_DTYPE;
 #ifdef SFB_TRACE
     p.trace = g_trace_ptr;
     p.dbg_skip = g_attn_skip;

@@ -4,7 +4,7 @@
 #include "common.cuh"
 
 namespace sfb {
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl, bool v_f16);
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnOpts& o);
 int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream);
 int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
@@ -75,7 +75,7 @@ int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
     const bool tc = (a->dtype == SFB_F16 || a->dtype == SFB_BF16) && a->head_dim == 64;
     const bool v_f16 = a->v_dtype == SFB_F16 && a->dtype == SFB_BF16;
     if (v_f16 && !tc) return SFB_ERR_DTYPE;
-    return tc ? sfb::attention_tc_launch(*a, s, false, v_f16) : sfb::attention_simt_launch(*a, s);
+    return tc ? sfb::attention_tc_launch(*a, s, [&] { sfb::AttnOpts o; o.v_f16 = v_f16; return o; }()) : sfb::attention_simt_launch(*a, s);
 }
 
 int sfb_attention_bhsd(const void* q, const void* k, const void* v, void* out, int32_t batch,

@@ -117,6 +117,15 @@ inline void prefer_max_shared(K kernel) {
     }
 }
 
+// Options of the tensor-core attention launch beyond sfb_attn_args (model path).
+struct AttnOpts {
+    bool pdl = false;              // programmatic dependent launch
+    bool v_f16 = false;            // bf16 Q/K, V already fp16
+    const void* qn_w = nullptr;    // bf16 [64] per-head RMSNorm weight applied to Q rows
+    const void* kn_w = nullptr;    // the same for K rows
+    float norm_eps = 1e-6f;
+};
+
 // Returns the status of `expr` from the enclosing function unless it is SFB_OK.
 #define SFB_TRY(expr) do { int _rc = (expr); if (_rc != SFB_OK) return _rc; } while (0)
 

@@ -35,7 +35,7 @@
 
 namespace sfb {
 
-int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, bool pdl, bool v_f16);
+int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnOpts& o);
 int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                       int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
@@ -290,7 +290,7 @@ static int create(Model& m) {
 static int attention(const Model& m, const __nv_bfloat16* q, int64_t q_sb, int64_t q_ss,
                      const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t kv_sb, int64_t kv_ss,
                      __nv_bfloat16* out, int B, int Lq, int Lk, const int32_t* kv_len, bool v_f16,
-                     cudaStream_t s) {
+                     const __nv_bfloat16* qn_w, const __nv_bfloat16* kn_w, cudaStream_t s) {
     sfb_attn_args a;
     std::memset(&a, 0, sizeof(a));
     a.q = q; a.k = k; a.v = v; a.out = out;
@@ -301,7 +301,13 @@ static int attention(const Model& m, const __nv_bfloat16* q, int64_t q_sb, int64
     a.out_stride[2] = m.c.hidden;
     a.batch = B; a.heads = m.c.heads; a.heads_kv = m.c.heads; a.seq_q = Lq; a.seq_k = Lk;
     a.head_dim = 64; a.dtype = SFB_BF16; a.kv_len = kv_len;
-    return attention_tc_launch(a, s, true, v_f16);
+    AttnOpts o;
+    o.pdl = true;
+    o.v_f16 = v_f16;
+    o.qn_w = qn_w;                   // qk-RMSNorm applied inside the attention kernel
+    o.kn_w = kn_w;
+    o.norm_eps = 1e-6f;
+    return attention_tc_launch(a, s, o);
 }
 
 // Condition encoding for one control tick (rdt1b.cpp:167-239 + the per-block
@@ -373,20 +379,18 @@ static int forward(Model& m, int B, float t, cudaStream_t s) {
         // x = x + proj(attn(qk-norm(qkv(norm1(x)))))
         SFB_TRY(rms_norm_launch(m.x, D, bl.norm1, m.xn, D, M, D, eps, s));
         SFB_TRY(linear(bl.qkv, m.xn, D, M, m.qkv, 3 * D, 0, nullptr, 0, s));
-        SFB_TRY(head_rms_norm_launch(m.qkv, 3 * D, M, c.heads, bl.qn, eps, s));
-        SFB_TRY(head_rms_norm_launch(m.qkv + D, 3 * D, M, c.heads, bl.kn, eps, s));
         SFB_TRY(attention(m, m.qkv, static_cast<int64_t>(S) * 3 * D, 3 * D, m.qkv + D, m.qkv + 2 * D,
-                          static_cast<int64_t>(S) * 3 * D, 3 * D, m.attn, B, S, S, nullptr, false, s));
+                          static_cast<int64_t>(S) * 3 * D, 3 * D, m.attn, B, S, S, nullptr, false,
+                          bl.qn, bl.kn, s));
         SFB_TRY(linear(bl.proj, m.attn, D, M, m.x, D, 0, m.x, D, s));
         // x = x + proj(cross_attn(qnorm(q(norm2(x))), K/V cache))
         const bool lang_blk = (l % 2 == 0);
         const int Lk = lang_blk ? c.max_lang_len : c.img_len;
         SFB_TRY(rms_norm_launch(m.x, D, bl.norm2, m.xn, D, M, D, eps, s));
         SFB_TRY(linear(bl.cq, m.xn, D, M, m.h, D, 0, nullptr, 0, s));
-        SFB_TRY(head_rms_norm_launch(m.h, D, M, c.heads, bl.cqn, eps, s));
         SFB_TRY(attention(m, m.h, static_cast<int64_t>(S) * D, D, m.kv[l], m.kv[l] + D,
                           static_cast<int64_t>(Lk) * 2 * D, 2 * D, m.attn, B, S, Lk,
-                          lang_blk ? m.lang_len : nullptr, true, s));
+                          lang_blk ? m.lang_len : nullptr, true, bl.cqn, nullptr, s));
         SFB_TRY(linear(bl.cproj, m.attn, D, M, m.x, D, 0, m.x, D, s));
         // x = x + fc2(gelu(fc1(norm3(x))))
         SFB_TRY(rms_norm_launch(m.x, D, bl.norm3, m.xn, D, M, D, eps, s));
