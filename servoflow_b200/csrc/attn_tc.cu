@@ -74,6 +74,8 @@ struct AttnTcParams {
 #ifdef SFB_TRACE
     unsigned long long* trace;
     int dbg_skip;                    // timing experiments only: return at once
+    unsigned long long* tl;
+    int tl_launch;
 #endif
 };
 
@@ -276,6 +278,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const uint32_t tmem = *tmem_holder;
     pdl_trigger();                       // TMEM is held: the next kernel may start
     pdl_wait();                          // Q/K/V, key lengths and the output belong to earlier kernels
+#ifdef SFB_TRACE
+    const unsigned long long tl_t1 = ptx::global_timer_ns();
+#endif
     SFB_T(1);
 
     // Key range of this (batch, q-tile), then this CTA's share of its tiles.
@@ -691,6 +696,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     if (!ok) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
     tc_fence_before_sync();
     __syncthreads();
+#ifdef SFB_TRACE
+    tl_record(p.tl, p.tl_launch, 3, cta_t0, tl_t1);
+#endif
     if (warp == 0) {
         tc_fence_after_sync();
         tmem_dealloc(tmem, kTmemCols);
@@ -716,6 +724,7 @@ static int make_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 #ifdef SFB_TRACE
 static unsigned long long* g_trace_ptr = nullptr;
 extern "C" void sfb_debug_set_trace(void* p) { g_trace_ptr = static_cast<unsigned long long*>(p); }
+extern "C" void sfb_debug_set_timeline(void* p) { tl_buf() = static_cast<unsigned long long*>(p); tl_count() = 0; }
 static int g_attn_skip = 0;
 extern "C" void sfb_debug_set_attn_skip(int s) { g_attn_skip = s; }
 #endif
@@ -771,6 +780,8 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnO
     if ((o.qn_w || o.kn_w) && (a.dtype != SFB_BF16 || a.head_dim != 64)) return SFB_ERR_DTYPE;
 #ifdef SFB_TRACE
     p.trace = g_trace_ptr;
+    p.tl = tl_buf();
+    p.tl_launch = tl_next();
     p.dbg_skip = g_attn_skip;
 #endif
     const int units = a.batch * a.heads * p.qtiles;

@@ -117,6 +117,25 @@ inline void prefer_max_shared(K kernel) {
     }
 }
 
+#ifdef SFB_TRACE
+// Timeline of kernel launches (debug builds only): per launch and CTA, the
+// global-timer start, the time past griddepcontrol.wait and the end.
+inline unsigned long long*& tl_buf() { static unsigned long long* b = nullptr; return b; }
+inline int& tl_count() { static int n = 0; return n; }
+inline int tl_next() { return tl_buf() ? tl_count()++ : -1; }
+__device__ __forceinline__ void tl_record(unsigned long long* buf, int launch, int kind,
+                                          unsigned long long t0, unsigned long long t1) {
+    if (buf == nullptr || launch < 0 || threadIdx.x != 0) return;
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    if (cta >= 512 || launch >= 4096) return;
+    unsigned long long* e = buf + (static_cast<size_t>(launch) * 512 + cta) * 4;
+    unsigned long long t2;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t2));
+    e[0] = t0; e[1] = t1; e[2] = t2;
+    e[3] = (static_cast<unsigned long long>(kind) << 32) | (gridDim.x * gridDim.y * gridDim.z);
+}
+#endif
+
 // Options of the tensor-core attention launch beyond sfb_attn_args (model path).
 struct AttnOpts {
     bool pdl = false;              // programmatic dependent launch

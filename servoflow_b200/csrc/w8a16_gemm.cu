@@ -55,6 +55,8 @@ struct W8Params {
     int32_t        stages;        // pipeline depth, kRingBytes / stage bytes, at most kMaxStages
 #ifdef SFB_TRACE
     unsigned long long* trace;
+    unsigned long long* tl;
+    int tl_launch;
 #endif
 };
 
@@ -62,7 +64,7 @@ namespace w8 {
 
 #ifdef SFB_TRACE
 #define W8_T(slot, i) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) \
-        p.trace[(slot) * 64 + (i)] = clock64(); } while (0)
+        p.trace[(slot) * 64 + (i)] = ptx::global_timer_ns(); } while (0)
 #else
 #define W8_T(slot, i) do { } while (0)
 #endif
@@ -71,8 +73,9 @@ constexpr int kThreads  = 10 * 32;        // TMA, MMA, 8 converter/epilogue warp
 constexpr int kConvWarps = 8;
 constexpr int kStageStride = 36;           // floats per row of an epilogue staging block
 constexpr int kMaxStages = 8;
-constexpr int kWBytes   = 128 * 64;            // int8 weight tile
-constexpr int kWbBytes  = 128 * 128;           // bf16 weight tile (SW128)
+// Weight tiles are TM = 128 or 64 output channels (MMA M) × 64 K elements.
+__host__ __device__ constexpr int w_bytes(int tm) { return tm * 64; }     // int8 weight tile
+__host__ __device__ constexpr int wb_bytes(int tm) { return tm * 128; }   // bf16 weight tile (SW128)
 // One ring area split into `stages` X tiles (bn · 128 B, bn <= 256), then as
 // many bf16 and int8 weight tiles; the depth follows the token tile: 4 stages
 // at bn = 256, 6 at 96, 8 at 64 and below.
@@ -89,11 +92,11 @@ constexpr int kOffRecv  = 65536 + 1024;
 static_assert(kOffRecv + 65536 <= kRingBytes, "merge areas fit the ring");
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
-__host__ __device__ constexpr int stage_bytes(int bn) { return kWBytes + kWbBytes + bn * 128; }
-__host__ __device__ constexpr int num_stages(int bn) {
-    return kRingBytes / stage_bytes(bn) < kMaxStages ? kRingBytes / stage_bytes(bn) : kMaxStages;
+__host__ __device__ constexpr int stage_bytes(int bn, int tm) { return w_bytes(tm) + wb_bytes(tm) + bn * 128; }
+__host__ __device__ constexpr int num_stages(int bn, int tm) {
+    return kRingBytes / stage_bytes(bn, tm) < kMaxStages ? kRingBytes / stage_bytes(bn, tm) : kMaxStages;
 }
-static_assert(num_stages(256) >= 4, "four stages at the widest token tile");
+static_assert(num_stages(256, 128) >= 4, "four stages at the widest token tile");
 
 __host__ __device__ constexpr int bar_full_w(int s) { return s; }                    // W int8 landed
 __host__ __device__ constexpr int bar_full_x(int s) { return kMaxStages + s; }       // X landed
@@ -107,9 +110,12 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.f + tanhf(k0 * fmaf(k1 * x * x, x, x)));
 }
 
-// kAct: 0 none, 1 GELU (tanh), 2 SiLU; kSplit: K split across a cluster.
-// Each instantiation carries only its own epilogue path.
-template <int kAct, bool kSplit>
+// kAct: 0 none, 1 GELU (tanh), 2 SiLU; kSplit: K split across a cluster;
+// kTM: output channels per CTA (MMA M), 128 or 64. With M = 64 the
+// accumulator row r sits in TMEM lane 32·(r / 16) + r % 16 (lanes 16..31 of
+// each 32-lane window unused; measured on B200). Each instantiation carries
+// only its own epilogue path.
+template <int kAct, bool kSplit, int kTM>
 __global__ void __launch_bounds__(kThreads, 1)
 w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmW,
@@ -123,17 +129,25 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     const int nst = p.stages;
     const int xtile = p.bn * 128;
     auto sX  = [&](int s) { return smem + s * xtile; };
-    auto sWb = [&](int s) { return smem + nst * xtile + s * kWbBytes; };
-    auto sW  = [&](int s) { return smem + nst * (xtile + kWbBytes) + s * kWBytes; };
+    constexpr int kWB = w_bytes(kTM), kWBB = wb_bytes(kTM);
+    constexpr int kRowsPerWin = kTM / 4;               // accumulator rows per 32-lane TMEM window
+    auto sWb = [&](int s) { return smem + nst * xtile + s * kWBB; };
+    auto sW  = [&](int s) { return smem + nst * (xtile + kWBB) + s * kWB; };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x;
-    const int n0 = blockIdx.y * 128;
+    const int n0 = blockIdx.y * kTM;
     const int m0 = blockIdx.z * p.bn;
     // this CTA's share of the 64-wide K chunks
     const int cbase = p.kchunks / p.splits, crem = p.kchunks - cbase * p.splits;
     const int c_begin = split * cbase + min(split, crem);
     const int nch = cbase + (split < crem ? 1 : 0);
+    // CTAs of different channel tiles walk their K range from different
+    // chunks, so the activation tile each one loads at a given moment differs
+    // (all channel tiles read the same activations; in lockstep they queue on
+    // the same L2 slices).
+    const int rot = nch > 0 ? static_cast<int>(blockIdx.y) % nch : 0;
+    auto kchunk = [&](int c) { const int r = c + rot; return c_begin + (r >= nch ? r - nch : r); };
 
 #ifdef SFB_TRACE
     const uint64_t cta_t0 = ptx::global_timer_ns();
@@ -149,7 +163,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         mbar_init(&bars[kBarMerge], 1);
         if (kSplit)         // partials of the other C-1 CTAs land here by bulk copy
             mbar_arrive_expect_tx(&bars[kBarMerge],
-                                  static_cast<uint32_t>((p.splits - 1) * p.bn * (128 / p.splits) * 4));
+                                  static_cast<uint32_t>((p.splits - 1) * p.bn * (kTM / p.splits) * 4));
         fence_mbarrier_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
@@ -164,6 +178,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     const uint32_t tmem = *tmem_holder;
     pdl_trigger();                                     // TMEM is held: the next kernel may start
 
+#ifdef SFB_TRACE
+    unsigned long long tl_t1 = 0;
+#endif
     bool ok = true;
     auto wait = [&](int bar, uint32_t parity) {
         if (!mbar_wait(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
@@ -177,19 +194,22 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         const int pre = min(nch, nst);
         if (elect_one()) {
             for (int c = 0; c < pre; ++c) {
-                mbar_arrive_expect_tx(&bars[bar_full_w(c)], kWBytes);
-                tma_load_2d(sW(c), &tmW, &bars[bar_full_w(c)], (c_begin + c) * 64, n0);
+                mbar_arrive_expect_tx(&bars[bar_full_w(c)], kWB);
+                tma_load_2d(sW(c), &tmW, &bars[bar_full_w(c)], kchunk(c) * 64, n0);
             }
         }
         __syncwarp();
         pdl_wait();
+#ifdef SFB_TRACE
+        tl_t1 = ptx::global_timer_ns();
+#endif
         for (int c = 0; c < nch; ++c) {
             const int s = c % nst;
             if (c >= nst) wait(bar_empty(s), ((c / nst) - 1) & 1);
             if (elect_one()) {
-                const int k0 = (c_begin + c) * 64;
+                const int k0 = kchunk(c) * 64;
                 if (c >= nst) {
-                    mbar_arrive_expect_tx(&bars[bar_full_w(s)], kWBytes);
+                    mbar_arrive_expect_tx(&bars[bar_full_w(s)], kWB);
                     tma_load_2d(sW(s), &tmW, &bars[bar_full_w(s)], k0, n0);
                 }
                 mbar_arrive_expect_tx(&bars[bar_full_x(s)], xbytes);
@@ -200,7 +220,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         }
     } else if (warp == 1) {
         // ── MMA issuer ──────────────────────────────────────────────────────
-        const uint32_t idesc = idesc_f16(128, static_cast<uint32_t>(p.bn), 1, 0, 0);
+        const uint32_t idesc = idesc_f16(kTM, static_cast<uint32_t>(p.bn), 1, 0, 0);
         for (int c = 0; c < nch; ++c) {
             const int s = c % nst;
             wait(bar_conv(s), (c / nst) & 1);
@@ -220,7 +240,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             __syncwarp();
         }
     } else {
-        // ── converters: int8 [128 × 64] → bf16 SW128 [128 × 64] ──────────────
+        // ── converters: int8 [TM × 64] → bf16 SW128 [TM × 64] ────────────────
         // Two groups of four warps take alternate chunks, so the conversion
         // latency of one chunk overlaps the next.
         const int grp = (warp - 2) >> 2;
@@ -231,14 +251,15 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             if (ct == 0) W8_T(1, c);
             const uint8_t* src = sW(s);
             uint8_t* dst = sWb(s);
-            uint2 raw[8];
+            constexpr int kIt = kTM / 16;              // 8-byte units per thread
+            uint2 raw[kIt];
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {           // all loads first: independent
+            for (int it = 0; it < kIt; ++it) {         // all loads first: independent
                 const int unit = it * 128 + ct;        // (row, 8-element chunk)
                 raw[it] = *reinterpret_cast<const uint2*>(src + (unit >> 3) * 64 + (unit & 7) * 8);
             }
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {
+            for (int it = 0; it < kIt; ++it) {
                 const int unit = it * 128 + ct;
                 const int r = unit >> 3, ch = unit & 7;
                 uint32_t o[4];
@@ -267,10 +288,12 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     const bool epi = warp >= 2;
     const int win = warp & 3;
     const int hh = (warp - 2) >> 2;                    // 0: warps 2..5, 1: warps 6..9
-    const int nrow = n0 + win * 32 + lane;             // output channel of this thread
+    const bool lane_ok = kTM == 128 || lane < 16;     // lane holds an accumulator row
+    const int trow = win * kRowsPerWin + lane;          // tile row (output channel) of this thread
+    const int nrow = n0 + trow;
     const uint32_t lane_off = static_cast<uint32_t>(win * 32) << 16;
     float sc = 0.f, bi = 0.f;
-    if (epi && nrow < p.N) {
+    if (epi && lane_ok && nrow < p.N) {
         sc = p.w_scale[nrow];
         if (p.bias) bi = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[nrow]);
     }
@@ -281,12 +304,32 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     };
     if (tid == 64) W8_T(4, 0);
     pdl_wait();                                        // before the residual read and the output write
+    const int mvalid = min(p.bn, p.M - m0);
+    // Split-K owner pass: the residual rows this thread adds, loaded while the
+    // MMAs finish.
+    const int seg_per_row = (kTM / p.splits) / 8;      // 8-channel segments per owned row
+    const int nunits = mvalid * seg_per_row;
+    constexpr int kMaxIt = 4;                          // (128 tokens · 8 segs) / 256 threads
+    uint4 rres[kMaxIt];
+    if constexpr (kSplit) {
+        if (epi) {
+            const int nb = n0 + split * (kTM / p.splits);
+#pragma unroll
+            for (int it = 0; it < kMaxIt; ++it) {
+                const int u = tid - 64 + it * kConvWarps * 32;
+                const int mm = u / seg_per_row, n = nb + (u - mm * seg_per_row) * 8;
+                rres[it] = make_uint4(0u, 0u, 0u, 0u);
+                if (p.residual && u < nunits && n < p.N)
+                    rres[it] = *reinterpret_cast<const uint4*>(
+                        static_cast<const __nv_bfloat16*>(p.residual) + (m0 + mm) * p.ldr + n);
+            }
+        }
+    }
     if (epi && nch > 0) {
         wait(kBarAcc, 0);
         tc_fence_after_sync();
     }
     if (tid == 64) W8_T(4, 1);
-    const int mvalid = min(p.bn, p.M - m0);
     if constexpr (!kSplit) {
         // Each warp takes 32-column blocks c0 = 32·hh, 32·hh + 64, ...: TMEM →
         // act(acc·s + b) staged as fp32 [32 tokens][32 channels] in shared memory
@@ -294,7 +337,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         // channels per token row, with the residual added in the same pass.
         if (epi) {
             float* stg = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * kStageStride;
-            const int nb = n0 + win * 32;               // first channel of this warp
+            const int nb = n0 + win * kRowsPerWin;      // first channel of this warp
+            constexpr int kSegs = kRowsPerWin / 8;      // 8-channel segments per token row
+            constexpr int kRowsPass = 32 / kSegs;       // token rows written per pass
 #pragma unroll 1
             for (int c0 = 32 * hh; c0 < p.bn; c0 += 64) {
                 float v[32];
@@ -307,8 +352,8 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                 for (int i = 0; i < 32; ++i) stg[i * kStageStride + lane] = act(fmaf(v[i], sc, bi));
                 __syncwarp();
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int r = j * 8 + (lane >> 2), seg = (lane & 3) * 8;   // token row, 8 channels
+                for (int j = 0; j < 32 / kRowsPass; ++j) {
+                    const int r = j * kRowsPass + lane / kSegs, seg = (lane % kSegs) * 8;   // token row, 8 channels
                     const int m = m0 + c0 + r, n = nb + seg;
                     if (c0 + r < mvalid && n < p.N && ok) {
                         const float4 a = *reinterpret_cast<const float4*>(stg + r * kStageStride + seg);
@@ -342,27 +387,22 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         }
     } else {
         // Split-K merge. CTA r owns channel rows [r·R, (r+1)·R) of the tile,
-        // R = 128 / C. Every CTA stages its fp32 partial as C contiguous
+        // R = TM / C. Every CTA stages its fp32 partial as C contiguous
         // owner slices [bn tokens][R channels] (padded by R floats between
         // slices so the per-lane stores hit distinct banks), then one thread
         // bulk-copies slice r into CTA r's receive area, signalling r's merge
         // barrier. The owner sums its own slice and the C - 1 received ones,
         // applies scale/bias/activation/residual and writes 16-byte vectors of
         // 8 channels per token.
-        const int C = p.splits, R = 128 / C;
+        const int C = p.splits, R = kTM / C;
         const int slice = p.bn * R;
         float* stg = reinterpret_cast<float*>(smem);
         float* rcv = reinterpret_cast<float*>(smem + kOffRecv);
-        const int segs = R / 8;                         // 8-channel segments per owned row
-        const int nunits = mvalid * segs;
-        constexpr int kMaxIt = 4;                       // (128 tokens · 8 segs) / 256 threads
-        uint4 rres[kMaxIt];
         if (epi) {
             // Staged values carry the channel scale and (from CTA 0 only) the bias,
             // so the owner's pass is a plain sum.
             const float bsplit = split == 0 ? bi : 0.f;
-            const int row = win * 32 + lane;
-            const int owner = row / R, slot = row - owner * R;
+            const int owner = trow / R, slot = trow - owner * R;
             float* d = stg + owner * (slice + R) + slot;
             float v[2][32];
             const int c0a = 32 * hh, c0b = 32 * hh + 64;
@@ -374,26 +414,15 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 #pragma unroll
                 for (int i = 0; i < 32; ++i) { v[0][i] = 0.f; v[1][i] = 0.f; }
             }
-            if (c0a < p.bn) {
+            if (lane_ok && c0a < p.bn) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) d[(c0a + i) * R] = fmaf(v[0][i], sc, bsplit);
             }
-            if (c0b < p.bn) {
+            if (lane_ok && c0b < p.bn) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) d[(c0b + i) * R] = fmaf(v[1][i], sc, bsplit);
             }
             fence_proxy_async_smem();
-            // the residual rows this thread adds in the owner pass, loaded early
-            const int nb = n0 + split * R;
-#pragma unroll
-            for (int it = 0; it < kMaxIt; ++it) {
-                const int u = tid - 64 + it * kConvWarps * 32;
-                const int mm = u / segs, n = nb + (u - mm * segs) * 8;
-                rres[it] = make_uint4(0u, 0u, 0u, 0u);
-                if (p.residual && u < nunits && n < p.N)
-                    rres[it] = *reinterpret_cast<const uint4*>(
-                        static_cast<const __nv_bfloat16*>(p.residual) + (m0 + mm) * p.ldr + n);
-            }
         }
         if (tid == 64) W8_T(4, 3);
         // every CTA's MMAs are done (its X ring is free) and its slices are staged
@@ -414,7 +443,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 #pragma unroll
             for (int it = 0; it < kMaxIt; ++it) {
                 const int u = tid - 64 + it * kConvWarps * 32;
-                const int mm = u / segs, seg = (u - mm * segs) * 8;
+                const int mm = u / seg_per_row, seg = (u - mm * seg_per_row) * 8;
                 const int n = nb + seg, m = m0 + mm;
                 if (u >= nunits || n >= p.N || !ok) continue;
                 float y[8];
@@ -462,6 +491,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     if (!ok) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
     tc_fence_before_sync();
     __syncthreads();
+#ifdef SFB_TRACE
+    tl_record(p.tl, p.tl_launch, kSplit ? 2 : 1, cta_t0, tl_t1);
+#endif
     if (warp == 0) {
         tc_fence_after_sync();
         tmem_dealloc(tmem, 256);
@@ -470,18 +502,23 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 
 using KernFn = void (*)(CUtensorMap, CUtensorMap, W8Params);
 
-inline KernFn pick(int act, bool split) {
-    static const KernFn t[3][2] = {
-        {w8a16_gemm_kernel<0, false>, w8a16_gemm_kernel<0, true>},
-        {w8a16_gemm_kernel<1, false>, w8a16_gemm_kernel<1, true>},
-        {w8a16_gemm_kernel<2, false>, w8a16_gemm_kernel<2, true>}};
-    return t[act][split ? 1 : 0];
+inline KernFn pick(int act, bool split, int tm) {
+    static const KernFn t[2][3][2] = {
+        {{w8a16_gemm_kernel<0, false, 128>, w8a16_gemm_kernel<0, true, 128>},
+         {w8a16_gemm_kernel<1, false, 128>, w8a16_gemm_kernel<1, true, 128>},
+         {w8a16_gemm_kernel<2, false, 128>, w8a16_gemm_kernel<2, true, 128>}},
+        {{w8a16_gemm_kernel<0, false, 64>, w8a16_gemm_kernel<0, true, 64>},
+         {w8a16_gemm_kernel<1, false, 64>, w8a16_gemm_kernel<1, true, 64>},
+         {w8a16_gemm_kernel<2, false, 64>, w8a16_gemm_kernel<2, true, 64>}}};
+    return t[tm == 64 ? 1 : 0][act][split ? 1 : 0];
 }
 
 }  // namespace w8
 
 #ifdef SFB_TRACE
 static unsigned long long* g_w8_trace = nullptr;
+static int g_w8_trace_launch = -1;        // trace only this timeline launch index (-1: every launch)
+extern "C" void sfb_debug_set_w8_trace_launch(int i) { g_w8_trace_launch = i; }
 extern "C" void sfb_debug_set_w8_trace(void* p) { g_w8_trace = static_cast<unsigned long long*>(p); }
 #endif
 
@@ -491,7 +528,7 @@ static int w8_max_clusters(const DeviceInfo& dev, int size) {
     static int cache[64][17] = {};
     int& slot = cache[dev.ordinal & 63][size & 15];
     if (slot != 0) return slot;
-    const w8::KernFn kern = w8::pick(0, true);        // the variants share their resource use
+    const w8::KernFn kern = w8::pick(0, true, 128);   // the variants share their resource use
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              w8::kSmemBytes) != cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed,
@@ -546,24 +583,35 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     p.kchunks = K / 64;
     // tokens per CTA: round up to 32, at most 256
     p.bn = M >= 256 ? 256 : ((M + 31) / 32) * 32;
-    const int ntile = (N + 127) / 128, mtile = (M + p.bn - 1) / p.bn;
+    const int mtile = (M + p.bn - 1) / p.bn;
+    // Split K across a cluster only when the tiles alone leave most SMs idle,
+    // and only as far as every cluster still fits in one wave: at one CTA per
+    // SM the GPCs hold fewer 8-CTA clusters than SMs / 8, and a cluster left
+    // over for a second wave doubles the kernel's time.
+    auto auto_splits = [&](int units) {
+        int sp = 1;
+        while (p.bn <= 128 && sp < 8 && units * sp * 2 <= dev.num_sms &&
+               p.kchunks / (sp * 2) >= 2 && units <= w8_max_clusters(dev, sp * 2))
+            sp *= 2;
+        return sp;
+    };
+    int tm = 128, ntile = (N + 127) / 128;
     int splits = num_splits;
     if (splits <= 0) {
-        // Split K across a cluster only when the tiles alone leave most SMs
-        // idle, and only as far as every cluster still fits in one wave: at one
-        // CTA per SM the GPCs hold fewer 8-CTA clusters than SMs / 8, and a
-        // cluster left over for a second wave doubles the kernel's time.
-        splits = 1;
-        const int units = ntile * mtile;
-        while (p.bn <= 128 && splits < 8 && units * splits * 2 <= dev.num_sms &&
-               p.kchunks / (splits * 2) >= 2 && units <= w8_max_clusters(dev, splits * 2))
-            splits *= 2;
+        splits = auto_splits(ntile * mtile);
+        // 64-channel tiles when 128-channel tiles cannot fill the GPU and the
+        // halved tile gives more CTAs (N = 2048 at 67 tokens: 32 tiles × 4
+        // splits instead of 16 × 4, 8-CTA clusters not fitting one wave)
+        const int ntile64 = (N + 63) / 64, s64 = auto_splits(ntile64 * mtile);
+        if (ntile * mtile * splits < dev.num_sms && ntile64 * mtile * s64 > ntile * mtile * splits) {
+            tm = 64; ntile = ntile64; splits = s64;
+        }
     }
     if (splits != 1 && splits != 2 && splits != 4 && splits != 8 && splits != 16) return SFB_ERR_INVALID;
     if (splits > 1 && p.bn > 128) return SFB_ERR_INVALID;
-    if (splits > p.kchunks) return SFB_ERR_INVALID;
+    if (splits > p.kchunks || splits > tm / 8) return SFB_ERR_INVALID;
     p.splits = splits;
-    p.stages = w8::num_stages(p.bn);
+    p.stages = w8::num_stages(p.bn, tm);
 
     CUtensorMap mx, mw;
     {
@@ -578,13 +626,13 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     {
         cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
         cuuint64_t str[1] = {(cuuint64_t)K};
-        cuuint32_t box[2] = {64, 128};
+        cuuint32_t box[2] = {64, (cuuint32_t)tm};
         cuuint32_t es[2] = {1, 1};
         int rc = encode_tensor_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w),
                                    dims, str, box, es, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc != SFB_OK) return rc;
     }
-    const w8::KernFn kern = w8::pick(act, p.splits > 1);
+    const w8::KernFn kern = w8::pick(act, p.splits > 1, tm);
     {
         static std::mutex mu;
         static std::vector<std::pair<int, w8::KernFn>> done;
@@ -604,7 +652,9 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
         }
     }
 #ifdef SFB_TRACE
-    p.trace = g_w8_trace;
+    p.tl = tl_buf();
+    p.tl_launch = tl_next();
+    p.trace = (g_w8_trace_launch < 0 || g_w8_trace_launch == p.tl_launch) ? g_w8_trace : nullptr;
 #endif
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.splits, ntile, mtile);
