@@ -71,6 +71,7 @@ struct AttnTcParams {
     const __nv_bfloat16* qn_w;       // per-head RMSNorm weight [64] applied to Q rows, or null
     const __nv_bfloat16* kn_w;       // the same for K rows, or null
     float    norm_eps;
+    int32_t  kv_stream;              // K/V read once per use (a per-tick cache): L2 evict-first
 #ifdef SFB_TRACE
     unsigned long long* trace;
     int dbg_skip;                    // timing experiments only: return at once
@@ -84,7 +85,7 @@ namespace attn_tc {
 #ifdef SFB_TRACE
 #define SFB_T(i) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && \
                           (threadIdx.x == 0 || threadIdx.x == 128 || threadIdx.x == 352)) { \
-        p.trace[(threadIdx.x == 352 ? 2 : threadIdx.x / 128) * 170 + (i)] = clock64(); } } while (0)
+        p.trace[(threadIdx.x == 352 ? 2 : threadIdx.x / 128) * 170 + (i)] = ptx::global_timer_ns(); } } while (0)
 #else
 #define SFB_T(i) do { } while (0)
 #endif
@@ -108,10 +109,12 @@ constexpr int kMergeBytes = kMergeRows * (2 * kOStride + 2) * 4;
 constexpr int kOffBar    = kOffMerge + kMergeBytes;
 constexpr int kOffTmem   = kOffBar + 8 * 40;
 constexpr int kOffRed    = kOffTmem + 16;                   // float [2 groups][m|l][128]
-constexpr int kSmemUsed  = kOffRed + 2 * 2 * 128 * 4;
+constexpr int kOffNormW  = (kOffRed + 2 * 2 * 128 * 4 + 15) & ~15;   // bf16 q/k norm weights [2][64]
+constexpr int kSmemUsed  = kOffNormW + 2 * 64 * 2;
 constexpr int kSmemBytes = kSmemUsed + 1024;                // + alignment slack
 constexpr int kTmemCols  = 512;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kOffNormW % 16 == 0 && kOffQ % 1024 == 0 && kOffStage % 1024 == 0, "vector/TMA alignment");
 static_assert(kOffBar % 8 == 0, "barrier alignment");
 
 // barrier indices
@@ -132,7 +135,7 @@ static_assert(kNumBars <= 40, "barrier area");
 // place: x · 1/sqrt(mean(x²) + eps) · w, fp32 math, bf16 result. The sum of
 // squares is formed as 8 per-chunk partials combined pairwise, the order of
 // the standalone per-head RMSNorm kernel, so both give identical bits.
-__device__ __forceinline__ void norm_row_sw128(uint8_t* tile, int r, const __nv_bfloat16* w, float eps) {
+__device__ __forceinline__ void norm_row_sw128(uint8_t* tile, int r, const __nv_bfloat16* w_smem, float eps) {
     uint4 c[8];
     float part[8];
 #pragma unroll
@@ -151,7 +154,7 @@ __device__ __forceinline__ void norm_row_sw128(uint8_t* tile, int r, const __nv_
     const float inv = 1.f / sqrtf(ss / 64.f + eps);
 #pragma unroll
     for (int lc = 0; lc < 8; ++lc) {
-        const uint4 gu = *reinterpret_cast<const uint4*>(w + lc * 8);
+        const uint4 gu = *reinterpret_cast<const uint4*>(w_smem + lc * 8);
         const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&gu);
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&c[lc]);
 #pragma unroll
@@ -272,6 +275,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         tmem_alloc(tmem_holder, kTmemCols);
         tmem_relinquish();
     }
+    // the q/k norm weights (constant parameters) staged in shared memory
+    __nv_bfloat16* norm_w = reinterpret_cast<__nv_bfloat16*>(smem + kOffNormW);
+    if (warp == 1 && lane < 16) {
+        const __nv_bfloat16* src = lane < 8 ? p.qn_w : p.kn_w;
+        if (src != nullptr)
+            reinterpret_cast<uint4*>(norm_w)[lane] = reinterpret_cast<const uint4*>(src)[lane & 7];
+    }
     tc_fence_before_sync();
     __syncthreads();
     tc_fence_after_sync();
@@ -295,7 +305,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 
     bool ok = true;
     auto wait = [&](int bar, uint32_t parity) {
-        if (!mbar_wait(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
+        if (!mbar_wait_spin(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
     };
 
     const int win = warp & 3;            // 32-lane window = row block
@@ -309,7 +319,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     // V-conversion warps below.
     if (p.qn_w != nullptr && warp < 4 && ntl > 0) {
         wait(kBarQ, 0);
-        norm_row_sw128(sQ, row, p.qn_w, p.norm_eps);
+        norm_row_sw128(sQ, row, norm_w, p.norm_eps);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[kBarQn]);
@@ -323,14 +333,21 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (ntl > 0) {
             constexpr uint32_t idS  = idesc_f16(128, 128, kFmtQK, 0, 0);  // Q·Kᵀ, both K-major
             constexpr uint32_t idPV = idesc_f16(128, 64, 0, 0, 1);        // P(tmem)·V(MN-major), fp16
+            // a static K/V cache is streamed once per use: evict-first in L2
+            const uint64_t kvpol = l2_evict_first_policy();
             auto issue_kv = [&](int t) {
                 const int s = t % kStages;
                 const int key0 = (t_begin + t) * kTileKeys;
                 if (elect_one()) {
                     mbar_arrive_expect_tx(&bars[bar_k(s)], kTileBytes);
-                    tma_load_4d(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b);
                     mbar_arrive_expect_tx(&bars[bar_v(s)], kTileBytes);
-                    tma_load_4d(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b);
+                    if (p.kv_stream) {
+                        tma_load_4d_hint(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b, kvpol);
+                        tma_load_4d_hint(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b, kvpol);
+                    } else {
+                        tma_load_4d(sK(s), &tmK, &bars[bar_k(s)], 0, key0, hk, b);
+                        tma_load_4d(sV(s), &tmV, &bars[bar_v(s)], 0, key0, hk, b);
+                    }
                 }
                 __syncwarp();
             };
@@ -370,8 +387,16 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 tma_load_4d(sQ, &tmQ, &bars[kBarQ], 0, q0, h, b);
             }
             __syncwarp();
+            SFB_T(150);
             int nL = min(kStages, ntl);                // tiles whose K/V load is issued
             for (int t = 0; t < nL; ++t) issue_kv(t);
+            SFB_T(151);
+#ifdef SFB_TRACE
+            wait(kBarQ, 0);
+            SFB_T(152);
+            wait(bar_k(0), 0);
+            SFB_T(153);
+#endif
             wait(p.qn_w ? kBarQn : kBarQ, 0);
             // Event loop. P·V completions are retired in issue order, so every
             // parity probe is at most one phase behind its barrier.
@@ -451,7 +476,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             if (p.kn_w != nullptr) {
                 wait(bar_k(s), (t / kStages) & 1);
                 for (int r = ct; r < kTileKeys; r += kConvWarps * 32)
-                    norm_row_sw128(sK(s), r, p.kn_w, p.norm_eps);
+                    norm_row_sw128(sK(s), r, norm_w + 64, p.norm_eps);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars[bar_kn(s)]);
@@ -726,6 +751,8 @@ static unsigned long long* g_trace_ptr = nullptr;
 extern "C" void sfb_debug_set_trace(void* p) { g_trace_ptr = static_cast<unsigned long long*>(p); }
 extern "C" void sfb_debug_set_timeline(void* p) { tl_buf() = static_cast<unsigned long long*>(p); tl_count() = 0; }
 static int g_attn_skip = 0;
+static int g_attn_trace_launch = -1;
+extern "C" void sfb_debug_set_attn_trace_launch(int i) { g_attn_trace_launch = i; }
 extern "C" void sfb_debug_set_attn_skip(int s) { g_attn_skip = s; }
 #endif
 
@@ -777,11 +804,12 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnO
     p.qn_w = static_cast<const __nv_bfloat16*>(o.qn_w);
     p.kn_w = static_cast<const __nv_bfloat16*>(o.kn_w);
     p.norm_eps = o.norm_eps;
+    p.kv_stream = o.v_f16 ? 1 : 0;   // the model's cross-attention cache
     if ((o.qn_w || o.kn_w) && (a.dtype != SFB_BF16 || a.head_dim != 64)) return SFB_ERR_DTYPE;
 #ifdef SFB_TRACE
-    p.trace = g_trace_ptr;
     p.tl = tl_buf();
     p.tl_launch = tl_next();
+    p.trace = (g_attn_trace_launch < 0 || g_attn_trace_launch == p.tl_launch) ? g_trace_ptr : nullptr;
     p.dbg_skip = g_attn_skip;
 #endif
     const int units = a.batch * a.heads * p.qtiles;

@@ -192,10 +192,11 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         // The int8 weights of the first stages are constant and are fetched
         // before waiting for the previous kernel; activations after.
         const int pre = min(nch, nst);
+        const uint64_t wpol = l2_evict_first_policy();   // weights are read once per step
         if (elect_one()) {
             for (int c = 0; c < pre; ++c) {
                 mbar_arrive_expect_tx(&bars[bar_full_w(c)], kWB);
-                tma_load_2d(sW(c), &tmW, &bars[bar_full_w(c)], kchunk(c) * 64, n0);
+                tma_load_2d_hint(sW(c), &tmW, &bars[bar_full_w(c)], kchunk(c) * 64, n0, wpol);
             }
         }
         __syncwarp();
@@ -210,7 +211,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                 const int k0 = kchunk(c) * 64;
                 if (c >= nst) {
                     mbar_arrive_expect_tx(&bars[bar_full_w(s)], kWB);
-                    tma_load_2d(sW(s), &tmW, &bars[bar_full_w(s)], k0, n0);
+                    tma_load_2d_hint(sW(s), &tmW, &bars[bar_full_w(s)], k0, n0, wpol);
                 }
                 mbar_arrive_expect_tx(&bars[bar_full_x(s)], xbytes);
                 tma_load_2d(sX(s), &tmX, &bars[bar_full_x(s)], k0, m0);
