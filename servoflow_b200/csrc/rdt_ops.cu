@@ -68,6 +68,54 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
     }
 }
 
+// rms_norm for D = 32·8·kC (kC 16-byte chunks per lane): the constant weight
+// is read before the dependency wait and the row is kept in registers, so the
+// kernel's critical path is one load of x, the reduction and the store. Same
+// operation order as rms_norm_kernel (identical results).
+template <int kC>
+__global__ void rms_norm_reg_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                    int64_t ldo, int rows, float eps) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    uint4 g[kC];
+#pragma unroll
+    for (int i = 0; i < kC; ++i) g[i] = *reinterpret_cast<const uint4*>(w + (i * 32 + lane) * 8);
+    pdl_trigger();
+    pdl_wait();
+    if (warp >= rows) return;
+    const __nv_bfloat16* xr = x + warp * ldx;
+    uint4 u[kC];
+#pragma unroll
+    for (int i = 0; i < kC; ++i) u[i] = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(h[k]);
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.f / sqrtf(ss / static_cast<float>(kC * 256) + eps);
+    __nv_bfloat16* orow = out + warp * ldo;
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
+        const __nv_bfloat162* gw = reinterpret_cast<const __nv_bfloat162*>(&g[i]);
+        uint4 r;
+        __nv_bfloat162* ro = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(h[k]), gg = __bfloat1622float2(gw[k]);
+            ro[k] = __floats2bfloat162_rn(f.x * inv * gg.x, f.y * inv * gg.y);
+        }
+        *reinterpret_cast<uint4*>(orow + (i * 32 + lane) * 8) = r;
+    }
+}
+
 // In place: for each token row and each head h in [0, heads), the 64 values at
 // x[row·ld + h·64 ...] are RMS-normalised with weight w[64]. 8 threads per head.
 __global__ void head_rms_norm_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int rows, int heads,
@@ -252,11 +300,17 @@ int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_
     if (D % 256 != 0 || (ldx % 8) || (ldo % 8)) return SFB_ERR_SHAPE;
     if (rows <= 0) return SFB_OK;
     const int warps_per_block = 4;
+    const unsigned grid = (rows + warps_per_block - 1) / warps_per_block;
+    if (D == 2048) {
+        prefer_max_shared(rdt::rms_norm_reg_kernel<8>);
+        return launch_kernel(rdt::rms_norm_reg_kernel<8>, grid, 32 * warps_per_block, 0, s, true,
+                             static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+                             static_cast<__nv_bfloat16*>(out), ldo, rows, eps);
+    }
     prefer_max_shared(rdt::rms_norm_kernel);
-    return launch_kernel(rdt::rms_norm_kernel, (rows + warps_per_block - 1) / warps_per_block,
-                         32 * warps_per_block, 0, s, true, static_cast<const __nv_bfloat16*>(x), ldx,
-                         static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), ldo, rows,
-                         D, eps);
+    return launch_kernel(rdt::rms_norm_kernel, grid, 32 * warps_per_block, 0, s, true,
+                         static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+                         static_cast<__nv_bfloat16*>(out), ldo, rows, D, eps);
 }
 
 int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w, float eps,
