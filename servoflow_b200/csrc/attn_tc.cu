@@ -305,7 +305,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 
     bool ok = true;
     auto wait = [&](int bar, uint32_t parity) {
-        if (!mbar_wait_spin(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
+        if (!mbar_wait(&bars[bar], parity, ok ? 1000000000ull : 0ull)) ok = false;
     };
 
     const int win = warp & 3;            // 32-lane window = row block
