@@ -312,6 +312,39 @@ def attention_roofline(be, dev, reps, sets=8):
     return nbytes, flops, float(np.median(per)), float(np.min(per)), 5 * reps + 2 * sets
 
 
+def serving(dev, rank, batches, sessions=32):
+    """Config 5 on this GPU: `sessions` independent robot sessions batched in one
+    model (M = 32 · 67 tokens per projection), full 5-step denoise per batch;
+    returns per-batch device latencies (ms)."""
+    import torch
+    from servoflow_b200.rdt1b import RDT1B, default_config
+    model = RDT1B(default_config(max_sessions=sessions), seed=3000 + rank)
+    g = torch.Generator().manual_seed(4000 + rank)
+    lang = torch.randn(sessions, LANG_LEN, 4096, generator=g).bfloat16().to(dev)
+    lens = torch.randint(8, LANG_LEN + 1, (sessions,), generator=g, dtype=torch.int32).to(dev)
+    img = torch.randn(sessions, IMG_LEN, 1152, generator=g).bfloat16().to(dev)
+    state = torch.randn(sessions, 128, generator=g).bfloat16().to(dev)
+    noise = torch.randn(sessions, HORIZON, ACTION, generator=g).to(dev)
+    actions = torch.empty_like(noise)
+    model.encode(lang, lens, img, state)
+    del lang, img
+    for _ in range(3):
+        model.sample(noise, actions)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    st = [torch.cuda.Event(enable_timing=True) for _ in range(batches)]
+    en = [torch.cuda.Event(enable_timing=True) for _ in range(batches)]
+    for i in range(batches):
+        st[i].record(stream)
+        model.sample(noise, actions)
+        en[i].record(stream)
+    torch.cuda.synchronize()
+    assert torch.isfinite(actions).all()
+    ms = [a.elapsed_time(b) for a, b in zip(st, en)]
+    model.close()
+    return ms
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -319,6 +352,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-serving", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -405,6 +439,7 @@ def main():
     assert torch.isfinite(act_h).all()
 
     gemm_bytes, gemm_s, gemm_launches = gemm_roofline(model, dev, reps=5)
+    serve_ms = [0.0] if args.no_serving else serving(dev, rank, batches=max(3, min(args.steps, 10)))
     at_bytes, at_flops, at_med, at_min, at_launches = attention_roofline(be, dev, reps=64)
     assert be.device_error() == 0
 
@@ -412,11 +447,12 @@ def main():
     e2e_ms = np.array([s.elapsed_time(e) for s, e in zip(e_st, e_en)])
     tick_ms = np.array([s.elapsed_time(e) for s, e in zip(t_st, t_en)])
     stats = torch.tensor([np.median(ms), np.mean(ms), np.percentile(ms, 99), np.median(e2e_ms),
-                          np.median(tick_ms), gemm_s, at_med, at_min],
+                          np.median(tick_ms), gemm_s, at_med, at_min, np.median(serve_ms),
+                          np.percentile(serve_ms, 99)],
                          dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_med, at_min = stats.tolist()
+    p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_med, at_min, sv_p50, sv_p99 = stats.tolist()
 
     if rank == 0:
         hbm, tflops, kind = peaks()
@@ -461,6 +497,14 @@ def main():
                     "d2h_bytes_per_step": act_h.numel() * 4,
                     "path": "RDT1B.sample_host -> sfb_rdt1b_sample: pinned host noise -> device, "
                             "graph replay, actions -> pinned host, all inside the timed region"},
+            "serving": None if args.no_serving else {
+                "what": "config 5: 32 independent sessions per GPU batched in one model, full 5-step "
+                        "denoise per batch (graph), sharded by session, no collective",
+                "sessions_per_gpu": 32, "sessions_total": 32 * world,
+                "batch_p50_ms": sv_p50, "batch_p99_ms": sv_p99,
+                "per_session_p99_ms": sv_p99,
+                "actions_per_s": world * 32 * HORIZON * 1e3 / sv_p50,
+                "chunks_per_s": world * 32 * 1e3 / sv_p50},
             "gpu_launches": kernels_per_step * args.steps * world,
             "gpu_launches_note": f"{kernels_per_step} kernels per denoise graph x {args.steps} timed steps "
                                  f"x {world} GPU(s) "

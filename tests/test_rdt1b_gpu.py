@@ -94,3 +94,27 @@ def test_masked_language_tokens_do_not_matter(setup):
     assert torch.equal(a[0], b[0])
     m.encode(s["lang"].to(s["dev"]), s["lens"].to(s["dev"]), s["img"].to(s["dev"]), s["state"].to(s["dev"]))
     torch.cuda.synchronize()
+
+
+def test_sessions_are_independent(setup):
+    # session 1's actions do not depend on session 0's inputs (same batch, same bits)
+    s = setup
+    m = s["model"]
+    dev = s["dev"]
+    noise = s["noise"].to(dev)
+    a = torch.empty_like(noise)
+    b = torch.empty_like(noise)
+    m.sample(noise, a)
+    lang2, img2, state2 = s["lang"].clone(), s["img"].clone(), s["state"].clone()
+    g = torch.Generator().manual_seed(7)
+    lang2[0] = torch.randn(lang2.shape[1:], generator=g).bfloat16()
+    img2[0] = torch.randn(img2.shape[1:], generator=g).bfloat16()
+    state2[0] = torch.randn(state2.shape[1:], generator=g).bfloat16()
+    noise2 = noise.clone()
+    noise2[0] = torch.randn(noise.shape[1:], generator=g).to(dev)
+    m.encode(lang2.to(dev), s["lens"].to(dev), img2.to(dev), state2.to(dev))
+    m.sample(noise2, b)
+    torch.cuda.synchronize()
+    assert torch.equal(a[1], b[1]) and not torch.equal(a[0], b[0])
+    m.encode(s["lang"].to(dev), s["lens"].to(dev), s["img"].to(dev), s["state"].to(dev))
+    torch.cuda.synchronize()
