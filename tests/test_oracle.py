@@ -114,3 +114,36 @@ def test_dequant_fp16_rounding_is_reference_hmul():
     out = oracle.dequant_int8(q, s, round_mode=1)
     exact = q.astype(np.float64) * s[:, None].astype(np.float64)
     assert np.array_equal(out, exact.astype(np.float16).astype(np.float32))
+
+
+def test_rdt1b_oracle_matches_reference_model():
+    """oracle/rdt1b_ref.RefRDT against the reference's own PyTorch RDT-1B
+    (tests/alignment/test_rdt1b_alignment.py:73-210 in the reference), run by
+    tests/golden/make_rdt1b_golden.py on seeded weights and inputs: full
+    language length (no masking), fp32."""
+    import importlib.util
+    from types import SimpleNamespace
+    from oracle.rdt1b_ref import RefRDT
+
+    spec = importlib.util.spec_from_file_location(
+        "make_rdt1b_golden", os.path.join(GOLDEN, "make_rdt1b_golden.py"))
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    g = np.load(os.path.join(GOLDEN, "rdt1b_small.npz"))
+    x = gen.inputs()
+    for k in ("lang", "img", "state", "noisy"):
+        assert np.array_equal(x[k].numpy(), g[k])      # the seeded inputs regenerate exactly
+    c = gen.CFG
+    cfg = SimpleNamespace(hidden=c["hidden_size"], heads=c["num_heads"], num_layers=c["depth"],
+                          ctrl_freq=int(g["freq"]))
+    w = gen.weights()
+    w["x_pos_embed"] = w["x_pos_embed"][0]
+    w["lang_cond_pos_embed"] = w["lang_cond_pos_embed"][0]
+    w["img_cond_pos_embed"] = w["img_cond_pos_embed"][0]
+    m = RefRDT(w, cfg)
+    with torch.no_grad():
+        lang_c, img_c = m.encode(x["lang"], x["img"])
+        lang_len = torch.tensor([x["lang"].shape[1]])
+        out = m.forward(lang_c, img_c, lang_len, x["state"][:, 0], x["noisy"], int(g["t"]))
+    assert out.shape == g["out"].shape
+    np.testing.assert_allclose(out.numpy(), g["out"], rtol=0, atol=1e-5)
