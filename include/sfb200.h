@@ -33,6 +33,7 @@ extern "C" {
 #define SFB_ERR_CUDA          -8  /* other CUDA runtime error               */
 #define SFB_ERR_DEVICE_TIMEOUT -9 /* a bounded device-side wait expired     */
 #define SFB_ERR_RANGE        -10  /* input outside the kernel's value range */
+#define SFB_ERR_IO           -11  /* file missing, unreadable or malformed  */
 
 /* ── dtype codes (== sf::DType, reference dtype.h:11-19) ──────────────────── */
 #define SFB_F32   0
@@ -231,6 +232,59 @@ int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, 
 /* The sampler's timesteps and per-step update x ← a·x + b·x0 + c·x0_prev. */
 int sfb_rdt1b_schedule(void* handle, float* timesteps, float* coef_a, float* coef_b, float* coef_c,
                        int32_t n);
+
+/* ── checkpoints (setup time; host code except the uploads) ──────────────────
+ * A tensor entry of a .safetensors file: replaces SafeTensorsLoader::TensorMeta
+ * (reference include/servoflow/loader/safetensors.h:46-52). dtype is an SFB
+ * code (4 = packed int4); offsets are relative to the data section. */
+typedef struct sfb_tensor_info {
+    char     name[256];
+    int32_t  dtype;
+    int32_t  ndim;
+    int64_t  shape[8];
+    uint64_t data_begin;
+    uint64_t data_end;
+} sfb_tensor_info;
+
+/* Lists the tensors of a safetensors file sorted by name, without reading
+ * their data: replaces SafeTensorsLoader::inspect (safetensors.h:53,
+ * src/loader/safetensors.cpp:65-108). Writes min(capacity, *count) entries;
+ * *count is the total; *data_offset (optional) = 8 + header length. Errors as
+ * the reference's parse_header: SFB_ERR_IO for a short file, a header past the
+ * end or malformed JSON; SFB_ERR_DTYPE for a dtype outside F32, F16, BF16, I8,
+ * I4, I32, BOOL. Needs no GPU. */
+int sfb_safetensors_inspect(const char* path, sfb_tensor_info* out, int32_t capacity, int32_t* count,
+                            uint64_t* data_offset);
+/* The reference converter's weight-name mapping (remap_key, tools/convert/
+ * hf_to_servoflow.py:41-66): returns 1 and writes the ServoFlow name, or 0 for
+ * an entry the converter drops (EMA shadows, optimizer/scheduler state, other
+ * modules). Needs no GPU. */
+int sfb_checkpoint_key(const char* hf_name, char* out, int32_t out_len);
+/* Fills *cfg from a checkpoint's config.json (RDT1BConfig::from_json,
+ * src/models/rdt1b/config.cpp:10-66: the converter's flat keys and the HF
+ * nested "rdt"/"noise_scheduler" keys over the defaults). max_sessions stays 1.
+ * SFB_ERR_UNSUPPORTED for num_train_timesteps != 1000, freq_dim != 256 or
+ * rms_norm_eps != 1e-6, which this runtime fixes. Needs no GPU. */
+int sfb_rdt1b_config_from_json(const char* path, sfb_rdt1b_config* cfg);
+/* Writes the model parameters one safetensors file provides. Names are taken
+ * as stored or mapped as sfb_checkpoint_key does. A float "<linear>.weight"
+ * [N, K] is quantised on the device into "<linear>.weight_q" (int8) and
+ * "<linear>.weight_scale" (fp32 [N]): s = max|row| / 127 (1 for a zero row),
+ * q = clamp(round-half-even(w / s), -127, 127). Other tensors are copied, or
+ * converted to the parameter's dtype (round-to-nearest-even), as
+ * load_weight_from_map does (src/loader/safetensors.cpp:156-183). *loaded
+ * counts the tensors written, *ignored the entries that name no parameter.
+ * Allocates a staging buffer and synchronises the device: setup time only.
+ * The K/V cache is stale until the next sfb_rdt1b_encode. */
+int sfb_rdt1b_load_safetensors(void* handle, const char* path, int64_t* loaded, int64_t* ignored);
+/* Loads every *.safetensors file of a checkpoint directory (name order; the
+ * first file providing a parameter keeps it), as RDT1BModel::load_weights
+ * (src/models/rdt1b/rdt1b.cpp:97-111). Fails (SFB_ERR_INVALID, message in
+ * sfb_last_error) when a model parameter is missing from every file. */
+int sfb_rdt1b_load_checkpoint(void* handle, const char* dir, int64_t* loaded, int64_t* ignored);
+/* Parameters not written by any load since create (seeded values remain);
+ * the first one's name goes to first_missing (optional). */
+int sfb_rdt1b_params_missing(void* handle, int64_t* missing, char* first_missing, int32_t buflen);
 
 #ifdef __cplusplus
 }  /* extern "C" */

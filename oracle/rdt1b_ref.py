@@ -50,6 +50,19 @@ def dpm_schedule(num_steps: int, train_steps: int = 1000):
     return ts, a, b, c
 
 
+def quantize_rows_int8(w: np.ndarray):
+    """Per-output-channel symmetric int8 quantisation of a [N, K] float
+    weight, the scheme whose dequantisation q·s is the reference's
+    dequantize_int8 (src/backend/cuda/ops/quantization.cu:18-50): in fp32,
+    s = max_k |w| / 127 (1 for an all-zero row), q = clip(rint(w / s), ±127)
+    with rint rounding half to even. Returns (q int8 [N, K], s float32 [N])."""
+    w = np.asarray(w, dtype=np.float32)
+    mx = np.abs(w).max(axis=1)
+    s = np.where(mx > 0, mx / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(w / s[:, None]), -127, 127).astype(np.int8)
+    return q, s
+
+
 def rms_norm(x, w, eps=1e-6):
     return x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
 

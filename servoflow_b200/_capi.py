@@ -24,6 +24,7 @@ SFB_ERR_UNSUPPORTED = -7
 SFB_ERR_CUDA = -8
 SFB_ERR_DEVICE_TIMEOUT = -9
 SFB_ERR_RANGE = -10
+SFB_ERR_IO = -11
 
 SFB_F32, SFB_F16, SFB_BF16, SFB_I8, SFB_I32, SFB_BOOL = 0, 1, 2, 3, 5, 6
 
@@ -60,12 +61,12 @@ class AttnArgs(ctypes.Structure):
 class SfbError(RuntimeError):
     """A non-zero status returned through the C ABI."""
 
-    def __init__(self, status: int, what: str):
+    def __init__(self, status: int, what: str, detail: bool = False):
         self.status = status
-        detail = ""
-        if status in (SFB_ERR_LAUNCH, SFB_ERR_CUDA):
-            detail = " — " + lib().sfb_last_error().decode()
-        super().__init__(f"{what}: {status_string(status)} (status {status}){detail}")
+        extra = ""
+        if detail or status in (SFB_ERR_LAUNCH, SFB_ERR_CUDA, SFB_ERR_IO):
+            extra = " — " + lib().sfb_last_error().decode()
+        super().__init__(f"{what}: {status_string(status)} (status {status}){extra}")
 
 
 _lib = None
@@ -119,6 +120,8 @@ def status_string(status: int) -> str:
     return lib().sfb_status_string(int(status)).decode()
 
 
-def check(status: int, what: str) -> None:
+def check(status: int, what: str, detail: bool = False) -> None:
+    """Raises SfbError for a non-zero status; detail=True appends the library's
+    message for the call (calls that record one on every failure)."""
     if status != SFB_OK:
-        raise SfbError(status, what)
+        raise SfbError(status, what, detail)

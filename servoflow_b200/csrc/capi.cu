@@ -30,6 +30,7 @@ const char* sfb_status_string(int status) {
         case SFB_ERR_CUDA:           return "CUDA runtime error";
         case SFB_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
         case SFB_ERR_RANGE:          return "input value outside the kernel's supported range";
+        case SFB_ERR_IO:             return "file missing, unreadable or malformed";
         default:                     return "unknown status";
     }
 }

@@ -28,6 +28,7 @@
 // Weights are random (seeded, generated on the device); the same tensors are
 // readable through sfb_rdt1b_param so a test can run the CPU oracle on them.
 #include <map>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -108,6 +109,7 @@ struct Model {
     int device = 0;
     std::vector<void*> allocs;
     std::map<std::string, std::pair<void*, std::pair<int64_t, int32_t>>> params;
+    std::set<std::string> loaded;             // parameters written from a checkpoint
     uint64_t seed = 0, counter = 0;
 
     Linear lang0, lang2, img0, img2, st0, st2, st4, t0, t2, f0, f2, fin1, fin2;

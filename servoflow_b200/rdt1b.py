@@ -36,8 +36,15 @@ def _declare(lib):
     lib.sfb_rdt1b_schedule.argtypes = [c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p,
                                        c.c_int32]
     lib.sfb_rdt1b_graph_kernels.argtypes = [c.c_void_p, c.c_int32, c.POINTER(c.c_int64)]
+    lib.sfb_rdt1b_config_from_json.argtypes = [c.c_char_p, c.POINTER(RDT1BConfig)]
+    lib.sfb_rdt1b_load_safetensors.argtypes = [c.c_void_p, c.c_char_p, c.POINTER(c.c_int64),
+                                               c.POINTER(c.c_int64)]
+    lib.sfb_rdt1b_load_checkpoint.argtypes = [c.c_void_p, c.c_char_p, c.POINTER(c.c_int64),
+                                              c.POINTER(c.c_int64)]
+    lib.sfb_rdt1b_params_missing.argtypes = [c.c_void_p, c.POINTER(c.c_int64), c.c_char_p, c.c_int32]
     for f in ("default_config", "create", "destroy", "encode", "forward", "sample", "param",
-              "schedule", "graph_kernels"):
+              "schedule", "graph_kernels", "config_from_json", "load_safetensors", "load_checkpoint",
+              "params_missing"):
         getattr(lib, "sfb_rdt1b_" + f).restype = c.c_int
     lib._rdt_declared = True
 
@@ -123,6 +130,30 @@ class RDT1B:
         torch.cuda.synchronize()
         _copy_d2d(out.data_ptr(), ptr.value, n.value * out.element_size())
         return out
+
+    def load_safetensors(self, path: str):
+        """Writes the parameters one .safetensors file provides (float
+        projection weights are quantised to int8 per output channel on the
+        device); returns (tensors loaded, entries ignored)."""
+        loaded, ignored = ctypes.c_int64(), ctypes.c_int64()
+        _capi.check(self.lib.sfb_rdt1b_load_safetensors(self.h, str(path).encode(), ctypes.byref(loaded),
+                                                        ctypes.byref(ignored)), f"load {path}", detail=True)
+        return loaded.value, ignored.value
+
+    def load_checkpoint(self, checkpoint_dir: str):
+        """Loads every *.safetensors of a checkpoint directory; raises if a
+        model parameter is in none of them. Returns (loaded, ignored)."""
+        loaded, ignored = ctypes.c_int64(), ctypes.c_int64()
+        _capi.check(self.lib.sfb_rdt1b_load_checkpoint(self.h, str(checkpoint_dir).encode(),
+                                                       ctypes.byref(loaded), ctypes.byref(ignored)),
+                    f"load checkpoint {checkpoint_dir}", detail=True)
+        return loaded.value, ignored.value
+
+    def params_missing(self):
+        """(number of parameters no load has written, the first one's name)."""
+        n, buf = ctypes.c_int64(), ctypes.create_string_buffer(256)
+        _capi.check(self.lib.sfb_rdt1b_params_missing(self.h, ctypes.byref(n), buf, 256), "params_missing")
+        return n.value, buf.value.decode()
 
     def schedule(self):
         n = self.cfg.num_steps
