@@ -122,6 +122,8 @@ struct Model {
     std::vector<__nv_bfloat16*> kv;
     // step workspaces
     __nv_bfloat16 *x, *xn, *qkv, *attn, *h, *ain, *ah1, *ah2, *seq, *tsc, *fsc, *th, *temb, *fh, *femb;
+    // timestep embeddings of every sampling step, computed once per tick
+    __nv_bfloat16 *tsc_all, *th_all, *temb_all;
     float *yfin, *xact, *x0prev;
     // encode workspace
     __nv_bfloat16* enc_h;
@@ -272,6 +274,9 @@ static int create(Model& m) {
     SFB_TRY(bf(&m.seq, BT1 * D));
     SFB_TRY(bf(&m.tsc, 256)); SFB_TRY(bf(&m.fsc, 256)); SFB_TRY(bf(&m.th, D)); SFB_TRY(bf(&m.temb, D));
     SFB_TRY(bf(&m.fh, D)); SFB_TRY(bf(&m.femb, D));
+    SFB_TRY(bf(&m.tsc_all, static_cast<int64_t>(c.num_steps) * 256));
+    SFB_TRY(bf(&m.th_all, static_cast<int64_t>(c.num_steps) * D));
+    SFB_TRY(bf(&m.temb_all, static_cast<int64_t>(c.num_steps) * D));
     SFB_TRY(f32(&m.yfin, BS * A));
     SFB_TRY(f32(&m.xact, static_cast<int64_t>(B) * c.horizon * A));
     SFB_TRY(f32(&m.x0prev, static_cast<int64_t>(B) * c.horizon * A));
@@ -346,12 +351,28 @@ static int encode(Model& m, int B, const void* lang, const int32_t* lang_len, co
         // V is stored in fp16 (the attention's P·V operand type), converted once per tick
         SFB_TRY(bf16_to_f16_launch(m.kv[l] + D, 2 * D, rows, D, s));
     }
+    // Timestep embeddings of the sampler's steps and the control-frequency
+    // embedding (sincos → Linear → SiLU → Linear, rdt1b.cpp:305-320). They
+    // depend on the weights and the fixed schedule only, so they are made
+    // here once per tick, all steps in one projection (rows are computed
+    // independently: the same values as one row at a time), instead of
+    // six kernels inside every denoising step.
+    const int n = c.num_steps;
+    for (int i = 0; i < n; ++i)
+        SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, m.tsteps[i], 256, m.tsc_all + i * 256));
+    SFB_TRY(linear(m.t0, m.tsc_all, 256, n, m.th_all, D, 2, nullptr, 0, s));
+    SFB_TRY(linear(m.t2, m.th_all, D, n, m.temb_all, D, 0, nullptr, 0, s));
+    SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, static_cast<float>(c.ctrl_freq), 256, m.fsc));
+    SFB_TRY(linear(m.f0, m.fsc, 256, 1, m.fh, D, 2, nullptr, 0, s));
+    SFB_TRY(linear(m.f2, m.fh, D, 1, m.femb, D, 0, nullptr, 0, s));
     return SFB_OK;
 }
 
 // One denoising network evaluation (rdt1b.cpp:254-369, test_rdt1b_alignment.py:181-210)
 // on the current x_t (m.xact) at timestep t, leaving the x0 prediction in m.yfin.
-static int forward(Model& m, int B, float t, cudaStream_t s) {
+// step >= 0: sampling step `step` of the schedule (t == tsteps[step]), whose
+// timestep embedding encode() made; step < 0: any t, embedded here.
+static int forward(Model& m, int B, float t, cudaStream_t s, int step = -1) {
     const auto& c = m.c;
     const int D = c.hidden, S = m.S(), T = c.horizon, A = c.action_dim;
     const int M = B * S, Ma = B * (T + 1);
@@ -367,14 +388,19 @@ static int forward(Model& m, int B, float t, cudaStream_t s) {
     SFB_TRY(linear(m.st2, m.ah1, D, Ma, m.ah2, D, 1, nullptr, 0, s));
     SFB_TRY(linear(m.st4, m.ah2, D, Ma, m.seq, D, 0, nullptr, 0, s));
     // timestep and control-frequency embeddings: sincos → Linear → SiLU → Linear
-    SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, t, 256, m.tsc));
-    SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, static_cast<float>(c.ctrl_freq), 256, m.fsc));
-    SFB_TRY(linear(m.t0, m.tsc, 256, 1, m.th, D, 2, nullptr, 0, s));
-    SFB_TRY(linear(m.t2, m.th, D, 1, m.temb, D, 0, nullptr, 0, s));
-    SFB_TRY(linear(m.f0, m.fsc, 256, 1, m.fh, D, 2, nullptr, 0, s));
-    SFB_TRY(linear(m.f2, m.fh, D, 1, m.femb, D, 0, nullptr, 0, s));
+    const __nv_bfloat16* temb = m.temb;
+    if (step >= 0) {
+        temb = m.temb_all + static_cast<int64_t>(step) * D;      // and m.femb, both from encode()
+    } else {
+        SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, t, 256, m.tsc));
+        SFB_TRY(launch_kernel(rdt::sincos_kernel, 1, 128, 0, s, true, static_cast<float>(c.ctrl_freq), 256, m.fsc));
+        SFB_TRY(linear(m.t0, m.tsc, 256, 1, m.th, D, 2, nullptr, 0, s));
+        SFB_TRY(linear(m.t2, m.th, D, 1, m.temb, D, 0, nullptr, 0, s));
+        SFB_TRY(linear(m.f0, m.fsc, 256, 1, m.fh, D, 2, nullptr, 0, s));
+        SFB_TRY(linear(m.f2, m.fh, D, 1, m.femb, D, 0, nullptr, 0, s));
+    }
     SFB_TRY(launch_kernel(rdt::assemble_x_kernel, grid_for(static_cast<int64_t>(M) * D / 8, 256), 256, 0, s, true,
-        m.temb, m.femb, m.seq, m.x_pos, m.x, B, S, D));
+        temb, m.femb, m.seq, m.x_pos, m.x, B, S, D));
 
     for (int l = 0; l < c.num_layers; ++l) {
         const Block& bl = m.blocks[l];
@@ -412,7 +438,7 @@ static int sample_loop(Model& m, int B, cudaStream_t s) {
     const auto& c = m.c;
     const int64_t n = static_cast<int64_t>(B) * c.horizon * c.action_dim;
     for (int i = 0; i < c.num_steps; ++i) {
-        SFB_TRY(forward(m, B, m.tsteps[i], s));
+        SFB_TRY(forward(m, B, m.tsteps[i], s, i));
         SFB_TRY(launch_kernel(rdt::dpm_update_kernel, grid_for(n, 256), 256, 0, s, true,
             m.xact, m.yfin, m.x0prev, m.ca[i], m.cb[i], m.cc[i], B, c.horizon, c.action_dim, m.S()));
     }
