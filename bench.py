@@ -135,10 +135,9 @@ class ClockSampler:
 
 
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    from servoflow_b200.sessions import rank_env
+    r = rank_env()
+    return r.world, r.rank, r.local
 
 
 # ── CPU oracle timing (cpu_baseline and --impl reference) ─────────────────────
@@ -318,8 +317,10 @@ def serving(dev, rank, batches, sessions=32):
     returns per-batch device latencies (ms)."""
     import torch
     from servoflow_b200.rdt1b import RDT1B, default_config
-    model = RDT1B(default_config(max_sessions=sessions), seed=3000 + rank)
-    g = torch.Generator().manual_seed(4000 + rank)
+    from servoflow_b200.sessions import rank_env, session_ids, session_seed
+    first = session_ids(rank_env().world, rank, sessions).start     # this rank's global sessions
+    model = RDT1B(default_config(max_sessions=sessions), seed=session_seed(first, "serving"))
+    g = torch.Generator().manual_seed(session_seed(first, "serving") + 100000)
     lang = torch.randn(sessions, LANG_LEN, 4096, generator=g).bfloat16().to(dev)
     lens = torch.randint(8, LANG_LEN + 1, (sessions,), generator=g, dtype=torch.int32).to(dev)
     img = torch.randn(sessions, IMG_LEN, 1152, generator=g).bfloat16().to(dev)
@@ -376,9 +377,11 @@ def main():
     from servoflow_b200.rdt1b import RDT1B, default_config
     be = B200Backend(dev.index)
 
-    # one robot session per GPU: its own weights, condition and noise (seeded by rank)
-    model = RDT1B(default_config(max_sessions=1), seed=1000 + rank)
-    g = torch.Generator().manual_seed(2000 + rank)
+    # one robot session per GPU: its own weights, condition and noise (seeded by session)
+    from servoflow_b200.sessions import barrier, max_over_ranks, session_ids, session_seed
+    sid = session_ids(world, rank, 1)[0]
+    model = RDT1B(default_config(max_sessions=1), seed=session_seed(sid, "weights"))
+    g = torch.Generator().manual_seed(session_seed(sid, "inputs"))
     lang = torch.randn(1, LANG_LEN, 4096, generator=g).bfloat16().to(dev)
     lang_len = torch.randint(8, LANG_LEN + 1, (1,), generator=g, dtype=torch.int32).to(dev)
     img = torch.randn(1, IMG_LEN, 1152, generator=g).bfloat16().to(dev)
@@ -400,8 +403,7 @@ def main():
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     sampler = ClockSampler(dev.index)
     with sampler:
-        if world > 1:
-            dist.barrier()
+        barrier()
         torch.cuda.synchronize()
         t_wall = time.perf_counter()
         for i in range(args.steps):
@@ -409,8 +411,7 @@ def main():
             model.sample(noise, actions)
             ends[i].record(stream)
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        barrier()
         t_wall = time.perf_counter() - t_wall
 
         # end to end through the public call: pinned host noise in, host actions out
@@ -446,13 +447,10 @@ def main():
     ms = np.array([s.elapsed_time(e) for s, e in zip(starts, ends)])
     e2e_ms = np.array([s.elapsed_time(e) for s, e in zip(e_st, e_en)])
     tick_ms = np.array([s.elapsed_time(e) for s, e in zip(t_st, t_en)])
-    stats = torch.tensor([np.median(ms), np.mean(ms), np.percentile(ms, 99), np.median(e2e_ms),
-                          np.median(tick_ms), gemm_s, at_med, at_min, np.median(serve_ms),
-                          np.percentile(serve_ms, 99)],
-                         dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_med, at_min, sv_p50, sv_p99 = stats.tolist()
+    stats = max_over_ranks([np.median(ms), np.mean(ms), np.percentile(ms, 99), np.median(e2e_ms),
+                            np.median(tick_ms), gemm_s, at_med, at_min, np.median(serve_ms),
+                            np.percentile(serve_ms, 99)], device=dev)
+    p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_med, at_min, sv_p50, sv_p99 = stats
 
     if rank == 0:
         hbm, tflops, kind = peaks()
