@@ -198,10 +198,10 @@ def run_reference(args, world, rank):
     for i in range(args.warmup):
         s.block(i % 2)
     ts = []
-    for i in range(args.steps):                     # one block per step, alternating kinds
+    for i in range(args.steps):                     # one (language, image) block pair per step
         if ts and time.perf_counter() - t_start > budget:
             break
-        ts.append(s.block(i % 2) * LAYERS * STEPS * 1e3)
+        ts.append((s.block(0) + s.block(1)) * (LAYERS // 2) * STEPS * 1e3)
     p50 = float(np.median(ts))
     line = {
         "impl": "reference", "metric": METRIC, "value": p50, "unit": "ms", "n_gpus": world,
@@ -212,8 +212,8 @@ def run_reference(args, world, rank):
                                "lang 1024 masked / image 4374 cross-attention, cross K/V cached)",
                    "parallelism": f"host CPU, torch fp32, {s.threads} threads"},
         "cpu_baseline": {"value": p50, "unit": "ms", "cores": s.threads, "kind": "port",
-                         "sample": f"one RDT block per step (language and image alternating), "
-                                   f"time scaled x{LAYERS * STEPS} to 28 blocks x 5 steps; "
+                         "sample": f"one (language block + image block) pair per step, "
+                                   f"time scaled x{(LAYERS // 2) * STEPS} to 28 blocks x 5 steps; "
                                    "oracle/rdt1b_ref.py (the reference has no CPU backend)"},
         "e2e": {"value": p50, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
