@@ -490,7 +490,9 @@ def main():
                           "alg_bytes_per_launch": at_bytes,
                           "traffic": profiled_traffic("attn_fwd_tc_image_xattn.md"),
                           "l2": "64 launches back to back over 8 distinct K/V caches (286 MB > 2x L2): "
-                                "every launch reads its K/V from HBM; median of 5 batches"},
+                                "every launch reads its K/V from HBM; median of 5 batches",
+                          "launch": "sfb_attention_fwd, programmatic dependent launch: a launch's "
+                                    "barrier/TMEM setup overlaps the previous launch's tail"},
             "e2e": {"value": e2e_p50, "unit": "ms", "h2d_bytes_per_step": noise_h.numel() * 4,
                     "d2h_bytes_per_step": act_h.numel() * 4,
                     "path": "RDT1B.sample_host -> sfb_rdt1b_sample: pinned host noise -> device, "

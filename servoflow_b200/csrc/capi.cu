@@ -76,7 +76,15 @@ int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
     const bool tc = (a->dtype == SFB_F16 || a->dtype == SFB_BF16) && a->head_dim == 64;
     const bool v_f16 = a->v_dtype == SFB_F16 && a->dtype == SFB_BF16;
     if (v_f16 && !tc) return SFB_ERR_DTYPE;
-    return tc ? sfb::attention_tc_launch(*a, s, [&] { sfb::AttnOpts o; o.v_f16 = v_f16; return o; }()) : sfb::attention_simt_launch(*a, s);
+    return tc ? sfb::attention_tc_launch(*a, s, [&] {
+        // Programmatic dependent launch: before its dependency wait the kernel
+        // only sets up barriers and TMEM (no reads of q, k, v, kv_len, masks),
+        // so it may start while the stream's previous kernel finishes.
+        sfb::AttnOpts o;
+        o.v_f16 = v_f16;
+        o.pdl = true;
+        return o;
+    }()) : sfb::attention_simt_launch(*a, s);
 }
 
 int sfb_attention_bhsd(const void* q, const void* k, const void* v, void* out, int32_t batch,
