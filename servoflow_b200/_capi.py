@@ -65,7 +65,7 @@ class SfbError(RuntimeError):
         self.status = status
         extra = ""
         if detail or status in (SFB_ERR_LAUNCH, SFB_ERR_CUDA, SFB_ERR_IO):
-            extra = " — " + lib().sfb_last_error().decode()
+            extra = " — " + lib().sfb_last_error().decode("utf-8", errors="replace")   # may quote file bytes
         super().__init__(f"{what}: {status_string(status)} (status {status}){extra}")
 
 

@@ -51,7 +51,8 @@ def inspect(path: str) -> list:
     arr = (TensorInfo * max(1, count.value))()
     _capi.check(lib.sfb_safetensors_inspect(str(path).encode(), arr, count.value, ctypes.byref(count), None),
                 f"inspect {path}", detail=True)
-    return [dict(name=t.name.decode(), dtype=DTYPE_NAMES[t.dtype], shape=tuple(t.shape[:t.ndim]),
+    return [dict(name=t.name.decode("utf-8", errors="replace"), dtype=DTYPE_NAMES[t.dtype],
+                 shape=tuple(t.shape[:t.ndim]),
                  data_offsets=(t.data_begin, t.data_end)) for t in arr[:count.value]]
 
 

@@ -141,3 +141,54 @@ def test_quantizer_restatement():
     assert s[2] == 1 and not q[2].any()
     assert np.abs(q).max() == 127 and q[3, 5] == 127
     assert np.all(np.abs(q.astype(np.float32) * s[:, None] - w) <= s[:, None] / 2 + 1e-9)
+
+
+def test_inspect_survives_corrupted_headers(tmp_path):
+    """Truncated and byte-flipped copies of a valid file: the reader returns
+    OK or an error status, never crashes (it parses untrusted files)."""
+    import random
+    from safetensors.torch import save_file
+    save_file({"a.weight": torch.zeros(3, 4), "b": torch.ones(2, dtype=torch.int8)}, str(tmp_path / "ok.st"))
+    good = (tmp_path / "ok.st").read_bytes()
+    hlen = struct.unpack("<Q", good[:8])[0]
+    rng = random.Random(7)
+    bad = tmp_path / "bad.st"
+    for i in range(300):
+        b = bytearray(good)
+        kind = i % 3
+        if kind == 0:
+            b = b[: rng.randrange(0, 8 + hlen + 1)]
+        elif kind == 1:
+            for _ in range(rng.randrange(1, 4)):
+                b[rng.randrange(8, 8 + hlen)] = rng.randrange(256)
+        else:
+            b[:8] = struct.pack("<Q", rng.choice([0, 1, hlen - 1, hlen + 1, 2 ** 63, 2 ** 64 - 1]))
+        bad.write_bytes(bytes(b))
+        try:
+            ckpt.inspect(str(bad))
+        except _capi.SfbError as e:
+            assert e.status in (_capi.SFB_ERR_IO, _capi.SFB_ERR_DTYPE, _capi.SFB_ERR_SHAPE), e.status
+
+
+def test_config_reader_survives_corrupted_json(manifest, tmp_path):
+    import random
+    good = json.dumps(manifest["hf_config"]).encode()
+    rng = random.Random(11)
+    p = tmp_path / "cfg.json"
+    for i in range(300):
+        b = bytearray(good)
+        if i % 2:
+            b = b[: rng.randrange(0, len(b))]
+        else:
+            for _ in range(rng.randrange(1, 4)):
+                b[rng.randrange(len(b))] = rng.randrange(256)
+        p.write_bytes(bytes(b))
+        try:
+            ckpt.config_from_json(str(p))
+        except _capi.SfbError as e:
+            assert e.status in (_capi.SFB_ERR_IO, _capi.SFB_ERR_INVALID, _capi.SFB_ERR_UNSUPPORTED), e.status
+    # deep nesting is refused, not recursed into without bound
+    p.write_text("[" * 100000 + "]" * 100000)
+    with pytest.raises(_capi.SfbError) as e:
+        ckpt.config_from_json(str(p))
+    assert e.value.status == _capi.SFB_ERR_IO

@@ -157,3 +157,27 @@ def test_missing_and_misshapen_tensors(gpu, converted, manifest, tmp_path):
         assert e.value.status == _capi.SFB_ERR_DTYPE
     finally:
         model.close()
+
+
+def test_prequantised_pairs_round_trip(gpu, converted, tmp_path):
+    """An int8 checkpoint (weight_q int8 + weight_scale fp32 per projection, as
+    the model stores them) loads bit for bit into a second model."""
+    from safetensors.torch import save_file
+    cfg = ckpt.config_from_json(os.path.join(converted[0], "config.json"))
+    a = ckpt.load_rdt1b(converted[0])
+    b = RDT1B(cfg, seed=99)
+    try:
+        names = ["blocks.1.attn.qkv", "blocks.0.ffn.fc2", "final_layer.ffn_final.fc2"]
+        t = {}
+        for n in names:
+            t[n + ".weight_q"] = a.param(n + ".weight_q").cpu()
+            t[n + ".weight_scale"] = a.param(n + ".weight_scale").cpu()
+            t[n + ".bias"] = a.param(n + ".bias").cpu()
+        save_file(t, str(tmp_path / "int8.safetensors"))
+        loaded, ignored = b.load_safetensors(str(tmp_path / "int8.safetensors"))
+        assert (loaded, ignored) == (3 * len(names), 0)
+        for k, v in t.items():
+            assert torch.equal(b.param(k).cpu(), v), k
+    finally:
+        a.close()
+        b.close()
