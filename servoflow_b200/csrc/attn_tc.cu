@@ -821,9 +821,10 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnO
 
     auto kern = a.dtype == SFB_BF16 ? attn_tc::attn_fwd_tc_kernel<__nv_bfloat16>
                                     : attn_tc::attn_fwd_tc_kernel<__half>;
-    static bool attr_done[2][64] = {};
+    // kernel attributes, set once per dtype and device (idempotent: a race only repeats them)
+    static std::atomic<bool> attr_done[2][64];
     const int ki = a.dtype == SFB_BF16 ? 0 : 1;
-    if (!attr_done[ki][dev.ordinal & 63]) {
+    if (!attr_done[ki][dev.ordinal & 63].load(std::memory_order_acquire)) {
         cudaError_t e1 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               attn_tc::kSmemBytes);
         cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -832,7 +833,7 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnO
             record_cuda_error(e1 != cudaSuccess ? e1 : e2, "attention kernel attributes");
             return SFB_ERR_CUDA;
         }
-        attr_done[ki][dev.ordinal & 63] = true;
+        attr_done[ki][dev.ordinal & 63].store(true, std::memory_order_release);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim  = dim3(p.splits, a.heads, a.batch * p.qtiles);

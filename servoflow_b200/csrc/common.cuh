@@ -4,6 +4,7 @@
 // kernel file), so the definitions here exist exactly once.
 #pragma once
 
+#include <atomic>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -106,14 +107,14 @@ inline void record_cuda_error(cudaError_t e, const char* where) {
 // SMs between launches. Applied once per kernel and device.
 template <typename K>
 inline void prefer_max_shared(K kernel) {
-    static bool done[64] = {};
+    static std::atomic<bool> done[64];      // idempotent: a race only repeats the call
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!done[dev & 63]) {
-        cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             static_cast<int>(cudaSharedmemCarveoutMaxShared));
-        (void)cudaGetLastError();
-        done[dev & 63] = true;
+    if (!done[dev & 63].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+            (void)cudaGetLastError();       // a hint only: clear its own error, no other
+        done[dev & 63].store(true, std::memory_order_release);
     }
 }
 

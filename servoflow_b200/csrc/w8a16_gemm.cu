@@ -529,9 +529,9 @@ extern "C" void sfb_debug_set_w8_trace(void* p) { g_w8_trace = static_cast<unsig
 // Clusters of `size` CTAs of the GEMM kernel that can be resident at once
 // (cached per device and size; 0 when the query fails).
 static int w8_max_clusters(const DeviceInfo& dev, int size) {
-    static int cache[64][17] = {};
-    int& slot = cache[dev.ordinal & 63][size & 15];
-    if (slot != 0) return slot;
+    static std::atomic<int> cache[64][17];            // 0: not queried yet (idempotent query)
+    std::atomic<int>& slot = cache[dev.ordinal & 63][size < 0 ? 0 : (size > 16 ? 16 : size)];
+    if (const int n = slot.load(std::memory_order_relaxed); n != 0) return n;
     const w8::KernFn kern = w8::pick(0, true, 128);   // the variants share their resource use
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              w8::kSmemBytes) != cudaSuccess ||
@@ -559,7 +559,7 @@ static int w8_max_clusters(const DeviceInfo& dev, int size) {
 #ifdef SFB_TRACE
     fprintf(stderr, "w8a16: cluster size %d -> %d resident clusters\n", size, n);
 #endif
-    slot = n;
+    slot.store(n, std::memory_order_relaxed);
     return n;
 }
 
