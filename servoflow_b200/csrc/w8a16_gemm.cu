@@ -588,6 +588,17 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     // tokens per CTA: round up to 32, at most 256 (16-token rounding measured
     // slower in the denoise: 67 tokens as N = 80 against N = 96)
     p.bn = M >= 256 ? 256 : ((M + 31) / 32) * 32;
+    if (M >= 256) {
+        // When 256-token tiles leave SMs idle in their single wave, take the
+        // narrowest token tile whose grid still fits one wave (less MMA work
+        // per CTA, the same single wave): M = 1072 → 9 tiles of 128 tokens,
+        // 144 CTAs, instead of 5 of 256 (80 CTAs). Grids of several waves keep
+        // 256 (per-CTA fixed costs favour the widest tile).
+        const int64_t nt = (N + 127) / 128;
+        auto ctas = [&](int bn) { return nt * ((M + bn - 1) / bn); };
+        if (ctas(256) < dev.num_sms)
+            for (int bn = 224; bn >= 32 && ctas(bn) <= dev.num_sms; bn -= 32) p.bn = bn;
+    }
     const int mtile = (M + p.bn - 1) / p.bn;
     // Split K across a cluster only when the tiles alone leave most SMs idle,
     // and only as far as every cluster still fits in one wave: at one CTA per
@@ -608,7 +619,8 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
         // halved tile gives more CTAs (N = 2048 at 67 tokens: 32 tiles × 4
         // splits instead of 16 × 4, 8-CTA clusters not fitting one wave)
         const int ntile64 = (N + 63) / 64, s64 = auto_splits(ntile64 * mtile);
-        if (ntile * mtile * splits < dev.num_sms && ntile64 * mtile * s64 > ntile * mtile * splits) {
+        if (ntile * mtile * splits < dev.num_sms && ntile64 * mtile * s64 > ntile * mtile * splits &&
+            ntile64 * mtile * s64 <= dev.num_sms) {           // and still one wave
             tm = 64; ntile = ntile64; splits = s64;
         }
     }
