@@ -104,3 +104,10 @@ def test_reference_dequant_then_matmul(be, gpu):
     torch.cuda.synchronize()
     ref = x.float() @ wd.t() + b.float()
     assert torch.allclose(y, ref, rtol=1e-4, atol=1e-4)
+
+
+# serving shapes (32 and 16 sessions × 67 tokens): 256-token tiles in one wave
+# of 144 CTAs, and 128-token tiles chosen to fill the wave
+@pytest.mark.parametrize("M,act,residual", [(2144, "none", False), (1072, "gelu", True)])
+def test_serving_shapes(be, gpu, M, act, residual):
+    check(be, M, 2048, 2048, 70 + M, gpu, act=act, residual=residual)
