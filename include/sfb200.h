@@ -4,8 +4,8 @@
  * Every entry point takes plain device pointers, sizes and an opaque
  * cudaStream_t (passed as void*), returns an int status (0 = OK, negative =
  * error, never throws) and never allocates device memory on the hot path.
- * The reference's C++ CUDABackend binds these in place of its own ops; the
- * binding stubs are shown in INTEGRATION.md.
+ * The reference's C++ CUDABackend binds these in place of its own ops (its
+ * attention, dequantize and graph hooks forward to the functions below).
  *
  * dtype codes are the numeric values of sf::DType in the reference
  * (include/servoflow/core/dtype.h:11-19), so a caller can pass

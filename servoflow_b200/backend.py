@@ -3,7 +3,7 @@ attention path (include/servoflow/backend/backend.h:102-110, 201-206,
 227-229), over the C ABI of libsfb200.so.
 
 Used by the tests and by bench.py; the production host side is C++ and binds
-the same C ABI. torch supplies device memory and streams
+the same C ABI (include/sfb200.h). torch supplies device memory and streams
 only; every op runs a libsfb200 kernel, and raises if the library is missing
 or the device is not an sm_100a part.
 """
