@@ -94,6 +94,14 @@ def test_config2_image_cross_attention(be, gpu):
     assert torch.equal(out2, run(be, q, k, v))
 
 
+def test_image_cross_attention_batched_sessions(be, gpu):
+    # the serving shape: several sessions' image K/V caches (bf16 K, fp16 V as
+    # the model stores them) in one launch; 4 sessions = 143 MB of K/V
+    q, k, v = make(4, 32, 32, 67, 4374, 64, torch.bfloat16, 8, gpu)
+    v16 = v.to(torch.float16)
+    check_close(run(be, q, k, v16), oracle_of(q, k, v16), torch.bfloat16)
+
+
 @pytest.mark.parametrize("Lk,B,masked", [(4374, 1, False), (1024, 4, True)])
 def test_fp16_v_cache(be, gpu, Lk, B, masked):
     # bf16 Q/K with the V cache already in fp16 (how the model stores it):
