@@ -58,6 +58,14 @@ const char* sfb_version(void);
  * Synchronous: it waits for the device. */
 int sfb_device_error(int* code, int reset);
 
+/* Diagnostic of the kernels' failure path: one warp waits, with the bounded
+ * mbarrier wait every kernel uses, on a barrier that nothing arrives at. The
+ * wait gives up after timeout_ns (1e5 .. 2e9), the kernel records
+ * SFB_ERR_DEVICE_TIMEOUT in the device error word (read it with
+ * sfb_device_error) and returns, and the context stays usable. *completed = 0
+ * when the wait gave up as it must, 1 if it completed. Synchronous. */
+int sfb_selftest_bounded_wait(int64_t timeout_ns, int32_t* completed);
+
 /* Synchronous copy between any two addresses (cudaMemcpyDefault); a helper
  * for hosts without their own CUDA runtime binding (tests read parameters). */
 int sfb_copy_device(void* dst, const void* src, int64_t bytes);

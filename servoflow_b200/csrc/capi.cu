@@ -58,6 +58,22 @@ int sfb_device_error(int* code, int reset) {
     return SFB_OK;
 }
 
+int sfb_selftest_bounded_wait(int64_t timeout_ns, int32_t* completed) {
+    if (completed == nullptr || timeout_ns < 100000 || timeout_ns > 2000000000) return SFB_ERR_INVALID;
+    if (!sfb::is_sm100(sfb::device_info())) return SFB_ERR_UNSUPPORTED;
+    int32_t* d = nullptr;
+    if (cudaMalloc(&d, sizeof(int32_t)) != cudaSuccess) { (void)cudaGetLastError(); return SFB_ERR_CUDA; }
+    sfb::bounded_wait_selftest_kernel<<<1, 32>>>(static_cast<uint64_t>(timeout_ns), d);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int32_t h = -1;
+    if (e == cudaSuccess) e = cudaMemcpy(&h, d, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) { sfb::record_cuda_error(e, "bounded wait self-test"); return SFB_ERR_CUDA; }
+    *completed = h;
+    return SFB_OK;
+}
+
 int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
     if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr || a->out == nullptr)
         return SFB_ERR_INVALID;

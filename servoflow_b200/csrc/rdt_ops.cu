@@ -22,6 +22,7 @@
 //                   tick, so every denoising step reads V in the P·V operand
 //                   type (exact for |v| <= 65504, else SFB_ERR_RANGE).
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace sfb {
 namespace rdt {
@@ -287,6 +288,29 @@ __global__ void bf16_to_f16_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, in
     }
     if (bad) atomicExch(&g_sfb_device_error, SFB_ERR_RANGE);
 }
+
+}  // namespace rdt
+
+// One warp waits, with the bounded mbarrier wait every kernel uses, on a
+// barrier that nothing arrives at: the wait must give up after timeout_ns and
+// the kernel must record SFB_ERR_DEVICE_TIMEOUT and return (the failure
+// path of the kernels, exercised without a fault). out = 1 if the wait
+// completed, 0 if it gave up.
+__global__ void bounded_wait_selftest_kernel(uint64_t timeout_ns, int32_t* out) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        ptx::fence_mbarrier_init();
+    }
+    __syncthreads();
+    const bool done = ptx::mbar_wait(&bar, 0, timeout_ns);
+    if (threadIdx.x == 0) {
+        *out = done ? 1 : 0;
+        if (!done) atomicExch(&g_sfb_device_error, SFB_ERR_DEVICE_TIMEOUT);
+    }
+}
+
+namespace rdt {
 
 inline unsigned grid_for(int64_t n, int threads) {
     int64_t g = (n + threads - 1) / threads;
