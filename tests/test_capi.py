@@ -77,3 +77,28 @@ def test_null_args_rejected_without_device():
     assert _capi.lib().sfb_dequantize_int8(None, None, 1, 1, None, 1, 0, 0, None) == _capi.SFB_OK
     assert _capi.lib().sfb_dequantize_int8(None, None, 1, 1, None, 1, 2, 2, None) == \
         _capi.SFB_ERR_INVALID
+
+
+def test_model_api_argument_checks_without_a_gpu():
+    """The RDT-1B entry points reject bad arguments before touching a device
+    (the same statuses a servoflow binding turns into exceptions)."""
+    from servoflow_b200.rdt1b import RDT1BConfig, _declare, default_config
+    lib = _capi.lib()
+    _declare(lib)
+    h = ctypes.c_void_p()
+    cfg = default_config()
+    assert lib.sfb_rdt1b_create(None, 0, ctypes.byref(h)) == _capi.SFB_ERR_INVALID
+    assert lib.sfb_rdt1b_create(ctypes.byref(cfg), 0, None) == _capi.SFB_ERR_INVALID
+    for bad in (dict(hidden=2000), dict(heads=31), dict(num_layers=0), dict(max_sessions=0),
+                dict(num_steps=0), dict(num_steps=65), dict(action_dim=100), dict(lang_dim=100),
+                dict(state_dim=64)):
+        c = default_config(**bad)
+        assert lib.sfb_rdt1b_create(ctypes.byref(c), 0, ctypes.byref(h)) == _capi.SFB_ERR_SHAPE, bad
+    x = ctypes.c_void_p(1)
+    assert lib.sfb_rdt1b_encode(None, 1, x, x, x, x, None) == _capi.SFB_ERR_INVALID
+    assert lib.sfb_rdt1b_forward(None, 1, x, 0.0, x, None) == _capi.SFB_ERR_INVALID
+    assert lib.sfb_rdt1b_sample(None, 1, x, x, 1, None) == _capi.SFB_ERR_INVALID
+    assert lib.sfb_rdt1b_destroy(None) == _capi.SFB_ERR_INVALID
+    n = ctypes.c_int64()
+    assert lib.sfb_rdt1b_graph_kernels(None, 1, ctypes.byref(n)) == _capi.SFB_ERR_INVALID
+    assert lib.sfb_rdt1b_schedule(None, None, None, None, None, 5) == _capi.SFB_ERR_INVALID

@@ -118,3 +118,31 @@ def test_sessions_are_independent(setup):
     assert torch.equal(a[1], b[1]) and not torch.equal(a[0], b[0])
     m.encode(s["lang"].to(dev), s["lens"].to(dev), s["img"].to(dev), s["state"].to(dev))
     torch.cuda.synchronize()
+
+
+def test_api_errors(setup):
+    """Bad arguments on a live model return statuses and leave it usable."""
+    import ctypes
+    from servoflow_b200 import _capi
+    s = setup
+    m, lib, dev = s["model"], s["model"].lib, s["dev"]
+    cfg = s["cfg"]
+    too_many = cfg.max_sessions + 1
+    big = torch.zeros(too_many, cfg.horizon, cfg.action_dim, device=dev)
+    out = torch.empty_like(big)
+    sh = torch.cuda.current_stream().cuda_stream
+    assert lib.sfb_rdt1b_forward(m.h, too_many, big.data_ptr(), 1.0, out.data_ptr(), sh) == _capi.SFB_ERR_SHAPE
+    assert lib.sfb_rdt1b_sample(m.h, too_many, big.data_ptr(), out.data_ptr(), 1, sh) == _capi.SFB_ERR_SHAPE
+    assert lib.sfb_rdt1b_sample(m.h, 0, big.data_ptr(), out.data_ptr(), 1, sh) == _capi.SFB_ERR_SHAPE
+    assert lib.sfb_rdt1b_encode(m.h, too_many, big.data_ptr(), big.data_ptr(), big.data_ptr(),
+                                big.data_ptr(), sh) == _capi.SFB_ERR_SHAPE
+    p, n, dt = ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_int32()
+    assert lib.sfb_rdt1b_param(m.h, b"blocks.0.no_such.weight", ctypes.byref(p), ctypes.byref(n),
+                               ctypes.byref(dt)) == _capi.SFB_ERR_INVALID
+    assert lib.sfb_rdt1b_schedule(m.h, None, None, None, None, cfg.num_steps + 1) == _capi.SFB_ERR_INVALID
+    # still usable
+    noise = s["noise"].to(dev)
+    y = torch.empty_like(noise)
+    m.forward(noise, 999.0, y)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all()
