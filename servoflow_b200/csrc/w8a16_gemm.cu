@@ -27,10 +27,11 @@
 //     one FADD, top 16 bits kept) and afterwards run the epilogue, staged
 //     through shared memory so that Y is written in 16-byte vectors.
 //   * Split-K over a thread-block cluster when M is small: each CTA
-//     accumulates a K range in TMEM, pushes its fp32 partial into the owning
-//     CTA's shared memory (owner = a block of token columns) with remote
-//     stores, and each owner sums, applies the epilogue and stores coalesced
-//     rows of Y. No global scratch.
+//     accumulates a K range in TMEM and stores its scaled fp32 partial from
+//     registers straight into the owning CTA's shared memory (owner = a
+//     block of TM / C channel rows) with distributed-shared-memory stores;
+//     one cluster barrier publishes them, and each owner sums, applies the
+//     epilogue and stores coalesced rows of Y. No global scratch.
 //   * Every mbarrier wait is bounded (1 s) and records SFB_ERR_DEVICE_TIMEOUT.
 #include "common.cuh"
 #include "sm100_ptx.cuh"
@@ -53,6 +54,7 @@ struct W8Params {
     int32_t        splits;        // cluster size along grid.x
     int32_t        y_f32;         // 1: fp32 output
     int32_t        stages;        // pipeline depth, kRingBytes / stage bytes, at most kMaxStages
+    int32_t        rcv_off;       // split-K: byte offset of the receive area (past the ring)
 #ifdef SFB_TRACE
     unsigned long long* trace;
     unsigned long long* tl;
@@ -84,12 +86,8 @@ constexpr int kOffBar   = kRingBytes;
 constexpr int kOffTmem  = kOffBar + 8 * (4 * kMaxStages + 2);
 constexpr int kSmemUsed = kOffTmem + 16;
 constexpr int kSmemBytes = kSmemUsed + 1024;
-// Split-K merge (only when splits > 1, bn <= 128) reuses the ring, idle by
-// then: a staging area [C owners][bn tokens][128/C + pad] at offset 0 and a
-// receive area [C sources][bn][128/C] at kOffRecv, each fp32 and at most
-// 64 KB + 512 B.
-constexpr int kOffRecv  = 65536 + 1024;
-static_assert(kOffRecv + 65536 <= kRingBytes, "merge areas fit the ring");
+// Split-K (splits > 1, bn <= 128) shortens the ring by the stages that a
+// TM × bn fp32 receive area needs; peers store their partials into it.
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 __host__ __device__ constexpr int stage_bytes(int bn, int tm) { return w_bytes(tm) + wb_bytes(tm) + bn * 128; }
@@ -103,7 +101,6 @@ __host__ __device__ constexpr int bar_full_x(int s) { return kMaxStages + s; }  
 __host__ __device__ constexpr int bar_conv(int s)  { return 2 * kMaxStages + s; }    // W bf16 ready
 __host__ __device__ constexpr int bar_empty(int s) { return 3 * kMaxStages + s; }    // stage consumed by MMA
 constexpr int kBarAcc = 4 * kMaxStages;                                              // accumulator done
-constexpr int kBarMerge = 4 * kMaxStages + 1;                                        // split-K partials landed
 
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;   // sqrt(2/pi), GELU tanh form
@@ -160,10 +157,6 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             mbar_init(&bars[bar_empty(s)], 1);
         }
         mbar_init(&bars[kBarAcc], 1);
-        mbar_init(&bars[kBarMerge], 1);
-        if (kSplit)         // partials of the other C-1 CTAs land here by bulk copy
-            mbar_arrive_expect_tx(&bars[kBarMerge],
-                                  static_cast<uint32_t>((p.splits - 1) * p.bn * (kTM / p.splits) * 4));
         fence_mbarrier_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
@@ -387,24 +380,14 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             }
         }
     } else {
-        // Split-K merge. CTA r owns channel rows [r·R, (r+1)·R) of the tile,
-        // R = TM / C. Every CTA stages its fp32 partial as C contiguous
-        // owner slices [bn tokens][R channels] (padded by R floats between
-        // slices so the per-lane stores hit distinct banks), then one thread
-        // bulk-copies slice r into CTA r's receive area, signalling r's merge
-        // barrier. The owner sums its own slice and the C - 1 received ones,
-        // applies scale/bias/activation/residual and writes 16-byte vectors of
-        // 8 channels per token.
+        // Split-K merge. CTA r owns channel rows [r·R, (r+1)·R) of the
+        // tile, R = TM / C; its receive area holds [C sources][bn tokens][R].
         const int C = p.splits, R = kTM / C;
         const int slice = p.bn * R;
-        float* stg = reinterpret_cast<float*>(smem);
-        float* rcv = reinterpret_cast<float*>(smem + kOffRecv);
+        float* rcv = reinterpret_cast<float*>(smem + p.rcv_off);
         if (epi) {
-            // Staged values carry the channel scale and (from CTA 0 only) the bias,
-            // so the owner's pass is a plain sum.
-            const float bsplit = split == 0 ? bi : 0.f;
+            const float bsplit = split == 0 ? bi : 0.f;     // the bias once, from CTA 0
             const int owner = trow / R, slot = trow - owner * R;
-            float* d = stg + owner * (slice + R) + slot;
             float v[2][32];
             const int c0a = 32 * hh, c0b = 32 * hh + 64;
             if (nch > 0) {
@@ -415,35 +398,27 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 #pragma unroll
                 for (int i = 0; i < 32; ++i) { v[0][i] = 0.f; v[1][i] = 0.f; }
             }
-            // (a token tile of 16·k columns can end inside the last 32-column block)
-            if (lane_ok && c0a < p.bn) {
+            if (lane_ok) {
+                // this thread's channel row, every token, into its owner's slot
+                const uint32_t base = dsmem_map(smem_u32(rcv + split * slice + slot), static_cast<uint32_t>(owner));
+                const uint32_t step = static_cast<uint32_t>(R) * 4u;
+                if (c0a < p.bn) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c0a + i < p.bn) d[(c0a + i) * R] = fmaf(v[0][i], sc, bsplit);
-            }
-            if (lane_ok && c0b < p.bn) {
+                    for (int i = 0; i < 32; ++i)
+                        if (c0a + i < p.bn) dsmem_st_f32(base + (c0a + i) * step, fmaf(v[0][i], sc, bsplit));
+                }
+                if (c0b < p.bn) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c0b + i < p.bn) d[(c0b + i) * R] = fmaf(v[1][i], sc, bsplit);
+                    for (int i = 0; i < 32; ++i)
+                        if (c0b + i < p.bn) dsmem_st_f32(base + (c0b + i) * step, fmaf(v[1][i], sc, bsplit));
+                }
             }
-            fence_proxy_async_smem();
         }
         if (tid == 64) W8_T(4, 3);
-        // every CTA's MMAs are done (its X ring is free) and its slices are staged
-        cluster_sync();
-        if (tid == 64) {
-            for (int j = 1; j < C; ++j) {
-                const int o = (split + j) % C;
-                bulk_copy_to_cluster(dsmem_map(smem_u32(rcv + split * slice), o),
-                                     smem_u32(stg + o * (slice + R)), static_cast<uint32_t>(slice * 4),
-                                     dsmem_map(smem_u32(&bars[kBarMerge]), o));
-            }
-        }
-        if (tid == 64) W8_T(4, 4);
-        if (epi) wait(kBarMerge, 0);
+        cluster_sync();                                 // every partial is in its owner (release / acquire)
         if (tid == 64) W8_T(4, 5);
         if (epi) {
-            const int nb = n0 + split * R;                 // first channel owned here
+            const int nb = n0 + split * R;              // first channel owned here
 #pragma unroll
             for (int it = 0; it < kMaxIt; ++it) {
                 const int u = tid - 64 + it * kConvWarps * 32;
@@ -455,7 +430,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                 for (int k = 0; k < 8; ++k) y[k] = 0.f;
 #pragma unroll 1
                 for (int r = 0; r < C; ++r) {
-                    const float* src = (r == split ? stg + r * (slice + R) : rcv + r * slice) + mm * R + seg;
+                    const float* src = rcv + r * slice + mm * R + seg;
                     const float4 a4 = *reinterpret_cast<const float4*>(src);
                     const float4 b4 = *reinterpret_cast<const float4*>(src + 4);
                     y[0] += a4.x; y[1] += a4.y; y[2] += a4.z; y[3] += a4.w;
@@ -482,7 +457,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             }
         }
         if (tid == 64) W8_T(4, 6);
-        cluster_sync();   // no CTA leaves while a peer's copy may still touch its shared memory
+        // (no second barrier: nothing reads or writes another CTA's memory now)
     }
 
     if (tid == 64) W8_T(4, 2);
@@ -516,6 +491,7 @@ inline KernFn pick(int act, bool split, int tm) {
          {w8a16_gemm_kernel<2, false, 64>, w8a16_gemm_kernel<2, true, 64>}}};
     return t[tm == 64 ? 1 : 0][act][split ? 1 : 0];
 }
+
 
 }  // namespace w8
 
@@ -629,6 +605,13 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
     if (splits > p.kchunks || splits > tm / 8) return SFB_ERR_INVALID;
     p.splits = splits;
     p.stages = w8::num_stages(p.bn, tm);
+    if (splits > 1) {
+        // split-K: the receive area of the merge, TM × bn fp32, lies past the
+        // ring's stages (at most 64 KB: four stages of the widest tile remain)
+        const int sb = w8::stage_bytes(p.bn, tm), rcv = tm * p.bn * 4;
+        p.stages = std::min(w8::kMaxStages, (w8::kRingBytes - rcv) / sb);
+        p.rcv_off = p.stages * sb;
+    }
 
     CUtensorMap mx, mw;
     {
