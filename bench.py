@@ -380,6 +380,64 @@ def serving(dev, rank, batches, sessions=32):
     return ms
 
 
+def octo_leg(dev, reps=50):
+    """The Octo row: Octo-Small at the reference's defaults (12 blocks, hidden
+    384, 64 tokens; diffusion head; 10 flow-matching steps), one session.
+    Returns device-timed medians (ms): encode (backbone + readout), sample
+    (one graph), sample from pinned host noise to host actions, and the
+    sampling graph's kernel count."""
+    import torch
+    from servoflow_b200.octo import Octo, default_config
+    from servoflow_b200.sessions import session_seed
+    model = Octo(default_config(), seed=session_seed(0, "weights"))
+    g = torch.Generator().manual_seed(4242)
+    tokens = torch.randn(1, 64, 384, generator=g).bfloat16().to(dev)
+    noise_h = torch.randn(1, 4, 7, generator=g).pin_memory()
+    act_h = torch.empty_like(noise_h).pin_memory()
+    noise = noise_h.to(dev)
+    act = torch.empty_like(noise)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        st = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        en = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        for i in range(reps):
+            st[i].record(stream)
+            fn()
+            en[i].record(stream)
+        torch.cuda.synchronize()
+        return float(np.median([a.elapsed_time(b) for a, b in zip(st, en)]))
+
+    enc = timed(lambda: model.encode(tokens))
+    smp = timed(lambda: model.sample(noise, act))
+    smp_h = timed(lambda: model.sample(noise_h, act_h))
+    assert torch.isfinite(act).all() and torch.equal(act.cpu(), act_h)
+    kernels = model.graph_kernels(1)
+    model.close()
+    return enc, smp, smp_h, kernels
+
+
+def octo_cpu(threads: int, reps: int = 3):
+    """The same two calls on the CPU oracle (fp32 torch, `threads` threads):
+    median ms of encode and of a 10-step sample."""
+    import time
+    import torch
+    from oracle import octo_ref
+    from servoflow_b200.octo import default_config
+    torch.set_num_threads(threads)
+    cfg = default_config()
+    ref = octo_ref.RefOcto(octo_ref.random_weights(cfg, seed=1), cfg)
+    tokens, noise = torch.randn(1, 64, 384), torch.randn(1, 4, 7)
+    enc, smp = [], []
+    with torch.no_grad():
+        for _ in range(reps):
+            t0 = time.perf_counter(); _, cond = ref.encode(tokens); enc.append(time.perf_counter() - t0)
+            t0 = time.perf_counter(); ref.sample(noise, cond); smp.append(time.perf_counter() - t0)
+    return float(np.median(enc)) * 1e3, float(np.median(smp)) * 1e3
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -477,6 +535,7 @@ def main():
     serve_ms = [0.0] if args.no_serving else serving(dev, rank, batches=max(3, min(args.steps, 10)))
     at_bytes, at_flops, at_med, at_min, at_launches = attention_roofline(be, dev, reps=64)
     atb_bytes, atb_ms = attention_batched(dev)
+    oc_enc, oc_smp, oc_smp_h, oc_kernels = octo_leg(dev)
     assert be.device_error() == 0
 
     ms = np.array([s.elapsed_time(e) for s, e in zip(starts, ends)])
@@ -484,8 +543,9 @@ def main():
     tick_ms = np.array([s.elapsed_time(e) for s, e in zip(t_st, t_en)])
     stats = max_over_ranks([np.median(ms), np.mean(ms), np.percentile(ms, 99), np.median(e2e_ms),
                             np.median(tick_ms), gemm_s, at_med, at_min, np.median(serve_ms),
-                            np.percentile(serve_ms, 99), atb_ms], device=dev)
-    p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_med, at_min, sv_p50, sv_p99, atb_ms = stats
+                            np.percentile(serve_ms, 99), atb_ms, oc_enc, oc_smp, oc_smp_h], device=dev)
+    (p50, mean, p99, e2e_p50, tick_p50, gemm_s, at_med, at_min, sv_p50, sv_p99, atb_ms,
+     oc_enc, oc_smp, oc_smp_h) = stats
 
     if rank == 0:
         hbm, tflops, kind = peaks()
@@ -547,6 +607,14 @@ def main():
                 "per_session_p99_ms": sv_p99,
                 "actions_per_s": world * 32 * HORIZON * 1e3 / sv_p50,
                 "chunks_per_s": world * 32 * 1e3 / sv_p50},
+            "octo": {"what": "Octo-Small at the reference's defaults (12 pre-LN blocks, hidden 384, "
+                             "6 heads, 64 tokens; MLP diffusion head; 10 flow-matching Euler steps in "
+                             "one CUDA graph), one session per GPU",
+                     "encode_ms": oc_enc, "sample_ms": oc_smp, "sample_host_ms": oc_smp_h,
+                     "sample_graph_kernels": oc_kernels,
+                     "path": "Octo.encode / Octo.sample -> sfb_octo_encode / sfb_octo_sample; "
+                             "sample_host_ms copies pinned host noise in and actions out inside the "
+                             "timed region"},
             "gpu_launches": kernels_per_step * args.steps * world,
             "gpu_launches_note": f"{kernels_per_step} kernels per denoise graph x {args.steps} timed steps "
                                  f"x {world} GPU(s) "
@@ -557,6 +625,9 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = CpuDenoiseSample(os.cpu_count() or 1).baseline(15.0)
+            ce, cs = octo_cpu(os.cpu_count() or 1)
+            line["octo"]["cpu_oracle"] = {"encode_ms": ce, "sample_ms": cs, "cores": os.cpu_count() or 1,
+                                          "kind": "port", "what": "oracle/octo_ref.py, fp32 torch"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

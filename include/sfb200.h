@@ -241,6 +241,67 @@ int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, 
 int sfb_rdt1b_schedule(void* handle, float* timesteps, float* coef_a, float* coef_b, float* coef_c,
                        int32_t n);
 
+/* ── Octo policy (model path) ─────────────────────────────────────────────────
+ * Replaces the reference's OctoModel / OctoBlock / OctoDiffusionHead
+ * (include/servoflow/models/octo/octo.h:18-132, src/models/octo/octo.cpp) on
+ * the same kernels: LayerNorm, the int8-weight linear layer, the tensor-core
+ * attention. Weights are seeded random values quantised to int8 per output
+ * channel (the reference's load_octo reads none, octo.cpp:247-260). All
+ * tensors are device memory except where stated; `sessions` independent
+ * robot sessions run batched (1 <= sessions <= max_sessions). */
+typedef struct sfb_octo_config {
+    int32_t num_layers;      /* 12 (OctoConfig, config.h:17-46) */
+    int32_t hidden;          /* 384 (= heads · 64) */
+    int32_t heads;           /* 6 */
+    int32_t head_dim;        /* 64 (the only value supported) */
+    int32_t intermediate;    /* 1536, multiple of 64 */
+    int32_t action_dim;      /* 7 */
+    int32_t action_horizon;  /* 4 */
+    int32_t head_hidden;     /* 256, multiple of 64 */
+    int32_t seq_len;         /* 64 backbone tokens (octo.cpp:202) */
+    int32_t max_sessions;    /* batch capacity */
+    int32_t num_steps;       /* 10 flow-matching steps (Schedule, sampler.h:24) */
+    int32_t readout_token;   /* -1: the reference's readout, a 0.1 fill
+                                (octo.cpp:218-223); k >= 0: backbone output token k */
+    float   weight_std;      /* 0.02, std of the random weights before quantisation */
+} sfb_octo_config;
+
+int sfb_octo_default_config(sfb_octo_config* cfg);
+int sfb_octo_create(const sfb_octo_config* cfg, uint64_t seed, void** handle);
+int sfb_octo_destroy(void* handle);
+/* OctoModel::encode_condition (octo.cpp:196-224): runs the backbone blocks
+ * over tokens bf16 [sessions, seq_len, hidden] (NULL: the reference's 0.1
+ * fill), writes the output tokens to `features` (optional, same shape) and
+ * sets each session's condition per readout_token. */
+int sfb_octo_encode(void* handle, int32_t sessions, const void* tokens, void* features, void* stream);
+/* Sets the condition directly: context bf16 [sessions, hidden], as the
+ * reference's tests pass it to denoise_step (tests/models/test_octo.cpp:30-45). */
+int sfb_octo_set_condition(void* handle, int32_t sessions, const void* context, void* stream);
+/* OctoModel::denoise_step (octo.cpp:226-238): x_t fp32 [sessions,
+ * action_horizon, action_dim] → velocity fp32 (same shape) from the
+ * diffusion head. t is accepted and, as in the reference, not used. */
+int sfb_octo_denoise_step(void* handle, int32_t sessions, const float* x_t, float t, float* velocity,
+                          void* stream);
+/* FlowMatchingSampler::sample (src/sampling/flow_matching.cpp:25-93): noise
+ * fp32 [sessions, action_horizon, action_dim] → actions after num_steps Euler
+ * steps x ← x + (t_{i+1} − t_i)·v over linspace(1, 0, num_steps + 1). noise
+ * and actions may be device or host pointers; the call returns once the work
+ * is queued on `stream`. use_graph as sfb_rdt1b_sample. */
+int sfb_octo_sample(void* handle, int32_t sessions, const float* noise, float* actions, int32_t use_graph,
+                    void* stream);
+/* The sampler's num_steps + 1 timesteps (host memory; n = num_steps + 1). */
+int sfb_octo_timesteps(void* handle, float* timesteps, int32_t n);
+/* Device pointer, element count and dtype of a parameter: "blocks.<l>.norm1.weight",
+ * "...norm1.bias", "...attn.qkv.weight_q", "...weight_scale", "...bias",
+ * "...attn.proj.*", "...norm2.*", "...mlp.fc1.*", "...mlp.fc2.*",
+ * "head.fc1.*" ([head_hidden, K] with K = action_dim·action_horizon + 128 +
+ * hidden rounded up to 64, zero columns past the valid width), "head.fc2.*",
+ * "head.fc3.*" ([action_dim·action_horizon rounded up to 128, head_hidden],
+ * zero rows past the valid count). */
+int sfb_octo_param(void* handle, const char* name, void** ptr, int64_t* numel, int32_t* dtype);
+/* Kernel launches in the captured sampling graph for `sessions`. */
+int sfb_octo_graph_kernels(void* handle, int32_t sessions, int64_t* kernels);
+
 /* ── checkpoints (setup time; host code except the uploads) ──────────────────
  * A tensor entry of a .safetensors file: replaces SafeTensorsLoader::TensorMeta
  * (reference include/servoflow/loader/safetensors.h:46-52). dtype is an SFB

@@ -1,0 +1,157 @@
+"""GPU tests of the Octo runtime against the CPU oracle (oracle/octo_ref.py)
+at the reference's Octo-Small configuration (hidden 384, 12 layers, 6 heads,
+64 tokens, 7 × 4 actions, 10 flow-matching steps).
+
+Criteria: the reference's alignment bar for a half-precision model
+(tests/alignment/test_rdt1b_alignment.py:426), max |ours − oracle| < 0.05
+and cosine similarity > 0.9999, against the oracle that stores tensors in
+bf16 where the runtime does. The backbone's residual stream grows past 8,
+where one bf16 ulp is 0.0625, so its outputs are held to
+|ours − oracle| <= 0.05 + 2^-7·|oracle| (the bar plus one ulp of the value)
+elementwise. Against the all-fp32 oracle the bar is cosine > 0.999 (12
+residual layers of bf16 storage). The sampler's bookkeeping is exact: eager,
+first graph and replay agree bit for bit.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import octo_ref
+from servoflow_b200.octo import Octo, default_config
+
+pytestmark = pytest.mark.gpu
+
+
+def close(ours, ref):
+    a = ours.float().cpu().reshape(-1).double()
+    b = ref.float().reshape(-1).double()
+    return (a - b).abs().max().item(), torch.nn.functional.cosine_similarity(a[None], b[None]).item()
+
+
+def close_tokens(ours, ref):
+    """(worst |Δ| − 2^-7·|ref|, cosine) for backbone outputs; the first must stay below 0.05."""
+    a = ours.float().cpu().reshape(-1).double()
+    b = ref.float().reshape(-1).double()
+    excess = ((a - b).abs() - b.abs() * 2.0 ** -7).max().item()
+    return excess, torch.nn.functional.cosine_similarity(a[None], b[None]).item()
+
+
+@pytest.fixture(scope="module")
+def setup(gpu):
+    cfg = default_config(max_sessions=2)
+    model = Octo(cfg, seed=77)
+    w = octo_ref.load_weights(model, cfg)
+    yield dict(cfg=cfg, model=model, w=w, ref=octo_ref.RefOcto(w, cfg, store=torch.bfloat16),
+               ref32=octo_ref.RefOcto(w, cfg), dev=gpu)
+    model.close()
+
+
+def test_padding_is_zero(setup):
+    """Head weights padded to the GEMM's granularity carry zeros only."""
+    w = setup["w"]
+    assert w["head.fc1.weight_full"].shape == (256, 576)
+    assert torch.count_nonzero(w["head.fc1.weight_full"][:, 540:]) == 0
+    assert w["head.fc3.weight_full"].shape == (128, 256)
+    assert torch.count_nonzero(w["head.fc3.weight_full"][28:]) == 0
+    assert torch.count_nonzero(w["head.fc3.bias_full"][28:]) == 0
+
+
+def test_backbone_matches_oracle(setup):
+    s = setup
+    cfg, dev = s["cfg"], s["dev"]
+    g = torch.Generator().manual_seed(5)
+    tokens = torch.randn(2, cfg.seq_len, cfg.hidden, generator=g).bfloat16()
+    feats = torch.empty(2, cfg.seq_len, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    s["model"].encode(tokens.to(dev), feats)
+    torch.cuda.synchronize()
+    out, _ = s["ref"].encode(tokens.float())
+    excess, cos = close_tokens(feats, out)
+    assert excess < 0.05 and cos > 0.9999, (excess, cos, out.abs().max().item())
+    out32, _ = s["ref32"].encode(tokens.float())
+    assert close(feats, out32)[1] > 0.999
+
+
+def test_encode_default_readout_and_denoise_step(setup):
+    """No tokens: the reference's 0.1 tokens and its 0.1 readout; then one
+    head evaluation. t is not used (the reference embeds a constant)."""
+    s = setup
+    cfg, dev, m = s["cfg"], s["dev"], s["model"]
+    feats = torch.empty(2, cfg.seq_len, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    m.encode(None, feats, sessions=2)
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(2, cfg.action_horizon, cfg.action_dim, generator=g)
+    v1 = torch.empty(2, cfg.action_horizon, cfg.action_dim, device=dev)
+    v2 = torch.empty_like(v1)
+    m.denoise_step(x.to(dev), 0.5, v1)
+    m.denoise_step(x.to(dev), 0.9, v2)
+    torch.cuda.synchronize()
+    assert torch.equal(v1, v2)
+    out, cond = s["ref"].encode(None, sessions=2)
+    excess, cos = close_tokens(feats, out)
+    assert excess < 0.05 and cos > 0.9999, (excess, cos)
+    ref_v = s["ref"].head(x, cond)
+    max_abs, cos = close(v1, ref_v)
+    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+
+
+def test_set_condition_and_sampling_graph(setup):
+    s = setup
+    cfg, dev, m = s["cfg"], s["dev"], s["model"]
+    g = torch.Generator().manual_seed(7)
+    ctx = torch.randn(2, cfg.hidden, generator=g).bfloat16()
+    noise = torch.randn(2, cfg.action_horizon, cfg.action_dim, generator=g)
+    m.set_condition(ctx.to(dev))
+    outs = [torch.empty(2, cfg.action_horizon, cfg.action_dim, device=dev) for _ in range(3)]
+    m.sample(noise.to(dev), outs[0], use_graph=False)
+    m.sample(noise.to(dev), outs[1], use_graph=True)       # eager, then capture
+    m.sample(noise.to(dev), outs[2], use_graph=True)       # replay
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    assert m.graph_kernels(2) == cfg.num_steps * 5           # head input, 3 projections, Euler step
+    assert m.timesteps() == [float(t) for t in octo_ref.timesteps(cfg.num_steps)]
+    ref = s["ref"].sample(noise, ctx.float())
+    max_abs, cos = close(outs[2], ref)
+    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+
+
+def test_sample_from_host_memory(setup):
+    s = setup
+    cfg, dev, m = s["cfg"], s["dev"], s["model"]
+    noise = torch.randn(1, cfg.action_horizon, cfg.action_dim).pin_memory()
+    out_h = torch.empty_like(noise).pin_memory()
+    out_d = torch.empty(1, cfg.action_horizon, cfg.action_dim, device=dev)
+    m.sample(noise, out_h)
+    m.sample(noise.to(dev), out_d)
+    torch.cuda.synchronize()
+    assert torch.equal(out_h, out_d.cpu())
+
+
+def test_readout_token_mode(gpu):
+    """readout_token >= 0: the condition is that backbone output token."""
+    cfg = default_config(num_layers=2, readout_token=63)
+    m = Octo(cfg, seed=3)
+    try:
+        ref = octo_ref.RefOcto(octo_ref.load_weights(m, cfg), cfg, store=torch.bfloat16)
+        g = torch.Generator().manual_seed(8)
+        tokens = torch.randn(1, cfg.seq_len, cfg.hidden, generator=g).bfloat16()
+        x = torch.randn(1, cfg.action_horizon, cfg.action_dim, generator=g)
+        v = torch.empty(1, cfg.action_horizon, cfg.action_dim, device=gpu)
+        m.encode(tokens.to(gpu))
+        m.denoise_step(x.to(gpu), 1.0, v)
+        torch.cuda.synchronize()
+        _, cond = ref.encode(tokens.float())
+        max_abs, cos = close(v, ref.head(x, cond))
+        assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+    finally:
+        m.close()
+
+
+def test_bad_session_counts(setup):
+    from servoflow_b200 import _capi
+    m, cfg, dev = setup["model"], setup["cfg"], setup["dev"]
+    x = torch.zeros(3, cfg.action_horizon, cfg.action_dim, device=dev)
+    with pytest.raises(_capi.SfbError) as e:
+        m.denoise_step(x, 0.5, x)
+    assert e.value.status == _capi.SFB_ERR_SHAPE
+    with pytest.raises(_capi.SfbError):
+        m.sample(x, x)

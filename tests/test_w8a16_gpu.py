@@ -84,6 +84,13 @@ def test_split_k(be, gpu, splits):
     check(be, 67, 512, 2048, 40 + splits, gpu, splits=splits)
 
 
+@pytest.mark.parametrize("N,splits", [(32, 0), (96, 0), (96, 1)])
+def test_partial_channel_tiles(be, gpu, N, splits):
+    # N below one 128- or 64-channel weight tile: rows past N are zero-filled
+    # by the tile load and never stored
+    check(be, 67, N, 256, 50 + N + splits, gpu, splits=splits)
+
+
 def test_fp32_output_no_bias(be, gpu):
     check(be, 67, 256, 1024, 9, gpu, bias=False, f32=True)
 
