@@ -380,6 +380,69 @@ def serving(dev, rank, batches, sessions=32):
     return ms
 
 
+def attention_configs(dev, reps=50):
+    """Configs 1 and 3 of the attention path through the C ABI, each warm
+    (back to back, same inputs) and cold (a 256 MB buffer, twice the L2,
+    written between launches; only the attention launch is timed). Config 1:
+    self-attention, B=1, H=32, Lq=Lk=67, fp32 (and bf16). Config 3: masked
+    language cross-attention, B=16, H=32, Lq=67, Lk padded to 1024, valid
+    lengths L_b ~ U[8, 1024] (seeded), bf16; its bytes count valid keys only
+    (Q + O + K/V of L_b keys). Returns {name: (alg bytes, flops, warm us,
+    cold us)}."""
+    import ctypes
+    import torch
+    from servoflow_b200 import _capi
+    from servoflow_b200.backend import attention_args
+    capi = _capi.lib()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator().manual_seed(13)
+    out = {}
+
+    def measure(a):
+        pa = ctypes.byref(a)
+        for _ in range(5):
+            _capi.check(capi.sfb_attention_fwd(pa, stream.cuda_stream), "attention")
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            capi.sfb_attention_fwd(pa, stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        warm = e0.elapsed_time(e1) / reps * 1e3
+        st = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        en = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        for i in range(reps):
+            flush.fill_(i & 0xff)
+            st[i].record(stream)
+            capi.sfb_attention_fwd(pa, stream.cuda_stream)
+            en[i].record(stream)
+        torch.cuda.synchronize()
+        cold = float(np.median([x.elapsed_time(y) for x, y in zip(st, en)])) * 1e3
+        return warm, cold
+
+    for name, dt in (("config1_self_fp32", torch.float32), ("config1_self_bf16", torch.bfloat16)):
+        q, k, v = (torch.randn(1, HEADS, TOKENS, 64, generator=g).to(dt).to(dev) for _ in range(3))
+        o = torch.empty_like(q)
+        warm, cold = measure(attention_args(q, k, v, o))
+        es = q.element_size()
+        out[name] = (4 * HEADS * TOKENS * 64 * es, 4.0 * HEADS * TOKENS * TOKENS * 64, warm, cold)
+    B3 = 16
+    lens = torch.randint(8, LANG_LEN + 1, (B3,), generator=g, dtype=torch.int32)
+    q = torch.randn(B3, HEADS, TOKENS, 64, generator=g).bfloat16().to(dev)
+    k = torch.randn(B3, HEADS, LANG_LEN, 64, generator=g).bfloat16().to(dev)
+    v = torch.randn(B3, HEADS, LANG_LEN, 64, generator=g).bfloat16().to(dev)
+    o = torch.empty_like(q)
+    lens_d = lens.to(dev)
+    warm, cold = measure(attention_args(q, k, v, o, mask=lens_d))
+    sl = int(lens.sum())
+    out["config3_lang_masked_b16"] = (2 * B3 * HEADS * TOKENS * 64 * 2 + 2 * HEADS * 64 * 2 * sl,
+                                      4.0 * HEADS * TOKENS * 64 * sl, warm, cold)
+    del flush
+    return out
+
+
 def octo_leg(dev, reps=50):
     """The Octo row: Octo-Small at the reference's defaults (12 blocks, hidden
     384, 64 tokens; diffusion head; 10 flow-matching steps), one session.
@@ -536,6 +599,7 @@ def main():
     at_bytes, at_flops, at_med, at_min, at_launches = attention_roofline(be, dev, reps=64)
     atb_bytes, atb_ms = attention_batched(dev)
     oc_enc, oc_smp, oc_smp_h, oc_kernels = octo_leg(dev)
+    acfg = attention_configs(dev)
     assert be.device_error() == 0
 
     ms = np.array([s.elapsed_time(e) for s, e in zip(starts, ends)])
@@ -594,7 +658,15 @@ def main():
                               "us_per_launch": atb_ms * 1e3,
                               "achieved_gbs": atb_bytes / (atb_ms * 1e-3) / 1e9,
                               "frac_hbm": atb_bytes / (atb_ms * 1e-3) / 1e9 / hbm,
-                              "alg_bytes_per_launch": atb_bytes}},
+                              "alg_bytes_per_launch": atb_bytes},
+                          "configs": {n: {"warm_us": w, "cold_l2_us": c, "alg_bytes": nb,
+                                          "cold_gbs": nb / (c * 1e-6) / 1e9,
+                                          "cold_frac_hbm": nb / (c * 1e-6) / 1e9 / hbm,
+                                          "cold_tflops": fl / (c * 1e-6) / 1e12}
+                                      for n, (nb, fl, w, c) in acfg.items()},
+                          "configs_note": "rank 0's device times (CUDA events); cold = a 256 MB "
+                                          "buffer written before each launch, warm = back to back; "
+                                          "config 3 bytes over valid keys only"},
             "e2e": {"value": e2e_p50, "unit": "ms", "h2d_bytes_per_step": noise_h.numel() * 4,
                     "d2h_bytes_per_step": act_h.numel() * 4,
                     "path": "RDT1B.sample_host -> sfb_rdt1b_sample: pinned host noise -> device, "
