@@ -123,3 +123,43 @@ class Octo:
         torch.cuda.synchronize()
         _copy_d2d(out.data_ptr(), ptr.value, n.value * out.element_size())
         return out
+
+
+def _main(argv=None):
+    """Octo-Small latency run, the counterpart of the reference's
+    examples/octo_inference.cpp: encode (backbone over the reference's 0.1
+    tokens) then `--iters` samples of `num_steps` flow-matching steps in one
+    graph; device-timed medians in ms, one line of JSON."""
+    import argparse
+    import json
+    import statistics
+
+    ap = argparse.ArgumentParser(description=_main.__doc__)
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda:0")
+    m = Octo(default_config(), seed=1)
+    noise = torch.randn(1, m.cfg.action_horizon, m.cfg.action_dim, device=dev)
+    act = torch.empty_like(noise)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.iters)]
+        for a, b in ev:
+            a.record(stream); fn(); b.record(stream)
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+    enc = timed(lambda: m.encode())
+    smp = timed(lambda: m.sample(noise, act))
+    print(json.dumps({"encode_ms": enc, "sample_ms": smp, "sample_graph_kernels": m.graph_kernels(1),
+                      "finite": bool(torch.isfinite(act).all())}))
+    m.close()
+
+
+if __name__ == "__main__":
+    _main()
