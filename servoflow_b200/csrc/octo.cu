@@ -160,6 +160,37 @@ __global__ void euler_kernel(float* __restrict__ x, const float* __restrict__ v,
     }
 }
 
+// The Euler step of one sampling step fused with the head input of the next
+// (euler_kernel then head_input_kernel in one pass): the thread of column
+// c < HA updates x[b, c] exactly as euler_kernel does and writes its bf16
+// copy into the next input row; the other columns are filled as
+// head_input_kernel fills them.
+__global__ void euler_input_kernel(float* __restrict__ x, const float* __restrict__ v, int64_t ldv,
+                                   const __nv_bfloat16* __restrict__ cond, __nv_bfloat16* __restrict__ out,
+                                   int B, int HA, int tdim, int D, int Kp, float t_fill, float dt) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t n = static_cast<int64_t>(B) * Kp;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % Kp), b = static_cast<int>(i / Kp);
+        __nv_bfloat16 o;
+        if (c < HA) {
+            const int64_t xi = static_cast<int64_t>(b) * HA + c;
+            const float nx = __fadd_rn(x[xi], __fmul_rn(dt, v[b * ldv + c]));
+            x[xi] = nx;
+            o = __float2bfloat16_rn(nx);
+        } else if (c < HA + tdim) {
+            o = __float2bfloat16_rn(t_fill);
+        } else if (c < HA + tdim + D) {
+            o = cond[static_cast<int64_t>(b) * D + (c - HA - tdim)];
+        } else {
+            o = __float2bfloat16_rn(0.f);
+        }
+        out[i] = o;
+    }
+}
+
 // velocity[b, c] = v[b·ldv + c] for c < HA (drops fc3's padded lanes)
 __global__ void copy_velocity_kernel(const float* __restrict__ v, int64_t ldv, float* __restrict__ out, int B,
                                      int HA) {
@@ -391,25 +422,39 @@ static int backbone(Model& m, int B, cudaStream_t s) {
     return SFB_OK;
 }
 
-// OctoDiffusionHead::forward on m.xact with the current condition → m.vel.
-static int head(Model& m, int B, cudaStream_t s) {
-    const auto& c = m.c;
-    const int HA = m.HA();
+// The head's input rows from m.xact and the current condition (octo.cpp:150-160).
+static int head_input(Model& m, int B, cudaStream_t s) {
     prefer_max_shared(head_input_kernel);
-    SFB_TRY(launch_kernel(head_input_kernel, grid_for(static_cast<int64_t>(B) * m.kin_pad, 256), 256, 0, s, true,
-        m.xact, m.cond, m.hin, B, HA, kTimeDim, c.hidden, m.kin_pad, kFill));
+    return launch_kernel(head_input_kernel, grid_for(static_cast<int64_t>(B) * m.kin_pad, 256), 256, 0, s, true,
+        m.xact, m.cond, m.hin, B, m.HA(), kTimeDim, m.c.hidden, m.kin_pad, kFill);
+}
+
+// fc1 → GELU → fc2 → GELU → fc3 of OctoDiffusionHead::forward on m.hin → m.vel.
+static int head_mlp(Model& m, int B, cudaStream_t s) {
+    const auto& c = m.c;
     SFB_TRY(linear(m.h1, m.hin, m.kin_pad, B, m.hh1, c.head_hidden, 1, nullptr, s));
     SFB_TRY(linear(m.h2, m.hh1, c.head_hidden, B, m.hh2, c.head_hidden, 1, nullptr, s));
     return linear(m.h3, m.hh2, c.head_hidden, B, m.vel, m.out_pad, 0, nullptr, s, true);
 }
 
+// num_steps head evaluations and Euler steps; the Euler step of step i and the
+// head input of step i + 1 run as one kernel (4 kernels per step, plus one).
 static int sample_loop(Model& m, int B, cudaStream_t s) {
     prefer_max_shared(euler_kernel);
+    prefer_max_shared(euler_input_kernel);
+    SFB_TRY(head_input(m, B, s));
     for (int i = 0; i < m.c.num_steps; ++i) {
-        SFB_TRY(head(m, B, s));
+        SFB_TRY(head_mlp(m, B, s));
         const float dt = m.ts[i + 1] - m.ts[i];
-        SFB_TRY(launch_kernel(euler_kernel, grid_for(static_cast<int64_t>(B) * m.HA(), 256), 256, 0, s, true,
-            m.xact, static_cast<const float*>(m.vel), static_cast<int64_t>(m.out_pad), B, m.HA(), dt));
+        if (i + 1 < m.c.num_steps) {
+            SFB_TRY(launch_kernel(euler_input_kernel, grid_for(static_cast<int64_t>(B) * m.kin_pad, 256), 256, 0, s,
+                true, m.xact, static_cast<const float*>(m.vel), static_cast<int64_t>(m.out_pad),
+                static_cast<const __nv_bfloat16*>(m.cond), m.hin, B, m.HA(), kTimeDim, m.c.hidden, m.kin_pad,
+                kFill, dt));
+        } else {
+            SFB_TRY(launch_kernel(euler_kernel, grid_for(static_cast<int64_t>(B) * m.HA(), 256), 256, 0, s, true,
+                m.xact, static_cast<const float*>(m.vel), static_cast<int64_t>(m.out_pad), B, m.HA(), dt));
+        }
     }
     return SFB_OK;
 }
@@ -523,7 +568,8 @@ int sfb_octo_denoise_step(void* handle, int32_t sessions, const float* x_t, floa
     cudaError_t e = cudaMemcpyAsync(m->xact, x_t, static_cast<size_t>(sessions) * HA * 4,
                                     cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) { record_cuda_error(e, "octo denoise copy"); return SFB_ERR_CUDA; }
-    SFB_TRY(octo::head(*m, sessions, s));
+    SFB_TRY(octo::head_input(*m, sessions, s));
+    SFB_TRY(octo::head_mlp(*m, sessions, s));
     return launch_kernel(octo::copy_velocity_kernel, octo::grid_for(static_cast<int64_t>(sessions) * HA, 256), 256, 0, s,
                          true, static_cast<const float*>(m->vel), static_cast<int64_t>(m->out_pad), velocity,
                          sessions, HA);

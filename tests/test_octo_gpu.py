@@ -107,7 +107,8 @@ def test_set_condition_and_sampling_graph(setup):
     m.sample(noise.to(dev), outs[2], use_graph=True)       # replay
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
-    assert m.graph_kernels(2) == cfg.num_steps * 5           # head input, 3 projections, Euler step
+    # head input, then per step 3 projections and the Euler step fused with the next head input
+    assert m.graph_kernels(2) == 1 + cfg.num_steps * 4
     assert m.timesteps() == [float(t) for t in octo_ref.timesteps(cfg.num_steps)]
     ref = s["ref"].sample(noise, ctx.float())
     max_abs, cos = close(outs[2], ref)
