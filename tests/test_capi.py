@@ -71,6 +71,31 @@ int main(void) {
     assert got == want
 
 
+def _c_offsets(struct: str, fields):
+    """Offsets of `fields` and the size of `struct` as the C compiler lays them out."""
+    import tempfile
+    prints = ", ".join(f"offsetof({struct}, {f})" for f in fields)
+    src = ("#include <stddef.h>\n#include <stdio.h>\n#include \"sfb200.h\"\n"
+           f"int main(void) {{ printf(\"{'%zu ' * (len(fields) + 1)}\\n\", {prints}, sizeof({struct})); "
+           "return 0; }\n")
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(src)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe], check=True)
+        return list(map(int, subprocess.run([exe], capture_output=True, text=True).stdout.split()))
+
+
+def test_model_config_structs_match_header():
+    """The ctypes mirrors of sfb_rdt1b_config and sfb_octo_config have the C layout."""
+    from servoflow_b200.octo import OctoConfig
+    from servoflow_b200.rdt1b import RDT1BConfig
+    for struct, py in (("sfb_rdt1b_config", RDT1BConfig), ("sfb_octo_config", OctoConfig)):
+        fields = [f for f, _ in py._fields_]
+        want = [getattr(py, f).offset for f in fields] + [ctypes.sizeof(py)]
+        assert _c_offsets(struct, fields) == want, struct
+
+
 def test_null_args_rejected_without_device():
     # argument validation runs before any CUDA call
     assert _capi.lib().sfb_attention_fwd(None, None) == _capi.SFB_ERR_INVALID
