@@ -28,9 +28,14 @@ Reported beside the headline:
             the L2, so every launch reads HBM), GB/s and TFLOP/s vs the peaks.
   cpu_baseline / --impl reference
             the CPU oracle of the same network (oracle/rdt1b_ref.py, torch
-            fp32 on all host threads) on a bounded sample of blocks per step,
-            scaled to 28 blocks x 5 steps. The reference has no CPU path
-            (only its CUDA backend registers), so this restatement stands in.
+            fp32 on all host threads), each step one whole 5-step denoise.
+            The reference has no CPU path (only its CUDA backend registers),
+            so this restatement stands in.
+  attention.configs.*.ref_naive_us / ref_fa2_us
+            the reference's own CUDA attention on the same inputs: its naive
+            kernel (ops/attention.cu:90-139, oracle/_ref/libsfref.so) and its
+            FlashAttention-2 forward (oracle/_ref/libsfref_fa2.so), both
+            built from the reference's sources for sm_100a.
 
 Multi-GPU (torchrun, one process per GPU): each rank serves its own session
 (own weights, K/V cache and graph) with no collective on the hot path (weak
@@ -141,80 +146,86 @@ def dist_setup():
 
 
 # ── CPU oracle timing (cpu_baseline and --impl reference) ─────────────────────
-class CpuDenoiseSample:
-    """The CPU oracle network (oracle/rdt1b_ref.py) on the host cores: one
-    language block and one image block with their cross K/V cached (as the
-    per-tick cache does), timed one block at a time; a block's time scaled by
-    28 blocks x 5 steps gives the denoise estimate. The adaptors, embedders
-    and final layer (<1% of the FLOPs) are left out of the sample."""
+class CpuDenoise:
+    """The CPU oracle network (oracle/rdt1b_ref.py, fp32 torch) on the host
+    cores, running the whole config-4 denoise each call: state adaptor,
+    timestep/frequency embedders, all 28 blocks, final layer and the 5
+    DPM-Solver++ updates, with the per-tick cross-attention K/V cache held
+    (as the GPU runtime holds it). The reference has no CPU path (only its
+    CUDA backend registers), so this restatement stands in for it."""
 
     def __init__(self, threads, seed=0):
         import torch
-        from oracle.rdt1b_ref import RefRDT, random_block_weights
+        from oracle.rdt1b_ref import RefRDT, random_weights
         self.torch = torch
         torch.set_num_threads(threads)
         self.threads = torch.get_num_threads()
-        cfg = SimpleNamespace(hidden=HIDDEN, heads=HEADS, num_layers=2)
-        self.ref = RefRDT(random_block_weights(cfg, [0, 1], seed=seed), cfg)
-        g = torch.Generator().manual_seed(seed)
-        lang_c = torch.randn(1, LANG_LEN, HIDDEN, generator=g)
-        img_c = torch.randn(1, IMG_LEN, HIDDEN, generator=g)
+        cfg = SimpleNamespace(hidden=HIDDEN, heads=HEADS, num_layers=LAYERS, action_dim=ACTION,
+                              horizon=HORIZON, state_dim=ACTION, lang_dim=4096, img_dim=1152,
+                              max_lang_len=LANG_LEN, img_len=IMG_LEN, num_steps=STEPS, ctrl_freq=25)
+        self.ref = RefRDT(random_weights(cfg, seed=seed), cfg)
+        g = torch.Generator().manual_seed(seed + 1)
+        # the per-tick cache at the conditions' shapes (values do not matter for timing)
+        self.kv = [(torch.randn(1, LANG_LEN if l % 2 == 0 else IMG_LEN, HIDDEN, generator=g),
+                    torch.randn(1, LANG_LEN if l % 2 == 0 else IMG_LEN, HIDDEN, generator=g))
+                   for l in range(LAYERS)]
         self.lang_len = torch.randint(8, LANG_LEN + 1, (1,), generator=g)
-        with torch.inference_mode():
-            self.kv = [self.ref.cross_kv(l, lang_c, img_c) for l in (0, 1)]
-        self.x = torch.randn(1, TOKENS, HIDDEN, generator=g)
+        self.state = torch.randn(1, ACTION, generator=g)
+        self.noise = torch.randn(1, HORIZON, ACTION, generator=g)
 
-    def block(self, l):
-        """Seconds for block l (0: language, 1: image) on the current x."""
+    def denoise_ms(self):
+        """One full 5-step denoise; milliseconds."""
         with self.torch.inference_mode():
             t0 = time.perf_counter()
-            self.x = self.ref.block(self.x, l, *self.kv[l], self.lang_len)
-            return time.perf_counter() - t0
+            out = self.ref.sample(None, None, self.lang_len, self.state, self.noise, self.kv)
+            ms = (time.perf_counter() - t0) * 1e3
+        assert bool(self.torch.isfinite(out).all())
+        return ms
 
-    def denoise_ms(self, t_lang, t_img):
-        return (t_lang + t_img) / 2 * LAYERS * STEPS * 1e3
+    def sample_text(self, n):
+        return (f"{n} full config-4 denoise(s) (28 blocks x 5 DPM-Solver++ steps, adaptors, embedders, "
+                f"final layer; cross K/V cached), fp32 torch on {self.threads} threads, oracle/rdt1b_ref.py")
 
     def baseline(self, budget_s):
-        """cpu_baseline object: pairs of blocks until the time budget is spent."""
-        self.block(0); self.block(1)                  # warm-up
-        est = []
+        """cpu_baseline object: full denoises until the time budget is spent (at least one)."""
+        ts = []
         t_end = time.perf_counter() + budget_s
-        while time.perf_counter() < t_end or not est:
-            est.append(self.denoise_ms(self.block(0), self.block(1)))
-        return {"value": float(np.median(est)), "unit": "ms", "cores": self.threads, "kind": "port",
-                "sample": f"{len(est)} (language block + image block) pairs, fp32 torch on "
-                          f"{self.threads} threads, cross K/V cached; block time scaled x{LAYERS * STEPS} "
-                          "to 28 blocks x 5 steps (oracle/rdt1b_ref.py)"}
+        while time.perf_counter() < t_end or not ts:
+            ts.append(self.denoise_ms())
+        return {"value": float(np.median(ts)), "unit": "ms", "cores": self.threads, "kind": "port",
+                "sample": self.sample_text(len(ts))}
 
 
 def run_reference(args, world, rank):
-    """The CPU oracle of the denoise on the host CPU (rank 0 only)."""
+    """The CPU oracle of the whole denoise on the host CPU, rank 0 only: each
+    step is one full config-4 denoise. Steps stop early once the time budget
+    is spent; steps_measured says how many ran."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    s = CpuDenoiseSample(threads)
-    budget = 150.0                                  # seconds for warm-up + timed steps
+    s = CpuDenoise(threads)
+    budget = 240.0                                  # seconds for warm-up + timed steps
     t_start = time.perf_counter()
-    for i in range(args.warmup):
-        s.block(i % 2)
+    for _ in range(min(args.warmup, 1)):            # one warm-up denoise (each is a full pass)
+        s.denoise_ms()
     ts = []
-    for i in range(args.steps):                     # one (language, image) block pair per step
+    for _ in range(args.steps):
         if ts and time.perf_counter() - t_start > budget:
             break
-        ts.append((s.block(0) + s.block(1)) * (LAYERS // 2) * STEPS * 1e3)
+        ts.append(s.denoise_ms())
     p50 = float(np.median(ts))
     line = {
         "impl": "reference", "metric": METRIC, "value": p50, "unit": "ms", "n_gpus": world,
-        "steps": args.steps, "steps_measured": len(ts), "warmup": args.warmup,
+        "steps": args.steps, "steps_measured": len(ts), "warmup": min(args.warmup, 1),
         "ms_per_step": float(np.mean(ts)), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded",
-        "config": {"workload": "config 4: RDT-1B 5-step denoise, B=1 (28 blocks, hidden 2048, 32 heads, "
-                               "lang 1024 masked / image 4374 cross-attention, cross K/V cached)",
+        "config": {"workload": "config 4: full RDT-1B denoise, B=1 session per GPU, 28 blocks, hidden "
+                               "2048, 32 heads, lang 1024 (masked) / image 4374 cross-attention, "
+                               "5 DPM-Solver++ steps, condition K/V cache resident",
+                   "global_batch": 1, "seq_len": TOKENS,
                    "parallelism": f"host CPU, torch fp32, {s.threads} threads"},
         "cpu_baseline": {"value": p50, "unit": "ms", "cores": s.threads, "kind": "port",
-                         "sample": f"one (language block + image block) pair per step, "
-                                   f"time scaled x{(LAYERS // 2) * STEPS} to 28 blocks x 5 steps; "
-                                   "oracle/rdt1b_ref.py (the reference has no CPU backend)"},
+                         "sample": s.sample_text(len(ts)) + " per step"},
         "e2e": {"value": p50, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -381,33 +392,39 @@ def serving(dev, rank, batches, sessions=32):
 
 
 def attention_configs(dev, reps=50):
-    """Configs 1 and 3 of the attention path through the C ABI, each warm
-    (back to back, same inputs) and cold (a 256 MB buffer, twice the L2,
-    written between launches; only the attention launch is timed). Config 1:
-    self-attention, B=1, H=32, Lq=Lk=67, fp32 (and bf16). Config 3: masked
-    language cross-attention, B=16, H=32, Lq=67, Lk padded to 1024, valid
-    lengths L_b ~ U[8, 1024] (seeded), bf16; its bytes count valid keys only
-    (Q + O + K/V of L_b keys). Returns {name: (alg bytes, flops, warm us,
-    cold us)}."""
+    """Configs 1-3 of the attention path through the C ABI, each warm (back to
+    back, same inputs) and cold (a 256 MB buffer, twice the L2, written between
+    launches; only the attention launch is timed). Config 1: self-attention,
+    B=1, H=32, Lq=Lk=67, fp32 (and bf16). Config 2: image cross-attention, B=1,
+    Lk=4374, bf16. Config 3: masked language cross-attention, B=16, Lk padded
+    to 1024, valid lengths L_b ~ U[8, 1024] (seeded), bf16; its bytes count
+    valid keys only. Beside ours, on the same inputs: the reference's own CUDA
+    attention, its naive kernel (every dtype) and its FlashAttention-2 (bf16),
+    which ignore the mask (attention.cu:30) and so run config 3 over all 1024
+    keys. Returns {name: {alg_bytes, flops, warm_us, cold_us, ref_naive_*,
+    ref_fa2_*}}."""
     import ctypes
     import torch
+    from oracle import oracle
     from servoflow_b200 import _capi
     from servoflow_b200.backend import attention_args
     capi = _capi.lib()
+    naive = oracle.ref_lib()
+    fa2 = oracle.ref_fa2_lib()
     stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     g = torch.Generator().manual_seed(13)
     out = {}
 
-    def measure(a):
-        pa = ctypes.byref(a)
+    def measure(launch):
         for _ in range(5):
-            _capi.check(capi.sfb_attention_fwd(pa, stream.cuda_stream), "attention")
+            launch()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(reps):
-            capi.sfb_attention_fwd(pa, stream.cuda_stream)
+            launch()
         e1.record(stream)
         torch.cuda.synchronize()
         warm = e0.elapsed_time(e1) / reps * 1e3
@@ -416,29 +433,52 @@ def attention_configs(dev, reps=50):
         for i in range(reps):
             flush.fill_(i & 0xff)
             st[i].record(stream)
-            capi.sfb_attention_fwd(pa, stream.cuda_stream)
+            launch()
             en[i].record(stream)
         torch.cuda.synchronize()
         cold = float(np.median([x.elapsed_time(y) for x, y in zip(st, en)])) * 1e3
         return warm, cold
 
-    for name, dt in (("config1_self_fp32", torch.float32), ("config1_self_bf16", torch.bfloat16)):
-        q, k, v = (torch.randn(1, HEADS, TOKENS, 64, generator=g).to(dt).to(dev) for _ in range(3))
+    def ours(a):
+        pa = ctypes.byref(a)
+        return lambda: _capi.check(capi.sfb_attention_fwd(pa, sh), "attention")
+
+    def refs(q, k, v, o, entry):
+        B, H, Lq, D = q.shape
+        Lk = k.shape[2]
+        code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[q.dtype]
+        if naive is not None:
+            fn = lambda: naive.sfref_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                               code, B, H, Lq, Lk, D, 0.0, 0, sh)
+            entry["ref_naive_warm_us"], entry["ref_naive_cold_us"] = measure(fn)
+        if fa2 is not None and code != 0:
+            ws = torch.empty(fa2.sfref_fa2_workspace_bytes(B, H, Lq), dtype=torch.uint8, device=dev)
+            fn = lambda: fa2.sfref_fa2_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                                 code, B, H, Lq, Lk, D, 0.0, 0, ws.data_ptr(), ws.numel(), sh)
+            entry["ref_fa2_warm_us"], entry["ref_fa2_cold_us"] = measure(fn)
+
+    for name, dt, Lk in (("config1_self_fp32", torch.float32, TOKENS), ("config1_self_bf16", torch.bfloat16, TOKENS),
+                         ("config2_image_bf16", torch.bfloat16, IMG_LEN)):
+        q = torch.randn(1, HEADS, TOKENS, 64, generator=g).to(dt).to(dev)
+        k, v = (torch.randn(1, HEADS, Lk, 64, generator=g).to(dt).to(dev) for _ in range(2))
         o = torch.empty_like(q)
-        warm, cold = measure(attention_args(q, k, v, o))
         es = q.element_size()
-        out[name] = (4 * HEADS * TOKENS * 64 * es, 4.0 * HEADS * TOKENS * TOKENS * 64, warm, cold)
+        e = {"alg_bytes": 2 * HEADS * (TOKENS + Lk) * 64 * es, "flops": 4.0 * HEADS * TOKENS * Lk * 64}
+        e["warm_us"], e["cold_us"] = measure(ours(attention_args(q, k, v, o)))
+        refs(q, k, v, torch.empty_like(q), e)
+        out[name] = e
     B3 = 16
     lens = torch.randint(8, LANG_LEN + 1, (B3,), generator=g, dtype=torch.int32)
     q = torch.randn(B3, HEADS, TOKENS, 64, generator=g).bfloat16().to(dev)
     k = torch.randn(B3, HEADS, LANG_LEN, 64, generator=g).bfloat16().to(dev)
     v = torch.randn(B3, HEADS, LANG_LEN, 64, generator=g).bfloat16().to(dev)
     o = torch.empty_like(q)
-    lens_d = lens.to(dev)
-    warm, cold = measure(attention_args(q, k, v, o, mask=lens_d))
     sl = int(lens.sum())
-    out["config3_lang_masked_b16"] = (2 * B3 * HEADS * TOKENS * 64 * 2 + 2 * HEADS * 64 * 2 * sl,
-                                      4.0 * HEADS * TOKENS * 64 * sl, warm, cold)
+    e = {"alg_bytes": 2 * B3 * HEADS * TOKENS * 64 * 2 + 2 * HEADS * 64 * 2 * sl,
+         "flops": 4.0 * HEADS * TOKENS * 64 * sl}
+    e["warm_us"], e["cold_us"] = measure(ours(attention_args(q, k, v, o, mask=lens.to(dev))))
+    refs(q, k, v, torch.empty_like(q), e)
+    out["config3_lang_masked_b16"] = e
     del flush
     return out
 
@@ -659,14 +699,20 @@ def main():
                               "achieved_gbs": atb_bytes / (atb_ms * 1e-3) / 1e9,
                               "frac_hbm": atb_bytes / (atb_ms * 1e-3) / 1e9 / hbm,
                               "alg_bytes_per_launch": atb_bytes},
-                          "configs": {n: {"warm_us": w, "cold_l2_us": c, "alg_bytes": nb,
-                                          "cold_gbs": nb / (c * 1e-6) / 1e9,
-                                          "cold_frac_hbm": nb / (c * 1e-6) / 1e9 / hbm,
-                                          "cold_tflops": fl / (c * 1e-6) / 1e12}
-                                      for n, (nb, fl, w, c) in acfg.items()},
+                          "configs": {n: dict(e, cold_gbs=e["alg_bytes"] / (e["cold_us"] * 1e-6) / 1e9,
+                                              cold_frac_hbm=e["alg_bytes"] / (e["cold_us"] * 1e-6) / 1e9 / hbm,
+                                              cold_tflops=e["flops"] / (e["cold_us"] * 1e-6) / 1e12,
+                                              **({"speedup_vs_ref_fa2_cold": e["ref_fa2_cold_us"] / e["cold_us"]}
+                                                 if "ref_fa2_cold_us" in e else {}),
+                                              **({"speedup_vs_ref_naive_cold": e["ref_naive_cold_us"] / e["cold_us"]}
+                                                 if "ref_naive_cold_us" in e else {}))
+                                      for n, e in acfg.items()},
                           "configs_note": "rank 0's device times (CUDA events); cold = a 256 MB "
                                           "buffer written before each launch, warm = back to back; "
-                                          "config 3 bytes over valid keys only"},
+                                          "config 3 bytes over valid keys only; ref_naive / ref_fa2 = "
+                                          "the reference's own CUDA attention (naive kernel, "
+                                          "FlashAttention-2) built from its sources for sm_100a, same "
+                                          "inputs (config 3 unmasked: the reference drops masks)"},
             "e2e": {"value": e2e_p50, "unit": "ms", "h2d_bytes_per_step": noise_h.numel() * 4,
                     "d2h_bytes_per_step": act_h.numel() * 4,
                     "path": "RDT1B.sample_host -> sfb_rdt1b_sample: pinned host noise -> device, "
@@ -696,7 +742,7 @@ def main():
             "wall_s_device_loop": t_wall,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = CpuDenoiseSample(os.cpu_count() or 1).baseline(15.0)
+            line["cpu_baseline"] = CpuDenoise(os.cpu_count() or 1).baseline(15.0)
             ce, cs = octo_cpu(os.cpu_count() or 1)
             line["octo"]["cpu_oracle"] = {"encode_ms": ce, "sample_ms": cs, "cores": os.cpu_count() or 1,
                                           "kind": "port", "what": "oracle/octo_ref.py, fp32 torch"}

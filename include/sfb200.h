@@ -91,6 +91,14 @@ int sfb_copy_device(void* dst, const void* src, int64_t bytes);
  *   convention of the reference model (include/servoflow/models/rdt1b/
  *   dit_block.h:141,153); the reference backend ignores masks
  *   (attention.cu:30), this one applies them.
+ * - attn_mask (optional, device): the additive float mask of the reference's
+ *   interface, [B, 1, Sq, Sk] (ops/attention.h:16, backend.h:104; the
+ *   reference's Octo passes one, octo.cpp:79,209): the logit of (b, h, i, j)
+ *   becomes scale·q·k + attn_mask[b·attn_mask_stride[0] + i·attn_mask_stride[1] + j],
+ *   keys contiguous. A stride of 0 broadcasts that dimension ([1, 1, Sq, Sk],
+ *   [B, 1, 1, Sk]). attn_mask_dtype: SFB_F32, SFB_F16 or SFB_BF16; -inf masks a
+ *   key. It combines with kv_len, key_mask and is_causal. The base address and
+ *   the non-zero strides need no alignment.
  * - A query row whose keys are all masked produces zeros (torch SDPA would
  *   produce NaN).
  * - heads % heads_kv == 0 (grouped K/V heads, as flash_attn::mha_fwd's H_k).
@@ -128,6 +136,9 @@ typedef struct sfb_attn_args {
     int32_t num_splits;
     int32_t v_dtype;        /* 0: V has `dtype`; SFB_F16 with dtype SFB_BF16: V is already
                                fp16 (a cache stored in the P·V operand type: no conversion) */
+    int32_t attn_mask_dtype;      /* dtype of attn_mask (ignored when it is NULL) */
+    const void* attn_mask;        /* optional additive mask, see above */
+    int64_t attn_mask_stride[2];  /* element strides: batch, query row (0 = broadcast) */
 } sfb_attn_args;
 
 int sfb_attention_fwd(const sfb_attn_args* args, void* stream);

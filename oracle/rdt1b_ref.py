@@ -108,7 +108,13 @@ class RefRDT:
             o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
         return o.transpose(1, 2).reshape(B, Sq, D)
 
-    def forward(self, lang_c, img_c, lang_len, state, x_t, t):
+    def cross_kv_all(self, lang_c, img_c):
+        """Every block's cross-attention (K, V): the per-tick cache."""
+        return [self.cross_kv(l, lang_c, img_c) for l in range(self.c.num_layers)]
+
+    def forward(self, lang_c, img_c, lang_len, state, x_t, t, kv=None):
+        """One network evaluation; kv (optional) is cross_kv_all's cache,
+        otherwise each block projects its condition here."""
         c, w = self.c, self.w
         B, T, A = x_t.shape
         D, H = c.hidden, c.heads
@@ -119,7 +125,7 @@ class RefRDT:
         femb = self.lin(self.lin(sincos(c.ctrl_freq), "freq_embedder.mlp.0", "silu"), "freq_embedder.mlp.2")
         x = torch.cat([temb.expand(B, 1, D), femb.expand(B, 1, D), seq], 1) + w["x_pos_embed"].view(-1, D)
         for l in range(c.num_layers):
-            k, v = self.cross_kv(l, lang_c, img_c)
+            k, v = kv[l] if kv is not None else self.cross_kv(l, lang_c, img_c)
             x = self.block(x, l, k, v, lang_len)
         h = rms_norm(x, w["final_layer.norm_final.weight"])
         out = self.lin(self.lin(h, "final_layer.ffn_final.fc1", "gelu"), "final_layer.ffn_final.fc2")
@@ -155,11 +161,13 @@ class RefRDT:
         h = rms_norm(x, w[p + "norm3.weight"])
         return x + self.lin(self.lin(h, p + "ffn.fc1", "gelu"), p + "ffn.fc2")
 
-    def sample(self, lang_c, img_c, lang_len, state, noise):
+    def sample(self, lang_c, img_c, lang_len, state, noise, kv=None):
         ts, a, b, cc = dpm_schedule(self.c.num_steps)
+        if kv is None:
+            kv = self.cross_kv_all(lang_c, img_c)     # once per tick, as the runtime's cache
         x, x0_prev = noise.clone(), torch.zeros_like(noise)
         for i, t in enumerate(ts):
-            x0 = self.forward(lang_c, img_c, lang_len, state, x, t)
+            x0 = self.forward(lang_c, img_c, lang_len, state, x, t, kv)
             x = a[i] * x + b[i] * x0 + cc[i] * x0_prev
             x0_prev = x0
         return x
@@ -221,4 +229,29 @@ def random_block_weights(cfg, layers, seed: int = 0, std: float = 0.02) -> dict:
         for n in ("attn.q_norm", "attn.k_norm", "cross_attn.q_norm", "cross_attn.k_norm"):
             w[p + n + ".weight"] = 1 + torch.randn(64, generator=g) * std
         lin(p + "ffn.fc1", D, D); lin(p + "ffn.fc2", D, D)
+    return w
+
+
+def random_weights(cfg, seed: int = 0, std: float = 0.02) -> dict:
+    """fp32 weights N(0, std) for the whole network (every name load_weights
+    returns) at cfg's shapes: the CPU timing workload, whose values do not
+    matter for timing."""
+    g = torch.Generator().manual_seed(seed)
+    D = cfg.hidden
+    w = random_block_weights(cfg, range(cfg.num_layers), seed=seed + 1, std=std)
+
+    def lin(name, n, k):
+        w[name + ".weight"] = torch.randn(n, k, generator=g) * std
+        w[name + ".bias"] = torch.randn(n, generator=g) * std
+
+    lin("lang_adaptor.0", D, cfg.lang_dim); lin("lang_adaptor.2", D, D)
+    lin("img_adaptor.0", D, cfg.img_dim); lin("img_adaptor.2", D, D)
+    lin("state_adaptor.0", D, 2 * cfg.state_dim); lin("state_adaptor.2", D, D); lin("state_adaptor.4", D, D)
+    for e in ("t_embedder", "freq_embedder"):
+        lin(e + ".mlp.0", D, 256); lin(e + ".mlp.2", D, D)
+    w["x_pos_embed"] = torch.randn(cfg.horizon + 3, D, generator=g) * std
+    w["lang_cond_pos_embed"] = torch.randn(cfg.max_lang_len, D, generator=g) * std
+    w["img_cond_pos_embed"] = torch.randn(cfg.img_len, D, generator=g) * std
+    w["final_layer.norm_final.weight"] = 1 + torch.randn(D, generator=g) * std
+    lin("final_layer.ffn_final.fc1", D, D); lin("final_layer.ffn_final.fc2", cfg.action_dim, D)
     return w

@@ -31,13 +31,16 @@
  * kv_len (which the reference drops, attention.cu:30) are applied as −inf
  * logits, the torch SDPA boolean-mask convention of the reference's Python
  * oracle; a row with no visible key yields zeros (SDPA would give NaN);
- * K/V heads may be grouped (heads % heads_kv == 0).
+ * K/V heads may be grouped (heads % heads_kv == 0). amask (optional) is the
+ * additive float mask of IBackend::attention (ops/attention.h:16), expanded
+ * to [B, Lq, Lk]: it is added to the scaled logit, as torch SDPA adds a float
+ * attn_mask; a -inf entry drops the key.
  * Layout: contiguous [B, H, L, D] float arrays.
  */
 void sfo_attention(const float* q, const float* k, const float* v, float* out,
                    int B, int H, int Hkv, int Lq, int Lk, int D, float scale,
                    int causal, const int32_t* kv_len, const uint8_t* key_mask,
-                   int nthreads) {
+                   int nthreads, const float* amask) {
     if (scale == 0.f) scale = 1.f / sqrtf((float)D);
     const int64_t rows = (int64_t)B * H * Lq;
 #ifdef _OPENMP
@@ -63,6 +66,10 @@ void sfo_attention(const float* q, const float* k, const float* v, float* out,
             double dot = 0.0;
             for (int d = 0; d < D; ++d) dot += (double)qr[d] * (double)kb[(int64_t)j * D + d];
             dot *= (double)scale;
+            if (amask) {
+                dot += (double)amask[((int64_t)b * Lq + qi) * Lk + j];
+                if (isinf(dot) && dot < 0) continue;
+            }
             const double mn = dot > m ? dot : m;
             const double e_old = exp(m - mn);   /* m = -inf on the first key → 0 */
             const double e_new = exp(dot - mn);

@@ -55,6 +55,9 @@ class AttnArgs(ctypes.Structure):
         ("key_mask_stride_b", ctypes.c_int64),
         ("num_splits", ctypes.c_int32),
         ("v_dtype", ctypes.c_int32),
+        ("attn_mask_dtype", ctypes.c_int32),
+        ("attn_mask", ctypes.c_void_p),
+        ("attn_mask_stride", ctypes.c_int64 * 2),
     ]
 
 

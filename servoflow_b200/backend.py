@@ -55,8 +55,10 @@ def attention_args(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, out: torch
     """Fills sfb_attn_args from 4-D tensors.
 
     layout "bhsd": [B, H, S, D] (the reference layout); "bshd": [B, S, H, D].
-    mask: None, a bool/uint8 [B, Sk] key-padding mask (True = keep), or an
-    int32 [B] tensor of valid key lengths.
+    mask: None, a bool/uint8 [B, Sk] key-padding mask (True = keep), an
+    int32 [B] tensor of valid key lengths, or the reference interface's
+    additive float mask (fp32/fp16/bf16, 4-D [B or 1, 1, Sq or 1, Sk], added
+    to the scaled logits; -inf masks a key).
     """
     for t, n in ((Q, "Q"), (K, "K"), (V, "V"), (out, "out")):
         _check_device(t, n)
@@ -100,9 +102,19 @@ def attention_args(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, out: torch
                 raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "key mask must be [B, Sk], row-contiguous")
             a.key_mask = mask.data_ptr()
             a.key_mask_stride_b = mask.stride(0)
+        elif mask.dtype in (torch.float32, torch.float16, torch.bfloat16) and mask.dim() == 4:
+            mb, mh, mq, mk = mask.shape
+            if mb not in (1, a.batch) or mh != 1 or mq not in (1, a.seq_q) or mk != a.seq_k \
+                    or (mk > 1 and mask.stride(3) != 1):
+                raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "additive mask must be [B|1, 1, Sq|1, Sk]")
+            a.attn_mask = mask.data_ptr()
+            a.attn_mask_dtype = dtype_code(mask.dtype)
+            a.attn_mask_stride[0] = mask.stride(0) if mb > 1 else 0
+            a.attn_mask_stride[1] = mask.stride(2) if mq > 1 else 0
         else:
             raise _capi.SfbError(_capi.SFB_ERR_SHAPE,
-                                 "mask must be bool/uint8 [B, Sk] or int32 [B] lengths")
+                                 "mask must be bool/uint8 [B, Sk], int32 [B] lengths or a float "
+                                 "[B, 1, Sq, Sk] additive mask")
     return a
 
 

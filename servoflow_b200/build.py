@@ -20,6 +20,9 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC", "-shared",
+    # a soname, so that a library linked against libsfb200 (the servoflow
+    # binding) shares the copy a process has already loaded
+    "-Xlinker", "-soname=libsfb200.so",
 ]
 
 

@@ -22,6 +22,9 @@ struct AttnSimtParams {
     const int32_t* kv_len;
     const uint8_t* key_mask;
     int64_t mask_sb;
+    const void* amask;               // additive mask (element strides am_sb, am_ss; keys contiguous)
+    int32_t am_dt;
+    int64_t am_sb, am_ss;
 };
 
 namespace attn_simt {
@@ -95,6 +98,8 @@ attn_fwd_simt_kernel(const AttnSimtParams p) {
             for (int d = 0; d < DP; ++d) s = fmaf(sQ[row][d], sK[lane][d], s);
             s *= p.scale;
             const bool valid = kvalid && (!p.causal || kj <= qi);
+            if (valid && p.amask != nullptr && qi < p.Lq)
+                s += attn_mask_at(p.amask, p.am_dt, b * p.am_sb + qi * p.am_ss + kj);
             if (!valid) s = -INFINITY;
             float tmax = s;
 #pragma unroll
@@ -160,6 +165,8 @@ int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream) {
     p.causal = a.is_causal ? 1 : 0;
     p.scale = a.scale == 0.f ? 1.f / sqrtf(static_cast<float>(a.head_dim)) : a.scale;
     p.kv_len = a.kv_len; p.key_mask = a.key_mask; p.mask_sb = a.key_mask_stride_b;
+    p.amask = a.attn_mask; p.am_dt = a.attn_mask_dtype;
+    p.am_sb = a.attn_mask_stride[0]; p.am_ss = a.attn_mask_stride[1];
     switch (a.dtype) {
         case SFB_F32:  return launch_simt_t<float>(p, stream);
         case SFB_F16:  return launch_simt_t<__half>(p, stream);

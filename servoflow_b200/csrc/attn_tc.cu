@@ -72,6 +72,10 @@ struct AttnTcParams {
     const __nv_bfloat16* kn_w;       // the same for K rows, or null
     float    norm_eps;
     int32_t  kv_stream;              // K/V read once per use (a per-tick cache): L2 evict-first
+    const void* amask;               // additive mask, added to the scaled logits (keys contiguous)
+    int32_t  am_dt;
+    int64_t  am_sb, am_ss;           // element strides: batch, query row (0 = broadcast)
+    float    inv_scale;              // 1 / softmax scale: the mask enters the raw logits as m / scale
 #ifdef SFB_TRACE
     unsigned long long* trace;
     int dbg_skip;                    // timing experiments only: return at once
@@ -128,8 +132,10 @@ __host__ __device__ constexpr int bar_o(int u) { return 1 + 3 * kStages + 2 * kB
 __host__ __device__ constexpr int bar_og(int g) { return 1 + 3 * kStages + 3 * kBufs + g; }  // group's PV done
 constexpr int kBarQn = 3 + 3 * kStages + 3 * kBufs;                                        // Q rows normalised
 __host__ __device__ constexpr int bar_kn(int s) { return kBarQn + 1 + s; }                  // K rows normalised
-constexpr int kNumBars = kBarQn + 1 + kStages;
+constexpr int kBarDrain = kBarQn + 1 + kStages;                                            // failure path: MMAs done
+constexpr int kNumBars = kBarDrain + 1;
 static_assert(kNumBars <= 40, "barrier area");
+constexpr uint64_t kDrainNs = 100000000ull;        // bound of each wait for in-flight copies/MMAs after a failure
 
 // RMS-normalises row r (64 bf16) of a 128-byte-swizzled [128 × 64] tile in
 // place: x · 1/sqrt(mean(x²) + eps) · w, fp32 math, bf16 result. The sum of
@@ -266,6 +272,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         mbar_init(&bars[bar_og(1)], 1);
         mbar_init(&bars[kBarQn], 4);
         for (int s = 0; s < kStages; ++s) mbar_init(&bars[bar_kn(s)], kConvWarps);
+        mbar_init(&bars[kBarDrain], 1);
         fence_mbarrier_init();
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -286,6 +293,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem = *tmem_holder;
+    // split-K: announce this CTA as started; the wait before the first store
+    // into a peer's merge buffer then guarantees every peer is running
+    if (p.splits > 1) cluster_arrive_relaxed();
     pdl_trigger();                       // TMEM is held: the next kernel may start
     pdl_wait();                          // Q/K/V, key lengths and the output belong to earlier kernels
 #ifdef SFB_TRACE
@@ -465,6 +475,20 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                     if (__shfl_sync(0xffffffffu, expired, 0)) ok = false;
                 }
             }
+            if (!ok) {
+                // Failure path: the copies and MMAs this warp issued complete
+                // before the CTA releases its shared memory and TMEM. Q; K of
+                // the tiles whose S was not issued; V of those whose P·V was not
+                // (each wait bounded); then one commit covering every MMA.
+                mbar_wait(&bars[kBarQ], 0, kDrainNs);
+                for (int t = max(nS, nL - kStages); t < nL; ++t)
+                    mbar_wait(&bars[bar_k(t % kStages)], (t / kStages) & 1, kDrainNs);
+                for (int t = max(nP, nL - kStages); t < nL; ++t)
+                    mbar_wait(&bars[bar_v(t % kStages)], (t / kStages) & 1, kDrainNs);
+                if (elect_one()) mma_commit(&bars[kBarDrain]);
+                __syncwarp();
+                mbar_wait(&bars[kBarDrain], 0, kDrainNs);
+            }
         }
     } else if ((conv_v || p.kn_w != nullptr) && warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
         // ── K-norm / V conversion warps: K rows RMS-normalised in place, bf16 V
@@ -518,7 +542,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             wait(bar_s(u), (j / kBufs) & 1);
             SFB_T(3 + 4 * uses);
             tc_fence_after_sync();
-            const bool full = (key0 + kTileKeys <= kend) && !use_mask && !p.causal;
+            const bool full = (key0 + kTileKeys <= kend) && !use_mask && !p.causal && p.amask == nullptr;
             // pass 1: row max of the raw logits. In a tile with invalid keys
             // (beyond kv_len, masked, or causal) those logits are replaced by
             // -inf in TMEM first, so pass 2 is the same code for every tile.
@@ -536,6 +560,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                     for (int i = 0; i < 32; ++i) {
                         a[i]  = (va >> i) & 1u ? a[i] : -INFINITY;
                         bb[i] = (vb >> i) & 1u ? bb[i] : -INFINITY;
+                    }
+                    if (p.amask != nullptr && qi < p.Lq) {
+                        // additive mask: raw logit + m / scale, so that the later
+                        // scaling gives scale·q·k + m
+                        const int64_t mrow = static_cast<int64_t>(b) * p.am_sb + static_cast<int64_t>(qi) * p.am_ss;
+                        const int ka = key0 + 64 * hh, kb = ka + 32;
+#pragma unroll 4
+                        for (int i = 0; i < 32; ++i) {
+                            if ((va >> i) & 1u) a[i] = fmaf(attn_mask_at(p.amask, p.am_dt, mrow + ka + i), p.inv_scale, a[i]);
+                            if ((vb >> i) & 1u) bb[i] = fmaf(attn_mask_at(p.amask, p.am_dt, mrow + kb + i), p.inv_scale, bb[i]);
+                        }
                     }
                     tmem_st32(tS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(a));
                     tmem_st32(tS + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(bb));
@@ -663,6 +698,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         float* sO = reinterpret_cast<float*>(smem + kOffMerge);        // [C][slots][2][kOStride]
         float* sM = sO + C * slots * 2 * kOStride;                     // [C][slots]
         float* sL = sM + C * slots;                                    // [C][slots]
+        cluster_wait();                  // every peer has started (arrived after its setup)
         if (has_rows) {
             const int owner = row % C, slot = row / C;
             const uint32_t dO = dsmem_map(smem_u32(sO + ((split * slots + slot) * 2 + grp) * kOStride), owner);
@@ -805,6 +841,11 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnO
     p.kn_w = static_cast<const __nv_bfloat16*>(o.kn_w);
     p.norm_eps = o.norm_eps;
     p.kv_stream = o.v_f16 ? 1 : 0;   // the model's cross-attention cache
+    p.amask = a.attn_mask;
+    p.am_dt = a.attn_mask_dtype;
+    p.am_sb = a.attn_mask_stride[0];
+    p.am_ss = a.attn_mask_stride[1];
+    p.inv_scale = 1.f / scale;
     if ((o.qn_w || o.kn_w) && (a.dtype != SFB_BF16 || a.head_dim != 64)) return SFB_ERR_DTYPE;
 #ifdef SFB_TRACE
     p.tl = tl_buf();

@@ -85,6 +85,11 @@ int sfb_attention_fwd(const sfb_attn_args* a, void* stream) {
     if (a->num_splits < 0 || a->num_splits > 16) return SFB_ERR_INVALID;
     if (a->v_dtype != 0 && a->v_dtype != a->dtype && !(a->v_dtype == SFB_F16 && a->dtype == SFB_BF16))
         return SFB_ERR_DTYPE;
+    if (a->attn_mask != nullptr && a->attn_mask_dtype != SFB_F32 && a->attn_mask_dtype != SFB_F16 &&
+        a->attn_mask_dtype != SFB_BF16)
+        return SFB_ERR_DTYPE;
+    if (a->attn_mask != nullptr && (a->attn_mask_stride[0] < 0 || a->attn_mask_stride[1] < 0))
+        return SFB_ERR_SHAPE;
     if (a->batch == 0 || a->seq_q == 0) return SFB_OK;
     const sfb::DeviceInfo& dev = sfb::device_info();
     if (!sfb::is_sm100(dev)) return SFB_ERR_UNSUPPORTED;

@@ -412,14 +412,23 @@ template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16
 template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
 
 // One block per output row (the same method as the model's seeded init).
+// A NaN or infinite weight has no int8 value (fmaxf would skip a NaN and an
+// infinity would zero the rest of its row): such rows are counted in *bad and
+// the load fails.
 template <typename S>
 __global__ void quantize_rows_kernel(const S* __restrict__ w, int8_t* __restrict__ q, float* __restrict__ s,
-                                     int K) {
+                                     int K, int* __restrict__ bad) {
     const int r = blockIdx.x;
     const S* row = w + static_cast<int64_t>(r) * K;
     __shared__ float red[32];
     float mx = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(to_f32(row[k])));
+    bool finite = true;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = to_f32(row[k]);
+        finite = finite && isfinite(v);
+        mx = fmaxf(mx, fabsf(v));
+    }
+    if (__any_sync(0xffffffffu, !finite) && (threadIdx.x & 31) == 0) atomicAdd(bad, 1);
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
     __syncthreads();
@@ -548,6 +557,9 @@ static int load_file(Model& m, const char* path, LoadStats& st, std::set<std::st
         return e == cudaSuccess;
     };
     if (staging > 0) cuda_ok(cudaMalloc(&stage, staging), "checkpoint staging buffer");
+    int* bad = nullptr;                       // rows with a non-finite weight, per quantised tensor
+    if (rc == SFB_OK) cuda_ok(cudaMalloc(reinterpret_cast<void**>(&bad), sizeof(int)), "checkpoint flag");
+    std::string bad_name;
     for (const Job& j : jobs) {
         if (rc != SFB_OK) break;
         const TensorMeta& t = *j.t;
@@ -559,12 +571,13 @@ static int load_file(Model& m, const char* path, LoadStats& st, std::set<std::st
             continue;
         }
         if (!cuda_ok(cudaMemcpy(stage, src, bytes, cudaMemcpyHostToDevice), "checkpoint upload")) break;
+        if (j.kind == kQuant && !cuda_ok(cudaMemset(bad, 0, sizeof(int)), "checkpoint flag")) break;
         const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)));
         auto run = [&](auto* typed) {
             using S = std::remove_cv_t<std::remove_pointer_t<decltype(typed)>>;
             if (j.kind == kQuant)
                 quantize_rows_kernel<S><<<static_cast<unsigned>(j.rows), 256>>>(
-                    typed, static_cast<int8_t*>(j.dst), static_cast<float*>(j.dst2), static_cast<int>(j.cols));
+                    typed, static_cast<int8_t*>(j.dst), static_cast<float*>(j.dst2), static_cast<int>(j.cols), bad);
             else if (j.kind == kToBf16)
                 convert_kernel<S, __nv_bfloat16><<<grid, 256>>>(typed, static_cast<__nv_bfloat16*>(j.dst), n);
             else
@@ -575,11 +588,19 @@ static int load_file(Model& m, const char* path, LoadStats& st, std::set<std::st
         else run(static_cast<const __nv_bfloat16*>(stage));
         if (!cuda_ok(cudaGetLastError(), "checkpoint conversion launch")) break;
         // the staging buffer is reused by the next tensor
-        cuda_ok(cudaDeviceSynchronize(), "checkpoint conversion");
+        if (!cuda_ok(cudaDeviceSynchronize(), "checkpoint conversion")) break;
+        if (j.kind == kQuant) {
+            int nbad = 0;
+            if (!cuda_ok(cudaMemcpy(&nbad, bad, sizeof(int), cudaMemcpyDeviceToHost), "checkpoint flag")) break;
+            if (nbad != 0) { rc = SFB_ERR_RANGE; bad_name = t.name; break; }
+        }
     }
     if (rc == SFB_OK) cuda_ok(cudaDeviceSynchronize(), "checkpoint upload");
     if (stage != nullptr) cudaFree(stage);
+    if (bad != nullptr) cudaFree(bad);
     if (prev != m.device) cudaSetDevice(prev);
+    if (rc == SFB_ERR_RANGE)
+        return fail(rc, "checkpoint: '" + bad_name + "' holds a NaN or infinite weight (no int8 value)");
     if (rc != SFB_OK) return rc;
     for (const Job& j : jobs) {
         m.loaded.insert(j.name);
@@ -695,6 +716,7 @@ int sfb_rdt1b_config_from_json(const char* path, sfb_rdt1b_config* cfg) {
 int sfb_rdt1b_load_safetensors(void* handle, const char* path, int64_t* loaded, int64_t* ignored) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || path == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     rdt::LoadStats st;
     SFB_TRY(rdt::load_file(*m, path, st, nullptr));
     if (loaded) *loaded = st.loaded;
@@ -705,6 +727,7 @@ int sfb_rdt1b_load_safetensors(void* handle, const char* path, int64_t* loaded, 
 int sfb_rdt1b_params_missing(void* handle, int64_t* missing, char* first_missing, int32_t buflen) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || missing == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     int64_t n = 0;
     std::string first;
     for (const auto& kv : m->params)
@@ -723,6 +746,7 @@ int sfb_rdt1b_params_missing(void* handle, int64_t* missing, char* first_missing
 int sfb_rdt1b_load_checkpoint(void* handle, const char* dir, int64_t* loaded, int64_t* ignored) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || dir == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     DIR* d = ::opendir(dir);
     if (d == nullptr) return fail(SFB_ERR_IO, std::string("checkpoint directory not found: ") + dir);
     std::vector<std::string> files;

@@ -137,6 +137,13 @@ __device__ __forceinline__ void tl_record(unsigned long long* buf, int launch, i
 }
 #endif
 
+// Element idx of an additive attention mask of dtype dt (SFB_F32/F16/BF16).
+__device__ __forceinline__ float attn_mask_at(const void* m, int dt, int64_t idx) {
+    if (dt == SFB_F32) return static_cast<const float*>(m)[idx];
+    if (dt == SFB_F16) return __half2float(static_cast<const __half*>(m)[idx]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(m)[idx]);
+}
+
 // Options of the tensor-core attention launch beyond sfb_attn_args (model path).
 struct AttnOpts {
     bool pdl = false;              // programmatic dependent launch
@@ -145,6 +152,34 @@ struct AttnOpts {
     const void* kn_w = nullptr;    // the same for K rows
     float norm_eps = 1e-6f;
 };
+
+// Makes a model's device current for the guard's lifetime and restores the
+// caller's device afterwards, so a handle created on GPU k works from a thread
+// whose current device is another one (every model entry point opens one).
+struct DeviceGuard {
+    int prev = -1, status = SFB_OK;
+    bool switched = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) { (void)cudaGetLastError(); prev = -1; }
+        if (prev != dev) {
+            const cudaError_t e = cudaSetDevice(dev);
+            if (e != cudaSuccess) { record_cuda_error(e, "model device"); status = SFB_ERR_CUDA; }
+            else switched = true;
+        }
+    }
+    ~DeviceGuard() {
+        if (switched && prev >= 0 && cudaSetDevice(prev) != cudaSuccess) (void)cudaGetLastError();
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
+// Opens a model entry point: the model's lock (calls on one handle from
+// several threads are serialised on the host) and its device.
+#define SFB_MODEL_ENTRY(m)                                            \
+    std::lock_guard<std::recursive_mutex> _sfb_lock((m)->mu);         \
+    DeviceGuard _sfb_dev((m)->device);                                \
+    if (_sfb_dev.status != SFB_OK) return _sfb_dev.status
 
 // Returns the status of `expr` from the enclosing function unless it is SFB_OK.
 #define SFB_TRY(expr) do { int _rc = (expr); if (_rc != SFB_OK) return _rc; } while (0)

@@ -274,6 +274,7 @@ struct Model {
     __nv_bfloat16 *cond, *hin, *hh1, *hh2;             // head
     float *xact, *vel;                                  // x_t [B, H·A], fc3 output [B, out_pad]
     std::vector<float> ts;                              // num_steps + 1 timesteps
+    std::recursive_mutex mu;                  // entry points of one handle are serialised
     std::map<int, cudaGraphExec_t> graphs;
     std::map<int, int64_t> graph_kernels;
     cudaStream_t own = nullptr;
@@ -509,6 +510,7 @@ int sfb_octo_create(const sfb_octo_config* cfg, uint64_t seed, void** handle) {
 int sfb_octo_destroy(void* handle) {
     auto* m = sfb::octo::get(handle);
     if (m == nullptr) return SFB_ERR_INVALID;
+    DeviceGuard _sfb_dev(m->device);
     cudaDeviceSynchronize();
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -523,6 +525,7 @@ int sfb_octo_encode(void* handle, int32_t sessions, const void* tokens, void* fe
     using namespace sfb;
     auto* m = octo::get(handle);
     if (m == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int D = m->c.hidden, S = m->c.seq_len;
@@ -549,6 +552,7 @@ int sfb_octo_set_condition(void* handle, int32_t sessions, const void* context, 
     using namespace sfb;
     auto* m = octo::get(handle);
     if (m == nullptr || context == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     cudaError_t e = cudaMemcpyAsync(m->cond, context, static_cast<size_t>(sessions) * m->c.hidden * 2,
                                     cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
@@ -562,6 +566,7 @@ int sfb_octo_denoise_step(void* handle, int32_t sessions, const float* x_t, floa
     (void)t;   // the reference's head embeds a constant, not t (octo.cpp:147-148)
     auto* m = octo::get(handle);
     if (m == nullptr || x_t == nullptr || velocity == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int HA = m->HA();
@@ -580,6 +585,7 @@ int sfb_octo_sample(void* handle, int32_t sessions, const float* noise, float* a
     using namespace sfb;
     auto* m = octo::get(handle);
     if (m == nullptr || noise == nullptr || actions == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     cudaStream_t caller = static_cast<cudaStream_t>(stream);
     cudaStream_t s = m->own;
@@ -640,6 +646,7 @@ int sfb_octo_sample(void* handle, int32_t sessions, const float* noise, float* a
 int sfb_octo_timesteps(void* handle, float* timesteps, int32_t n) {
     auto* m = sfb::octo::get(handle);
     if (m == nullptr || timesteps == nullptr || n != m->c.num_steps + 1) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     for (int i = 0; i < n; ++i) timesteps[i] = m->ts[i];
     return SFB_OK;
 }
@@ -648,6 +655,7 @@ int sfb_octo_param(void* handle, const char* name, void** ptr, int64_t* numel, i
     auto* m = sfb::octo::get(handle);
     if (m == nullptr || name == nullptr || ptr == nullptr || numel == nullptr || dtype == nullptr)
         return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     auto it = m->params.find(name);
     if (it == m->params.end()) return SFB_ERR_INVALID;
     *ptr = it->second.first;
@@ -659,6 +667,7 @@ int sfb_octo_param(void* handle, const char* name, void** ptr, int64_t* numel, i
 int sfb_octo_graph_kernels(void* handle, int32_t sessions, int64_t* kernels) {
     auto* m = sfb::octo::get(handle);
     if (m == nullptr || kernels == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     auto it = m->graph_kernels.find(sessions);
     if (it == m->graph_kernels.end()) return SFB_ERR_INVALID;
     *kernels = it->second;

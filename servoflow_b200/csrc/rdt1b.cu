@@ -129,6 +129,7 @@ struct Model {
     __nv_bfloat16* enc_h;
     // DPM-Solver++ coefficients and timesteps
     std::vector<float> ca, cb, cc, tsteps;
+    std::recursive_mutex mu;                  // entry points of one handle are serialised
     std::map<int, cudaGraphExec_t> graphs;
     std::map<int, int64_t> graph_kernels;     // kernel nodes of each captured graph
     // the graph is captured and replayed on the model's own stream (capture is
@@ -491,6 +492,7 @@ int sfb_rdt1b_create(const sfb_rdt1b_config* cfg, uint64_t seed, void** handle) 
 int sfb_rdt1b_destroy(void* handle) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr) return SFB_ERR_INVALID;
+    DeviceGuard _sfb_dev(m->device);
     cudaDeviceSynchronize();
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -507,6 +509,7 @@ int sfb_rdt1b_encode(void* handle, int32_t sessions, const void* lang_tokens, co
     if (m == nullptr || lang_tokens == nullptr || lang_len == nullptr || img_tokens == nullptr ||
         state == nullptr)
         return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     return rdt::encode(*m, sessions, lang_tokens, lang_len, img_tokens, state,
                        static_cast<cudaStream_t>(stream));
@@ -516,6 +519,7 @@ int sfb_rdt1b_forward(void* handle, int32_t sessions, const float* x_t, float t,
                       void* stream) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || x_t == nullptr || x0_out == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t bytes = static_cast<size_t>(sessions) * m->c.horizon * m->c.action_dim * 4;
@@ -534,6 +538,7 @@ int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* 
                      int32_t use_graph, void* stream) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || noise == nullptr || actions == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
     cudaStream_t caller = static_cast<cudaStream_t>(stream);
     // all work runs on the model's stream, ordered after the caller's prior work
@@ -597,6 +602,7 @@ int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, 
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || name == nullptr || ptr == nullptr || numel == nullptr || dtype == nullptr)
         return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     auto it = m->params.find(name);
     if (it == m->params.end()) return SFB_ERR_INVALID;
     *ptr = it->second.first;
@@ -608,6 +614,7 @@ int sfb_rdt1b_param(void* handle, const char* name, void** ptr, int64_t* numel, 
 int sfb_rdt1b_graph_kernels(void* handle, int32_t sessions, int64_t* kernels) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || kernels == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     auto it = m->graph_kernels.find(sessions);
     if (it == m->graph_kernels.end()) return SFB_ERR_INVALID;
     *kernels = it->second;
@@ -618,6 +625,7 @@ int sfb_rdt1b_schedule(void* handle, float* timesteps, float* coef_a, float* coe
                        int32_t n) {
     auto* m = static_cast<rdt::Model*>(handle);
     if (m == nullptr || n != m->c.num_steps) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
     for (int i = 0; i < n; ++i) {
         if (timesteps) timesteps[i] = m->tsteps[i];
         if (coef_a) coef_a[i] = m->ca[i];

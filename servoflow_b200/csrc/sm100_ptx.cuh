@@ -355,6 +355,12 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint3
 __device__ __forceinline__ void cluster_arrive() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
+// Arrival without release semantics: marks this thread as started, so that a
+// later cluster_wait() in every CTA guarantees all peers are running before
+// their shared memory is written.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

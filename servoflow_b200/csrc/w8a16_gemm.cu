@@ -101,6 +101,8 @@ __host__ __device__ constexpr int bar_full_x(int s) { return kMaxStages + s; }  
 __host__ __device__ constexpr int bar_conv(int s)  { return 2 * kMaxStages + s; }    // W bf16 ready
 __host__ __device__ constexpr int bar_empty(int s) { return 3 * kMaxStages + s; }    // stage consumed by MMA
 constexpr int kBarAcc = 4 * kMaxStages;                                              // accumulator done
+constexpr int kBarDrain = kBarAcc + 1;             // failure path: every MMA issued so far has completed
+constexpr uint64_t kDrainNs = 100000000ull;        // bound of each wait for in-flight copies/MMAs after a failure
 
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;   // sqrt(2/pi), GELU tanh form
@@ -157,6 +159,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             mbar_init(&bars[bar_empty(s)], 1);
         }
         mbar_init(&bars[kBarAcc], 1);
+        mbar_init(&bars[kBarDrain], 1);
         fence_mbarrier_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
@@ -169,6 +172,9 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem = *tmem_holder;
+    // split-K: announce this CTA as started; the wait before the first store
+    // into a peer's shared memory then guarantees every peer is running
+    if constexpr (kSplit) cluster_arrive_relaxed();
     pdl_trigger();                                     // TMEM is held: the next kernel may start
 
 #ifdef SFB_TRACE
@@ -197,9 +203,12 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
 #ifdef SFB_TRACE
         tl_t1 = ptx::global_timer_ns();
 #endif
+        int issued = 0;                                 // chunks whose X load (and W load) is issued
         for (int c = 0; c < nch; ++c) {
             const int s = c % nst;
             if (c >= nst) wait(bar_empty(s), ((c / nst) - 1) & 1);
+            if (!ok) break;                             // a wait expired: issue nothing more
+            issued = c + 1;
             if (elect_one()) {
                 const int k0 = kchunk(c) * 64;
                 if (c >= nst) {
@@ -212,6 +221,14 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             }
             __syncwarp();
         }
+        // Copies in flight must land before the CTA releases its shared memory:
+        // wait (bounded, also after a failure) for the last stages issued. On the
+        // normal path the MMA warp has consumed them all and these return at once.
+        const int wissued = max(issued, pre);
+        for (int c = max(0, wissued - nst); c < wissued; ++c)
+            if (!mbar_wait(&bars[bar_full_w(c % nst)], (c / nst) & 1, kDrainNs)) ok = false;
+        for (int c = max(0, issued - nst); c < issued; ++c)
+            if (!mbar_wait(&bars[bar_full_x(c % nst)], (c / nst) & 1, kDrainNs)) ok = false;
     } else if (warp == 1) {
         // ── MMA issuer ──────────────────────────────────────────────────────
         const uint32_t idesc = idesc_f16(kTM, static_cast<uint32_t>(p.bn), 1, 0, 0);
@@ -219,6 +236,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             const int s = c % nst;
             wait(bar_conv(s), (c / nst) & 1);
             wait(bar_full_x(s), (c / nst) & 1);
+            if (!ok) break;                             // a wait expired: issue nothing more
             tc_fence_after_sync();
             const uint32_t aw = smem_u32(sWb(s)), ax = smem_u32(sX(s));
             if (elect_one()) {
@@ -232,6 +250,12 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                 if (c == nch - 1) mma_commit(&bars[kBarAcc]);
             }
             __syncwarp();
+        }
+        if (!ok) {
+            // every MMA issued so far completes before TMEM is released
+            if (elect_one()) mma_commit(&bars[kBarDrain]);
+            __syncwarp();
+            mbar_wait(&bars[kBarDrain], 0, kDrainNs);
         }
     } else {
         // ── converters: int8 [TM × 64] → bf16 SW128 [TM × 64] ────────────────
@@ -385,6 +409,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
         const int C = p.splits, R = kTM / C;
         const int slice = p.bn * R;
         float* rcv = reinterpret_cast<float*>(smem + p.rcv_off);
+        cluster_wait();                                 // every peer has started (arrived after its setup)
         if (epi) {
             const float bsplit = split == 0 ? bi : 0.f;     // the bias once, from CTA 0
             const int owner = trow / R, slot = trow - owner * R;

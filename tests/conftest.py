@@ -20,6 +20,7 @@ def _built():
 
     oracle.build()
     build.build_library()
+    oracle.build_binding()
     yield
 
 

@@ -3,10 +3,11 @@ the C ABI (servoflow_b200.backend → libsfb200.so).
 
 Tolerances (stated by the task for this path):
   fp32: max |ours − oracle| <= 1e-5.
-  bf16/fp16: max |ours − oracle| <= 2e-3 + ½ ulp of the output type at
-  |oracle| — the second term is the rounding of the result itself to
-  bf16/fp16, which any half-precision attention (the reference's FA2
-  included) incurs; it is ≤ 2e-3 for |out| < 0.5 (bf16).
+  bf16/fp16: max |ours − oracle| <= 2e-3 wherever |oracle| < 0.5, asserted
+  plainly. Where |oracle| >= 0.5 the bound is 2e-3 + ½ ulp of the output type
+  at |oracle|: rounding a bf16 result in [0.5, 1) alone moves it by up to
+  1.95e-3, which any bf16 attention (the reference's FA2 included) incurs.
+  Each check prints the plain max |ours − oracle| over all elements.
 The oracle always sees the same (rounded) inputs as the kernel.
 """
 import os
@@ -29,16 +30,22 @@ def half_ulp(x, dtype):
     return 0.5 * np.exp2(np.floor(np.log2(ax)) - mant)
 
 
-def check_close(out, ref, dtype):
+def check_close(out, ref, dtype, label=None):
     out = out.float().cpu().numpy()
     err = np.abs(out - ref)
     if dtype == torch.float32:
         tol = np.float32(1e-5)
     else:
         tol = 2e-3 + half_ulp(ref, dtype)
+        small = np.abs(ref) < 0.5
+        if small.any():
+            assert err[small].max() <= 2e-3, f"plain 2e-3 bound: max err {err[small].max():.3e}"
     bad = err > tol
     assert not np.isnan(out).any()
     assert not bad.any(), f"max err {err.max():.3e} at {np.unravel_index(err.argmax(), err.shape)}"
+    if label:
+        print(f"[parity] {label}: plain max |ours - oracle| = {err.max():.3e} "
+              f"(max |oracle| {np.abs(ref).max():.3f})")
     return float(err.max())
 
 
@@ -74,21 +81,21 @@ def be(gpu):
 def test_config1_self_attention_fp32(be, gpu):
     q, k, v = make(1, 32, 32, 67, 67, 64, torch.float32, 42, gpu)
     out = run(be, q, k, v, scale=0.125)
-    check_close(out, oracle_of(q, k, v, scale=0.125), torch.float32)
+    check_close(out, oracle_of(q, k, v, scale=0.125), torch.float32, "config 1 fp32")
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_config1_self_attention_half(be, gpu, dtype):
     q, k, v = make(1, 32, 32, 67, 67, 64, dtype, 43, gpu)
     out = run(be, q, k, v, scale=0.125)
-    check_close(out, oracle_of(q, k, v, scale=0.125), dtype)
+    check_close(out, oracle_of(q, k, v, scale=0.125), dtype, f"config 1 {dtype}")
 
 
 def test_config2_image_cross_attention(be, gpu):
     q, k, v = make(1, 32, 32, 67, 4374, 64, torch.bfloat16, 2, gpu)
     ref = oracle_of(q, k, v)
-    err = check_close(run(be, q, k, v), ref, torch.bfloat16)
-    assert err <= 2e-3   # |out| is small here: the plain bound holds
+    err = check_close(run(be, q, k, v), ref, torch.bfloat16, "config 2 bf16")
+    assert err <= 2e-3   # |out| is small here: the plain bound holds everywhere
     # K/V are reused across the 5 denoising steps: repeated calls are identical
     out2 = run(be, q, k, v)
     assert torch.equal(out2, run(be, q, k, v))
@@ -124,8 +131,8 @@ def test_config3_language_cross_attention_masked(be, gpu):
     keep = torch.arange(Lk)[None, :] < lens[:, None]
     ref = oracle_of(q, k, v, kv_len=lens.numpy())
     # key-padding mask form (bool [B, Lk]) and valid-length form (int32 [B])
-    check_close(run(be, q, k, v, mask=keep.to(gpu)), ref, torch.bfloat16)
-    check_close(run(be, q, k, v, mask=lens.to(gpu)), ref, torch.bfloat16)
+    check_close(run(be, q, k, v, mask=keep.to(gpu)), ref, torch.bfloat16, "config 3 bf16 (byte mask)")
+    check_close(run(be, q, k, v, mask=lens.to(gpu)), ref, torch.bfloat16, "config 3 bf16 (kv_len)")
 
 
 # ── golden vectors of the reference's oracle, through the GPU ─────────────────
@@ -220,6 +227,31 @@ def test_mask_with_holes_bf16(be, gpu):
     check_close(out, oracle_of(q, k, v, key_mask=keep.numpy()), torch.bfloat16)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("form", ["full", "batch1", "row1"])
+def test_additive_float_mask(be, gpu, dtype, form):
+    """The reference interface's additive mask [B, 1, Sq, Sk] (ops/attention.h:16,
+    backend.h:104), with its broadcast forms, in the mask's own dtype."""
+    B, Lq, Lk = 2, 67, 300
+    q, k, v = make(B, 4, 4, Lq, Lk, 64, dtype, 16, gpu)
+    shape = {"full": (B, 1, Lq, Lk), "batch1": (1, 1, Lq, Lk), "row1": (B, 1, 1, Lk)}[form]
+    g = torch.Generator().manual_seed(17)
+    m = torch.randn(shape, generator=g) * 2
+    m[torch.rand(shape, generator=g) < 0.3] = float("-inf")
+    m[..., 0] = 0.0
+    m = m.to(dtype)
+    out = run(be, q, k, v, mask=m.to(gpu))
+    check_close(out, oracle_of(q, k, v, attn_mask=m.float().numpy()), dtype)
+
+
+def test_zero_additive_mask_is_unmasked(be, gpu):
+    """The reference's Octo passes an all-zero fp16 [B, 1, S, S] mask
+    (octo.cpp:79,209): the result equals unmasked attention bit for bit."""
+    q, k, v = make(1, 6, 6, 64, 64, 64, torch.bfloat16, 18, gpu)
+    zero = torch.zeros(1, 1, 64, 64, dtype=torch.float16, device=gpu)
+    assert torch.equal(run(be, q, k, v, mask=zero), run(be, q, k, v))
+
+
 def test_error_codes(be, gpu):
     q, k, v = make(1, 4, 4, 67, 128, 64, torch.bfloat16, 1, gpu)
     out = torch.empty_like(q)
@@ -275,3 +307,32 @@ def test_reference_kernel_pins_oracle(gpu):
     B200Backend(0).attention(q, k, v, ours, scale=0.125)
     torch.cuda.synchronize()
     assert (ours - out).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("cfg", ["config1_bf16", "config1_fp16", "config2_bf16", "config3_bf16_unmasked"])
+def test_reference_fa2_pins_oracle(gpu, cfg):
+    """The reference's own FlashAttention-2 forward (oracle/_ref/libsfref_fa2.so,
+    its vendored FA2 built for sm_100a) on the same inputs as ours. FA2 rounds
+    P to the input type before P·V, so its own distance to the exact oracle is
+    larger than ours; both are printed. Config 3 runs without the mask: the
+    reference drops masks (attention.cu:30)."""
+    fa2 = oracle.ref_fa2_lib()
+    if fa2 is None:
+        pytest.skip("oracle/_ref/libsfref_fa2.so not built (needs the reference tree at build time)")
+    dtype = torch.float16 if "fp16" in cfg else torch.bfloat16
+    B, Lk = {"config1": (1, 67), "config2": (1, 4374), "config3": (16, 1024)}[cfg[:7]]
+    q, k, v = make(B, 32, 32, 67, Lk, 64, dtype, 77, gpu)
+    out = torch.empty_like(q)
+    ws = torch.empty(fa2.sfref_fa2_workspace_bytes(B, 32, 67), dtype=torch.uint8, device=gpu)
+    rc = fa2.sfref_fa2_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                 1 if dtype == torch.float16 else 2, B, 32, 67, Lk, 64, 0.0, 0,
+                                 ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
+    ref = oracle_of(q, k, v)
+    fa2_err = float(np.abs(out.float().cpu().numpy() - ref).max())
+    ours = run(B200Backend(0), q, k, v)
+    ours_err = check_close(ours, ref, dtype)
+    print(f"[parity] {cfg}: reference FA2 vs oracle {fa2_err:.3e}; ours vs oracle {ours_err:.3e}; "
+          f"ours vs FA2 {(ours.float() - out.float()).abs().max().item():.3e}")
+    assert fa2_err <= 1e-2          # the reference itself agrees with the oracle

@@ -52,8 +52,9 @@ def test_args_struct_layout_matches_header():
 #include <stdio.h>
 #include "sfb200.h"
 int main(void) {
-  printf("%zu %zu %zu %zu %zu\n", offsetof(sfb_attn_args, q_stride), offsetof(sfb_attn_args, batch),
+  printf("%zu %zu %zu %zu %zu %zu %zu\n", offsetof(sfb_attn_args, q_stride), offsetof(sfb_attn_args, batch),
          offsetof(sfb_attn_args, scale), offsetof(sfb_attn_args, key_mask_stride_b),
+         offsetof(sfb_attn_args, attn_mask), offsetof(sfb_attn_args, attn_mask_stride),
          sizeof(sfb_attn_args));
   return 0;
 }
@@ -67,7 +68,7 @@ int main(void) {
         got = list(map(int, subprocess.run([exe], capture_output=True, text=True).stdout.split()))
     A = _capi.AttnArgs
     want = [A.q_stride.offset, A.batch.offset, A.scale.offset, A.key_mask_stride_b.offset,
-            ctypes.sizeof(A)]
+            A.attn_mask.offset, A.attn_mask_stride.offset, ctypes.sizeof(A)]
     assert got == want
 
 

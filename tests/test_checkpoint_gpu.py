@@ -155,6 +155,14 @@ def test_missing_and_misshapen_tensors(gpu, converted, manifest, tmp_path):
         with pytest.raises(_capi.SfbError) as e:
             model.load_safetensors(str(bad))
         assert e.value.status == _capi.SFB_ERR_DTYPE
+        # a float weight holding a NaN or an infinity has no int8 value: the load fails
+        for bad_value in (float("nan"), float("inf")):
+            w = torch.randn(cfg.hidden, cfg.hidden) * 0.02
+            w[5, 17] = bad_value
+            save_file({"blocks.0.attn.proj.weight": w}, str(bad))
+            with pytest.raises(_capi.SfbError) as e:
+                model.load_safetensors(str(bad))
+            assert e.value.status == _capi.SFB_ERR_RANGE and "blocks.0.attn.proj.weight" in str(e.value)
     finally:
         model.close()
 

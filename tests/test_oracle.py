@@ -76,6 +76,24 @@ def test_kv_len_and_gqa_match_sdpa():
     assert np.abs(out - ref).max() <= 1e-6
 
 
+@pytest.mark.parametrize("shape", [(2, 1, 9, 40), (1, 1, 9, 40), (2, 1, 1, 40)])
+def test_additive_mask_matches_sdpa(shape):
+    """The float [B, 1, Sq, Sk] mask of IBackend::attention (ops/attention.h:16),
+    added to the scaled logits as torch SDPA adds a float attn_mask; -inf drops
+    a key. Broadcast forms [1, 1, Sq, Sk] and [B, 1, 1, Sk] included."""
+    rng = np.random.default_rng(sum(shape))
+    B, H, Lq, Lk = 2, 3, 9, 40
+    q = rng.standard_normal((B, H, Lq, 64), dtype=np.float32)
+    k = rng.standard_normal((B, H, Lk, 64), dtype=np.float32)
+    v = rng.standard_normal((B, H, Lk, 64), dtype=np.float32)
+    m = rng.standard_normal(shape).astype(np.float32) * 2
+    m[rng.random(shape) < 0.25] = -np.inf
+    m[..., 0] = 0.0                        # every row keeps a key
+    ref = sdpa(q, k, v, mask=torch.from_numpy(m).double())
+    out = oracle.attention(q, k, v, attn_mask=m)
+    assert np.abs(out - ref).max() <= 1e-6
+
+
 def test_fully_masked_row_is_zero():
     q = np.ones((2, 1, 3, 64), np.float32)
     out = oracle.attention(q, q, q, kv_len=np.array([0, 3], np.int32))
