@@ -240,6 +240,14 @@ int sfb_rdt1b_forward(void* handle, int32_t sessions, const float* x_t, float t,
  * replayed afterwards. */
 int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* actions,
                      int32_t use_graph, void* stream);
+/* Execution path of a one-session call (sessions == 1): 0 (the default) runs
+ * each run of projections between two attentions as one launch of the
+ * persistent projection kernel, with the pre-norms folded into it; 1 runs one
+ * kernel per projection and per norm (the path every batch of two or more
+ * sessions takes). Results agree within the model's tolerance, not bit for
+ * bit. Changing it drops the captured graphs. No counterpart in the
+ * reference. */
+int sfb_rdt1b_set_path(void* handle, int32_t path);
 /* Kernel launches in the captured sampling graph for `sessions` (known after
  * the first use_graph call for that session count). Diagnostic; no
  * counterpart in the reference. */

@@ -137,6 +137,20 @@ struct Model {
     cudaStream_t own = nullptr;
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
 
+    // One session (B = 1): runs of consecutive projections between two
+    // attention kernels go through the persistent projection kernel
+    // (rdt_dense.cu) as stage tables built once here. dl[0] is block 0's
+    // qkv; then, per block l, dl[1 + 2l] = (proj, cross q) and
+    // dl[2 + 2l] = (cross proj, fc1, fc2, next qkv or the final layer).
+    struct DenseLaunch { int first, count, ctr; };
+    bool dense_ok = false;
+    int path = 0;                             // 0: persistent kernel at one session; 1: per-projection kernels
+    DenseStage* d_stages = nullptr;           // device copy of the stage table
+    unsigned long long* d_ctr = nullptr;      // completion counters, 1 + count per launch
+    std::vector<DenseLaunch> dl;
+    __nv_bfloat16* xg = nullptr;              // bf16(x · g) of the next pre-norm, [S, D]
+    float* ss = nullptr;                      // partial Σ x² per token row, [D / 16][80]
+
     int S() const { return c.horizon + 3; }
 };
 
@@ -216,6 +230,72 @@ static void dpm_coefficients(Model& m) {
     }
 }
 
+// The stage tables of the one-session path (see Model::dl). Without a
+// device that can hold the kernel's clusters, the path stays off.
+static int build_dense(Model& m) {
+    const auto& c = m.c;
+    const int D = c.hidden, S = m.S(), L = c.num_layers, A = c.action_dim;
+    if (S > 80 || D % 256 != 0 || D / 64 / 4 > 8 || A % 64 != 0) return SFB_OK;
+    if (dense_clusters(device_info()) <= 0) return SFB_OK;
+    std::vector<DenseStage> st;
+    auto stage = [&](const Linear& Lw, const __nv_bfloat16* x, int TM, int act, void* y, int64_t ldy, bool y_f32,
+                     const __nv_bfloat16* res, const float* ss_in, int n_ss_in, const __nv_bfloat16* g_next) {
+        DenseStage d;
+        std::memset(&d, 0, sizeof(d));
+        SFB_TRY(dense_stage_init(d, x, D, S, Lw.w, Lw.N, Lw.K, TM));
+        d.w_scale = Lw.s; d.bias = Lw.b; d.residual = res; d.ldr = D;
+        d.y = y; d.ldy = ldy; d.y_f32 = y_f32 ? 1 : 0; d.act = act;
+        d.ss_in = ss_in; d.n_ss_in = n_ss_in; d.eps = 1e-6f;
+        if (g_next != nullptr) { d.g_next = g_next; d.xg = m.xg; d.ldg = D; d.ss_out = m.ss; }
+        st.push_back(d);
+        return SFB_OK;
+    };
+    const int nss = (D / 64) * 4;             // partials of an N = D stage with 64-row tiles
+    int nctr = 0;
+    auto launch = [&](int first) {
+        const int n = static_cast<int>(st.size()) - first;
+        m.dl.push_back({first, n, nctr});
+        nctr += 1 + n;
+    };
+    m.dl.clear();
+    int f = 0;
+    SFB_TRY(stage(m.blocks[0].qkv, m.xg, 128, 0, m.qkv, 3 * D, false, nullptr, m.ss, 1, nullptr));
+    launch(f);
+    for (int l = 0; l < L; ++l) {
+        const Block& bl = m.blocks[l];
+        f = static_cast<int>(st.size());
+        SFB_TRY(stage(bl.proj, m.attn, 64, 0, m.x, D, false, m.x, nullptr, 0, bl.norm2));
+        SFB_TRY(stage(bl.cq, m.xg, 64, 0, m.h, D, false, nullptr, m.ss, nss, nullptr));
+        launch(f);
+        f = static_cast<int>(st.size());
+        SFB_TRY(stage(bl.cproj, m.attn, 64, 0, m.x, D, false, m.x, nullptr, 0, bl.norm3));
+        SFB_TRY(stage(bl.fc1, m.xg, 64, 1, m.h, D, false, nullptr, m.ss, nss, nullptr));
+        SFB_TRY(stage(bl.fc2, m.h, 64, 0, m.x, D, false, m.x, nullptr, 0,
+                      l + 1 < L ? m.blocks[l + 1].norm1 : m.norm_final));
+        if (l + 1 < L) {
+            SFB_TRY(stage(m.blocks[l + 1].qkv, m.xg, 128, 0, m.qkv, 3 * D, false, nullptr, m.ss, nss, nullptr));
+        } else {
+            SFB_TRY(stage(m.fin1, m.xg, 64, 1, m.h, D, false, nullptr, m.ss, nss, nullptr));
+            SFB_TRY(stage(m.fin2, m.h, 64, 0, m.yfin, A, true, nullptr, nullptr, 0, nullptr));
+        }
+        launch(f);
+    }
+    SFB_TRY(dalloc(m, reinterpret_cast<void**>(&m.d_stages), st.size() * sizeof(DenseStage)));
+    SFB_TRY(dalloc(m, reinterpret_cast<void**>(&m.d_ctr), static_cast<size_t>(nctr) * 8));
+    if (cudaMemcpy(m.d_stages, st.data(), st.size() * sizeof(DenseStage), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(m.d_ctr, 0, static_cast<size_t>(nctr) * 8) != cudaSuccess) {
+        record_cuda_error(cudaGetLastError(), "dense stage table");
+        return SFB_ERR_CUDA;
+    }
+    m.dense_ok = true;
+    return SFB_OK;
+}
+
+static int dense(const Model& m, int i, cudaStream_t s) {
+    const Model::DenseLaunch& d = m.dl[i];
+    return dense_launch(m.d_stages + d.first, d.count, m.d_ctr + d.ctr, m.S(), s, true);
+}
+
 static int create(Model& m) {
     const auto& c = m.c;
     const int D = c.hidden, B = c.max_sessions, S = m.S();
@@ -283,7 +363,10 @@ static int create(Model& m) {
     SFB_TRY(f32(&m.x0prev, static_cast<int64_t>(B) * c.horizon * A));
     const int64_t enc_rows = static_cast<int64_t>(B) * std::max(c.max_lang_len, c.img_len);
     SFB_TRY(bf(&m.enc_h, enc_rows * D));
+    SFB_TRY(bf(&m.xg, static_cast<int64_t>(S) * D));
+    SFB_TRY(f32(&m.ss, static_cast<int64_t>(D / 16) * 80));
     dpm_coefficients(m);
+    SFB_TRY(build_dense(m));
     if (cudaStreamCreateWithFlags(&m.own, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&m.ev_in, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&m.ev_out, cudaEventDisableTiming) != cudaSuccess) {
@@ -403,6 +486,29 @@ static int forward(Model& m, int B, float t, cudaStream_t s, int step = -1) {
     SFB_TRY(launch_kernel(rdt::assemble_x_kernel, grid_for(static_cast<int64_t>(M) * D / 8, 256), 256, 0, s, true,
         temb, m.femb, m.seq, m.x_pos, m.x, B, S, D));
 
+    if (B == 1 && m.dense_ok && m.path == 0) {
+        // one session: the projections between attentions run as stages of the
+        // persistent kernel, the pre-norms folded into them
+        prefer_max_shared(rdt::norm_prep_kernel);
+        SFB_TRY(launch_kernel(rdt::norm_prep_kernel, (S + 7) / 8, 256, 0, s, true,
+            m.x, static_cast<int64_t>(D), m.blocks[0].norm1, m.xg, static_cast<int64_t>(D), m.ss, S, D));
+        SFB_TRY(dense(m, 0, s));
+        for (int l = 0; l < c.num_layers; ++l) {
+            const Block& bl = m.blocks[l];
+            SFB_TRY(attention(m, m.qkv, static_cast<int64_t>(S) * 3 * D, 3 * D, m.qkv + D, m.qkv + 2 * D,
+                              static_cast<int64_t>(S) * 3 * D, 3 * D, m.attn, B, S, S, nullptr, false,
+                              bl.qn, bl.kn, s));
+            SFB_TRY(dense(m, 1 + 2 * l, s));
+            const bool lang_blk = (l % 2 == 0);
+            const int Lk = lang_blk ? c.max_lang_len : c.img_len;
+            SFB_TRY(attention(m, m.h, static_cast<int64_t>(S) * D, D, m.kv[l], m.kv[l] + D,
+                              static_cast<int64_t>(Lk) * 2 * D, 2 * D, m.attn, B, S, Lk,
+                              lang_blk ? m.lang_len : nullptr, true, bl.cqn, nullptr, s));
+            SFB_TRY(dense(m, 2 + 2 * l, s));
+        }
+        return SFB_OK;
+    }
+
     for (int l = 0; l < c.num_layers; ++l) {
         const Block& bl = m.blocks[l];
         // x = x + proj(attn(qk-norm(qkv(norm1(x)))))
@@ -478,6 +584,9 @@ int sfb_rdt1b_create(const sfb_rdt1b_config* cfg, uint64_t seed, void** handle) 
     if (m == nullptr) return SFB_ERR_CUDA;
     m->c = c;
     m->seed = seed;
+    // SFB_RDT1B_PATH=1 selects the per-projection kernels at one session by
+    // default (sfb_rdt1b_set_path changes it per handle)
+    if (const char* e = std::getenv("SFB_RDT1B_PATH")) m->path = std::strcmp(e, "1") == 0 ? 1 : 0;
     cudaGetDevice(&m->device);
     const int rc = rdt::create(*m);
     if (rc != SFB_OK) {
@@ -594,6 +703,22 @@ int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* 
         cudaEventRecord(m->ev_out, s) != cudaSuccess || cudaStreamWaitEvent(caller, m->ev_out, 0) != cudaSuccess) {
         record_cuda_error(cudaGetLastError(), "rdt1b sample output");
         return SFB_ERR_CUDA;
+    }
+    return SFB_OK;
+}
+
+int sfb_rdt1b_set_path(void* handle, int32_t path) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || path < 0 || path > 1) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
+    if (path != m->path) {
+        // captured graphs hold the other path's kernels
+        cudaError_t e = cudaStreamSynchronize(m->own);
+        for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+        m->graphs.clear();
+        m->graph_kernels.clear();
+        m->path = path;
+        if (e != cudaSuccess) { record_cuda_error(e, "rdt1b set path"); return SFB_ERR_CUDA; }
     }
     return SFB_OK;
 }

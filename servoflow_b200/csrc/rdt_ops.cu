@@ -289,6 +289,38 @@ __global__ void bf16_to_f16_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, in
     if (bad) atomicExch(&g_sfb_device_error, SFB_ERR_RANGE);
 }
 
+// The inputs of a norm folded into the next projection (the persistent
+// projection kernel): per row m, ss[m] = Σ_k x[m,k]² (fp32 of the bf16
+// values) and xg[m, :] = bf16(x[m, :] · g). Warp per row; D % 256 == 0.
+__global__ void norm_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                 const __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ xg,
+                                 int64_t ldg, float* __restrict__ ss, int rows, int D) {
+    pdl_trigger();
+    pdl_wait();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const __nv_bfloat16* xr = x + warp * ldx;
+    float a = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+        const uint4 gu = *reinterpret_cast<const uint4*>(g + c);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const __nv_bfloat162* gg = reinterpret_cast<const __nv_bfloat162*>(&gu);
+        uint4 o;
+        __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]), w = __bfloat1622float2(gg[i]);
+            a = fmaf(f.x, f.x, fmaf(f.y, f.y, a));
+            ho[i] = __floats2bfloat162_rn(f.x * w.x, f.y * w.y);
+        }
+        *reinterpret_cast<uint4*>(xg + warp * ldg + c) = o;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) ss[warp] = a;
+}
+
 }  // namespace rdt
 
 // One warp waits, with the bounded mbarrier wait every kernel uses, on a

@@ -36,6 +36,7 @@ def _declare(lib):
     lib.sfb_rdt1b_schedule.argtypes = [c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p,
                                        c.c_int32]
     lib.sfb_rdt1b_graph_kernels.argtypes = [c.c_void_p, c.c_int32, c.POINTER(c.c_int64)]
+    lib.sfb_rdt1b_set_path.argtypes = [c.c_void_p, c.c_int32]
     lib.sfb_rdt1b_config_from_json.argtypes = [c.c_char_p, c.POINTER(RDT1BConfig)]
     lib.sfb_rdt1b_load_safetensors.argtypes = [c.c_void_p, c.c_char_p, c.POINTER(c.c_int64),
                                                c.POINTER(c.c_int64)]
@@ -43,7 +44,7 @@ def _declare(lib):
                                               c.POINTER(c.c_int64)]
     lib.sfb_rdt1b_params_missing.argtypes = [c.c_void_p, c.POINTER(c.c_int64), c.c_char_p, c.c_int32]
     for f in ("default_config", "create", "destroy", "encode", "forward", "sample", "param",
-              "schedule", "graph_kernels", "config_from_json", "load_safetensors", "load_checkpoint",
+              "schedule", "graph_kernels", "set_path", "config_from_json", "load_safetensors", "load_checkpoint",
               "params_missing"):
         getattr(lib, "sfb_rdt1b_" + f).restype = c.c_int
     lib._rdt_declared = True
@@ -107,6 +108,11 @@ class RDT1B:
         assert not noise.is_cuda and not out.is_cuda
         _capi.check(self.lib.sfb_rdt1b_sample(self.h, noise.shape[0], noise.data_ptr(), out.data_ptr(),
                                               1, _sh(stream)), "rdt1b sample")
+
+    def set_path(self, path: int) -> None:
+        """One-session execution path: 0 persistent projection kernel (default),
+        1 one kernel per projection and norm (sfb_rdt1b_set_path)."""
+        _capi.check(self.lib.sfb_rdt1b_set_path(self.h, int(path)), "set_path")
 
     def graph_kernels(self, sessions: int = 1) -> int:
         """Kernel launches in the captured sampling graph for `sessions`."""

@@ -146,3 +146,63 @@ def test_api_errors(setup):
     m.forward(noise, 999.0, y)
     torch.cuda.synchronize()
     assert torch.isfinite(y).all()
+
+
+@pytest.fixture(scope="module")
+def one(gpu):
+    """One session (the persistent projection kernel's path) at full width,
+    3 blocks (language, image, language), short conditions."""
+    cfg = default_config(num_layers=3, max_lang_len=96, img_len=300, max_sessions=1)
+    model = RDT1B(cfg, seed=4321)
+    g = torch.Generator().manual_seed(44)
+    lang = torch.randn(1, cfg.max_lang_len, cfg.lang_dim, generator=g).bfloat16()
+    img = torch.randn(1, cfg.img_len, cfg.img_dim, generator=g).bfloat16()
+    state = torch.randn(1, cfg.state_dim, generator=g).bfloat16()
+    lens = torch.tensor([51], dtype=torch.int32)
+    noise = torch.randn(1, cfg.horizon, cfg.action_dim, generator=g)
+    model.encode(lang.to(gpu), lens.to(gpu), img.to(gpu), state.to(gpu))
+    torch.cuda.synchronize()
+    ref = rdt1b_ref.RefRDT(rdt1b_ref.load_weights(model, cfg), cfg)
+    lang_c, img_c = ref.encode(lang.float(), img.float())
+    yield dict(cfg=cfg, model=model, ref=ref, state=state, lens=lens, noise=noise, lang_c=lang_c,
+               img_c=img_c, dev=gpu)
+    model.close()
+
+
+def test_one_session_paths_match_oracle(one):
+    """Path 0 (persistent projection kernel, norms folded in) and path 1 (one
+    kernel per projection) both meet the bar against the oracle, and agree
+    with each other."""
+    s = one
+    noise = s["noise"].to(s["dev"])
+    outs = []
+    for path in (0, 1):
+        s["model"].set_path(path)
+        y = torch.empty_like(noise)
+        s["model"].forward(noise, 999.0, y)
+        torch.cuda.synchronize()
+        outs.append(y)
+    s["model"].set_path(0)
+    ref = s["ref"].forward(s["lang_c"], s["img_c"], s["lens"], s["state"].float(), s["noise"], 999)
+    for path, y in enumerate(outs):
+        max_abs, cos = close(y, ref)
+        print(f"[parity] one session, path {path}: max |d| {max_abs:.3e}, cos {cos:.7f}")
+        assert max_abs < 0.05 and cos > 0.9999, (path, max_abs, cos)
+    max_abs, cos = close(outs[0], outs[1].cpu())
+    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+
+
+def test_one_session_graph_replays_are_identical(one):
+    s = one
+    noise = s["noise"].to(s["dev"])
+    eager, first, replay = (torch.empty_like(noise) for _ in range(3))
+    s["model"].sample(noise, eager, use_graph=False)
+    s["model"].sample(noise, first, use_graph=True)
+    s["model"].sample(noise, replay, use_graph=True)
+    torch.cuda.synchronize()
+    assert torch.equal(eager, first) and torch.equal(first, replay)
+    ref = s["ref"].sample(s["lang_c"], s["img_c"], s["lens"], s["state"].float(), s["noise"])
+    max_abs, cos = close(replay, ref)
+    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+    from servoflow_b200.backend import B200Backend
+    assert B200Backend(0).device_error(reset=True) == 0
