@@ -175,8 +175,8 @@ int sfb_dequantize_int8(const int8_t* in, const void* scale, int32_t scale_dtype
  *
  * x: bf16 [M, K], row stride ldx (elements, ldx·2 a multiple of 16 bytes);
  * w: int8 [N, K] row-major, contiguous (one row per output channel);
- * w_scale: fp32 [N]; bias: bf16 [N] or NULL; residual: bf16 [M, N] with row
- * stride ldr, or NULL (may alias y); y: y_dtype (SFB_BF16 or SFB_F32) [M, N]
+ * w_scale: fp32 [N]; bias: bf16 [N] or NULL; residual: [M, N] in y_dtype with
+ * row stride ldr, or NULL (may alias y); y: y_dtype (SFB_BF16 or SFB_F32) [M, N]
  * with row stride ldy. act: 0 none, 1 GELU (tanh form, as the reference's
  * cuBLASLt GELU epilogue and the RDT-1B MLPs use), 2 SiLU (timestep MLP). K % 64 == 0, N % 32 == 0.
  * num_splits: split-K cluster size for M <= 128: 1, 2, 4 or 8 (0 = automatic).
@@ -186,6 +186,30 @@ int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w
                      const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                      int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
                      int32_t num_splits, void* stream);
+
+/* ── two int8-weight linear layers as one launch (one session) ────────────────
+ * Replaces, for a block's MLP at one session (Mlp::forward, reference
+ * src/models/rdt1b/dit_block.cu:143-163: fc1 → GELU → fc2), the pair of
+ * dequantize + gemm_bias_act calls of each layer (quantization.cu:18-95,
+ * cuda_backend.cu:337-467):
+ *
+ *   h = act( x · (w1 · s1)ᵀ + b1 )          (bf16 [M, F], in the workspace)
+ *   y = h · (w2 · s2)ᵀ + b2 [+ residual]    (y_dtype [M, N]; residual in y_dtype, may alias y)
+ *
+ * run as two stages of the persistent projection kernel, ordered on the device
+ * (no kernel boundary between them). x: bf16 [M, K] (row stride ldx); w1:
+ * int8 [F, K], w2: int8 [N, F], row-major; s1, s2: fp32 per output channel;
+ * b1, b2: bf16 or NULL. act: 0 none, 1 GELU (tanh), 2 SiLU. M <= 80;
+ * K and F multiples of 256 and at most 2048; F and N multiples of 64.
+ * workspace: device memory of at least sfb_w8a16_mlp_workspace_bytes(M, F)
+ * bytes, 256-byte aligned; it holds the stage counters (cleared by every
+ * call) and h. Calls that share a workspace must not overlap on the GPU.
+ * The result equals two sfb_w8a16_linear calls up to fp32 summation order. */
+size_t sfb_w8a16_mlp_workspace_bytes(int32_t M, int32_t F);
+int sfb_w8a16_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const void* b1,
+                  const int8_t* w2, const float* s2, const void* b2, const void* residual, int64_t ldr,
+                  void* y, int64_t ldy, int32_t y_dtype, int32_t M, int32_t K, int32_t F, int32_t N,
+                  int32_t act, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ── RDT-1B denoising runtime ──────────────────────────────────────────────────
  * The model-level path around the kernels above, replacing for RDT-1B the
@@ -240,6 +264,30 @@ int sfb_rdt1b_forward(void* handle, int32_t sessions, const float* x_t, float t,
  * replayed afterwards. */
 int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* actions,
                      int32_t use_graph, void* stream);
+/* One control tick of the inference engine: replaces InferenceEngine::infer
+ * (src/engine/inference_engine.cpp:99-174) with its condition cache keyed by
+ * a caller-supplied frame id (mark_new_frame, :90-93).
+ * - When frame_id differs from the frame the K/V cache was built from (or
+ *   the cache was invalidated, or `sessions` changed), the conditions are
+ *   copied in and encoded (adaptors + every block's cross-attention K/V) on
+ *   the model's encode stream, after the caller's prior work and the previous
+ *   denoise, and an event orders the denoise after it. Otherwise lang_tokens,
+ *   lang_len and img_tokens may be NULL and nothing is re-encoded.
+ * - The robot state is copied every tick (the reference caches it with the
+ *   condition, rdt1b.cpp:207-231; here each tick's actions see its state).
+ * - Then sfb_rdt1b_sample(..., use_graph = 1): noise in, actions out.
+ * Every buffer may be host memory (pinned keeps the copies asynchronous) or
+ * device memory, with the shapes of sfb_rdt1b_encode / sfb_rdt1b_sample. The
+ * first tick creates the encode stream and the device staging buffers of the
+ * conditions (setup-time allocation, like create); later ticks allocate
+ * nothing. Returns once the work is queued on `stream`. */
+int sfb_rdt1b_tick(void* handle, int32_t sessions, uint64_t frame_id, const void* lang_tokens,
+                   const int32_t* lang_len, const void* img_tokens, const void* state, const float* noise,
+                   float* actions, void* stream);
+/* Forces the next tick to re-encode (InferenceEngine::invalidate_condition_cache). */
+int sfb_rdt1b_invalidate_condition(void* handle);
+/* Ticks run and conditions encoded so far on this handle (diagnostic). */
+int sfb_rdt1b_tick_stats(void* handle, int64_t* ticks, int64_t* encodes);
 /* Execution path of a one-session call (sessions == 1): 0 (the default) runs
  * each run of projections between two attentions as one launch of the
  * persistent projection kernel, with the pre-norms folded into it; 1 runs one

@@ -178,7 +178,11 @@ def ref_fa2_lib():
     """The reference's FlashAttention-2 forward, hdim 64 (None if not built)."""
     global _ref_fa2
     if _ref_fa2 is None and os.path.exists(REF_FA2_SO):
-        h = ctypes.CDLL(REF_FA2_SO)
+        try:
+            h = ctypes.CDLL(REF_FA2_SO)
+        except OSError as e:                      # a stale or partial build
+            print(f"oracle: cannot load {REF_FA2_SO}: {e}", file=sys.stderr)
+            return None
         h.sfref_fa2_workspace_bytes.restype = ctypes.c_long
         h.sfref_fa2_workspace_bytes.argtypes = [_i, _i, _i]
         h.sfref_fa2_attention.restype = _i

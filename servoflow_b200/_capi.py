@@ -98,6 +98,13 @@ def _declare(lib: ctypes.CDLL) -> None:
                                      c.c_void_p, c.c_int64, c.c_void_p, c.c_int64, c.c_int32,
                                      c.c_int32, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
                                      c.c_void_p]
+    lib.sfb_w8a16_mlp_workspace_bytes.restype = c.c_size_t
+    lib.sfb_w8a16_mlp_workspace_bytes.argtypes = [c.c_int32, c.c_int32]
+    lib.sfb_w8a16_mlp.restype = c.c_int
+    lib.sfb_w8a16_mlp.argtypes = [c.c_void_p, c.c_int64, c.c_void_p, c.c_void_p, c.c_void_p,
+                                  c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64,
+                                  c.c_void_p, c.c_int64, c.c_int32, c.c_int32, c.c_int32, c.c_int32,
+                                  c.c_int32, c.c_int32, c.c_void_p, c.c_size_t, c.c_void_p]
     lib.sfb_dequantize_int8.restype = c.c_int
     lib.sfb_dequantize_int8.argtypes = [c.c_void_p, c.c_void_p, c.c_int32, c.c_int64, c.c_void_p,
                                         c.c_int32, c.c_int64, c.c_int64, c.c_void_p]

@@ -152,6 +152,23 @@ class B200Backend:
             output.data_ptr(), dtype_code(output.dtype), rows, cols, _stream_handle(stream)),
             "dequantize")
 
+    # Two int8-weight linear layers as one persistent launch (a block's MLP at one session)
+    def w8a16_mlp(self, x, w1, s1, w2, s2, out, b1=None, b2=None, residual=None, act: str = "gelu",
+                  workspace=None, stream=None) -> None:
+        """out[M, N] = act(x·(w1·s1)ᵀ + b1)·(w2·s2)ᵀ + b2 [+ residual] (sfb_w8a16_mlp)."""
+        M, K = x.shape
+        F, N = w1.shape[0], w2.shape[0]
+        need = self._lib.sfb_w8a16_mlp_workspace_bytes(M, F)
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+        acts = {"none": 0, "gelu": 1, "silu": 2}
+        p = lambda t: None if t is None else t.data_ptr()
+        _capi.check(self._lib.sfb_w8a16_mlp(
+            x.data_ptr(), x.stride(0), w1.data_ptr(), s1.data_ptr(), p(b1), w2.data_ptr(), s2.data_ptr(),
+            p(b2), p(residual), residual.stride(0) if residual is not None else 0, out.data_ptr(),
+            out.stride(0), dtype_code(out.dtype), M, K, F, N, acts[act], workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), _stream_handle(stream)), "w8a16_mlp")
+
     # Fused replacement of dequantize + gemm_bias_act (backend.h:160-185, 205-206)
     def w8a16_linear(self, x, w_q, w_scale, out, bias=None, residual=None, act: str = "none",
                      num_splits: int = 0, stream=None) -> None:
@@ -168,9 +185,9 @@ class B200Backend:
             raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "inconsistent shapes")
         if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != N):
             raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "bias must be bf16 [N]")
-        if residual is not None and (residual.dtype != torch.bfloat16 or tuple(residual.shape) != (M, N)
+        if residual is not None and (residual.dtype != out.dtype or tuple(residual.shape) != (M, N)
                                      or residual.stride(1) != 1):
-            raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "residual must be bf16 [M, N] row-major")
+            raise _capi.SfbError(_capi.SFB_ERR_SHAPE, "residual must be [M, N] row-major in out's dtype")
         acts = {"none": 0, "gelu": 1, "silu": 2}
         _capi.check(self._lib.sfb_w8a16_linear(
             x.data_ptr(), x.stride(0), w_q.data_ptr(), w_scale.data_ptr(),

@@ -10,6 +10,11 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
                       const void* bias, const void* residual, int64_t ldr, void* y, int64_t ldy,
                       int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
                       int32_t num_splits, cudaStream_t stream, bool pdl);
+size_t w8a16_mlp_workspace_bytes(int M, int F);
+int w8a16_mlp_launch(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const void* b1,
+                     const int8_t* w2, const float* s2, const void* b2, const void* residual, int64_t ldr,
+                     void* y, int64_t ldy, int32_t y_dtype, int32_t M, int32_t K, int32_t F, int32_t N,
+                     int32_t act, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 int dequantize_int8_launch(const int8_t* in, const void* scale, int32_t scale_dtype,
                            int64_t scale_numel, void* out, int32_t out_dtype, int64_t rows,
                            int64_t cols, cudaStream_t stream);
@@ -139,6 +144,16 @@ int sfb_w8a16_linear(const void* x, int64_t ldx, const int8_t* w, const float* w
                      int32_t num_splits, void* stream) {
     return sfb::w8a16_gemm_launch(x, ldx, w, w_scale, bias, residual, ldr, y, ldy, y_dtype, M, N, K,
                                   act, num_splits, static_cast<cudaStream_t>(stream), false);
+}
+
+size_t sfb_w8a16_mlp_workspace_bytes(int32_t M, int32_t F) { return sfb::w8a16_mlp_workspace_bytes(M, F); }
+
+int sfb_w8a16_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const void* b1,
+                  const int8_t* w2, const float* s2, const void* b2, const void* residual, int64_t ldr,
+                  void* y, int64_t ldy, int32_t y_dtype, int32_t M, int32_t K, int32_t F, int32_t N,
+                  int32_t act, void* workspace, size_t workspace_bytes, void* stream) {
+    return sfb::w8a16_mlp_launch(x, ldx, w1, s1, b1, w2, s2, b2, residual, ldr, y, ldy, y_dtype, M, K, F, N,
+                                 act, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -42,7 +42,7 @@ int w8a16_gemm_launch(const void* x, int64_t ldx, const int8_t* w, const float* 
                       int32_t y_dtype, int32_t M, int32_t N, int32_t K, int32_t act,
                       int32_t num_splits, cudaStream_t stream, bool pdl);
 int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_t ldo, int rows,
-                    int D, float eps, cudaStream_t s);
+                    int D, float eps, cudaStream_t s, bool x_f32 = false);
 int head_rms_norm_launch(void* x, int64_t ld, int rows, int heads, const void* w, float eps,
                          cudaStream_t s);
 int bf16_to_f16_launch(void* x, int64_t ld, int rows, int cols, cudaStream_t s);
@@ -121,7 +121,8 @@ struct Model {
     int32_t* lang_len;
     std::vector<__nv_bfloat16*> kv;
     // step workspaces
-    __nv_bfloat16 *x, *xn, *qkv, *attn, *h, *ain, *ah1, *ah2, *seq, *tsc, *fsc, *th, *temb, *fh, *femb;
+    float* x;                                 // residual stream [B·S, D], fp32
+    __nv_bfloat16 *xn, *qkv, *attn, *h, *ain, *ah1, *ah2, *seq, *tsc, *fsc, *th, *temb, *fh, *femb;
     // timestep embeddings of every sampling step, computed once per tick
     __nv_bfloat16 *tsc_all, *th_all, *temb_all;
     float *yfin, *xact, *x0prev;
@@ -150,6 +151,16 @@ struct Model {
     std::vector<DenseLaunch> dl;
     __nv_bfloat16* xg = nullptr;              // bf16(x · g) of the next pre-norm, [S, D]
     float* ss = nullptr;                      // partial Σ x² per token row, [D / 16][80]
+
+    // Control-tick engine (sfb_rdt1b_tick): the frame whose conditions fill
+    // the K/V cache, and the encode stream ordered before the denoise.
+    bool cond_valid = false;
+    uint64_t cond_frame = 0;
+    int cond_sessions = 0;
+    cudaStream_t enc = nullptr;
+    cudaEvent_t ev_enc = nullptr, ev_prev = nullptr;
+    void *st_lang = nullptr, *st_img = nullptr, *st_len = nullptr, *st_state = nullptr;   // device staging
+    int64_t ticks = 0, encodes = 0;
 
     int S() const { return c.horizon + 3; }
 };
@@ -181,7 +192,7 @@ static int new_linear(Model& m, Linear& L, int N, int K, const std::string& name
 }
 
 static int linear(const Linear& L, const __nv_bfloat16* x, int64_t ldx, int M, void* y, int64_t ldy,
-                  int act, const __nv_bfloat16* residual, int64_t ldr, cudaStream_t s, bool y_f32 = false) {
+                  int act, const void* residual, int64_t ldr, cudaStream_t s, bool y_f32 = false) {
     return w8a16_gemm_launch(x, ldx, L.w, L.s, L.b, residual, ldr, y, ldy, y_f32 ? SFB_F32 : SFB_BF16, M,
                              L.N, L.K, act, 0, s, true);
 }
@@ -239,7 +250,7 @@ static int build_dense(Model& m) {
     if (dense_clusters(device_info()) <= 0) return SFB_OK;
     std::vector<DenseStage> st;
     auto stage = [&](const Linear& Lw, const __nv_bfloat16* x, int TM, int act, void* y, int64_t ldy, bool y_f32,
-                     const __nv_bfloat16* res, const float* ss_in, int n_ss_in, const __nv_bfloat16* g_next) {
+                     const void* res, const float* ss_in, int n_ss_in, const __nv_bfloat16* g_next) {
         DenseStage d;
         std::memset(&d, 0, sizeof(d));
         SFB_TRY(dense_stage_init(d, x, D, S, Lw.w, Lw.N, Lw.K, TM));
@@ -264,13 +275,13 @@ static int build_dense(Model& m) {
     for (int l = 0; l < L; ++l) {
         const Block& bl = m.blocks[l];
         f = static_cast<int>(st.size());
-        SFB_TRY(stage(bl.proj, m.attn, 64, 0, m.x, D, false, m.x, nullptr, 0, bl.norm2));
+        SFB_TRY(stage(bl.proj, m.attn, 64, 0, m.x, D, true, m.x, nullptr, 0, bl.norm2));
         SFB_TRY(stage(bl.cq, m.xg, 64, 0, m.h, D, false, nullptr, m.ss, nss, nullptr));
         launch(f);
         f = static_cast<int>(st.size());
-        SFB_TRY(stage(bl.cproj, m.attn, 64, 0, m.x, D, false, m.x, nullptr, 0, bl.norm3));
+        SFB_TRY(stage(bl.cproj, m.attn, 64, 0, m.x, D, true, m.x, nullptr, 0, bl.norm3));
         SFB_TRY(stage(bl.fc1, m.xg, 64, 1, m.h, D, false, nullptr, m.ss, nss, nullptr));
-        SFB_TRY(stage(bl.fc2, m.h, 64, 0, m.x, D, false, m.x, nullptr, 0,
+        SFB_TRY(stage(bl.fc2, m.h, 64, 0, m.x, D, true, m.x, nullptr, 0,
                       l + 1 < L ? m.blocks[l + 1].norm1 : m.norm_final));
         if (l + 1 < L) {
             SFB_TRY(stage(m.blocks[l + 1].qkv, m.xg, 128, 0, m.qkv, 3 * D, false, nullptr, m.ss, nss, nullptr));
@@ -349,7 +360,7 @@ static int create(Model& m) {
         const int Lk = (l % 2 == 0) ? c.max_lang_len : c.img_len;
         SFB_TRY(bf(&m.kv[l], static_cast<int64_t>(B) * Lk * 2 * D));
     }
-    SFB_TRY(bf(&m.x, BS * D)); SFB_TRY(bf(&m.xn, BS * D)); SFB_TRY(bf(&m.qkv, BS * 3 * D));
+    SFB_TRY(f32(&m.x, BS * D)); SFB_TRY(bf(&m.xn, BS * D)); SFB_TRY(bf(&m.qkv, BS * 3 * D));
     SFB_TRY(bf(&m.attn, BS * D)); SFB_TRY(bf(&m.h, BS * D));
     SFB_TRY(bf(&m.ain, BT1 * 2 * c.state_dim)); SFB_TRY(bf(&m.ah1, BT1 * D)); SFB_TRY(bf(&m.ah2, BT1 * D));
     SFB_TRY(bf(&m.seq, BT1 * D));
@@ -512,28 +523,28 @@ static int forward(Model& m, int B, float t, cudaStream_t s, int step = -1) {
     for (int l = 0; l < c.num_layers; ++l) {
         const Block& bl = m.blocks[l];
         // x = x + proj(attn(qk-norm(qkv(norm1(x)))))
-        SFB_TRY(rms_norm_launch(m.x, D, bl.norm1, m.xn, D, M, D, eps, s));
+        SFB_TRY(rms_norm_launch(m.x, D, bl.norm1, m.xn, D, M, D, eps, s, true));
         SFB_TRY(linear(bl.qkv, m.xn, D, M, m.qkv, 3 * D, 0, nullptr, 0, s));
         SFB_TRY(attention(m, m.qkv, static_cast<int64_t>(S) * 3 * D, 3 * D, m.qkv + D, m.qkv + 2 * D,
                           static_cast<int64_t>(S) * 3 * D, 3 * D, m.attn, B, S, S, nullptr, false,
                           bl.qn, bl.kn, s));
-        SFB_TRY(linear(bl.proj, m.attn, D, M, m.x, D, 0, m.x, D, s));
+        SFB_TRY(linear(bl.proj, m.attn, D, M, m.x, D, 0, m.x, D, s, true));
         // x = x + proj(cross_attn(qnorm(q(norm2(x))), K/V cache))
         const bool lang_blk = (l % 2 == 0);
         const int Lk = lang_blk ? c.max_lang_len : c.img_len;
-        SFB_TRY(rms_norm_launch(m.x, D, bl.norm2, m.xn, D, M, D, eps, s));
+        SFB_TRY(rms_norm_launch(m.x, D, bl.norm2, m.xn, D, M, D, eps, s, true));
         SFB_TRY(linear(bl.cq, m.xn, D, M, m.h, D, 0, nullptr, 0, s));
         SFB_TRY(attention(m, m.h, static_cast<int64_t>(S) * D, D, m.kv[l], m.kv[l] + D,
                           static_cast<int64_t>(Lk) * 2 * D, 2 * D, m.attn, B, S, Lk,
                           lang_blk ? m.lang_len : nullptr, true, bl.cqn, nullptr, s));
-        SFB_TRY(linear(bl.cproj, m.attn, D, M, m.x, D, 0, m.x, D, s));
+        SFB_TRY(linear(bl.cproj, m.attn, D, M, m.x, D, 0, m.x, D, s, true));
         // x = x + fc2(gelu(fc1(norm3(x))))
-        SFB_TRY(rms_norm_launch(m.x, D, bl.norm3, m.xn, D, M, D, eps, s));
+        SFB_TRY(rms_norm_launch(m.x, D, bl.norm3, m.xn, D, M, D, eps, s, true));
         SFB_TRY(linear(bl.fc1, m.xn, D, M, m.h, D, 1, nullptr, 0, s));
-        SFB_TRY(linear(bl.fc2, m.h, D, M, m.x, D, 0, m.x, D, s));
+        SFB_TRY(linear(bl.fc2, m.h, D, M, m.x, D, 0, m.x, D, s, true));
     }
     // final layer: norm → fc1 (GELU) → fc2, fp32 output [B·S, A]
-    SFB_TRY(rms_norm_launch(m.x, D, m.norm_final, m.xn, D, M, D, eps, s));
+    SFB_TRY(rms_norm_launch(m.x, D, m.norm_final, m.xn, D, M, D, eps, s, true));
     SFB_TRY(linear(m.fin1, m.xn, D, M, m.h, D, 1, nullptr, 0, s));
     SFB_TRY(linear(m.fin2, m.h, D, M, m.yfin, A, 0, nullptr, 0, s, true));
     return SFB_OK;
@@ -605,6 +616,9 @@ int sfb_rdt1b_destroy(void* handle) {
     cudaDeviceSynchronize();
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
+    if (m->ev_enc) cudaEventDestroy(m->ev_enc);
+    if (m->ev_prev) cudaEventDestroy(m->ev_prev);
+    if (m->enc) cudaStreamDestroy(m->enc);
     if (m->ev_out) cudaEventDestroy(m->ev_out);
     if (m->own) cudaStreamDestroy(m->own);
     for (void* ptr : m->allocs) cudaFree(ptr);
@@ -704,6 +718,82 @@ int sfb_rdt1b_sample(void* handle, int32_t sessions, const float* noise, float* 
         record_cuda_error(cudaGetLastError(), "rdt1b sample output");
         return SFB_ERR_CUDA;
     }
+    return SFB_OK;
+}
+
+int sfb_rdt1b_tick(void* handle, int32_t sessions, uint64_t frame_id, const void* lang_tokens,
+                   const int32_t* lang_len, const void* img_tokens, const void* state, const float* noise,
+                   float* actions, void* stream) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || state == nullptr || noise == nullptr || actions == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
+    if (sessions < 1 || sessions > m->c.max_sessions) return SFB_ERR_SHAPE;
+    const auto& c = m->c;
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    const size_t lang_b = static_cast<size_t>(sessions) * c.max_lang_len * c.lang_dim * 2;
+    const size_t img_b = static_cast<size_t>(sessions) * c.img_len * c.img_dim * 2;
+    const size_t len_b = static_cast<size_t>(sessions) * 4, state_b = static_cast<size_t>(sessions) * c.state_dim * 2;
+    auto fail_cuda = [&](const char* what) { record_cuda_error(cudaGetLastError(), what); return SFB_ERR_CUDA; };
+    const bool need_encode = !m->cond_valid || m->cond_frame != frame_id || m->cond_sessions != sessions;
+    if (need_encode && (lang_tokens == nullptr || lang_len == nullptr || img_tokens == nullptr))
+        return SFB_ERR_INVALID;
+    if (m->enc == nullptr) {
+        // first tick: the encode stream, its events and the staging buffers (setup)
+        if (cudaStreamCreateWithFlags(&m->enc, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&m->ev_enc, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&m->ev_prev, cudaEventDisableTiming) != cudaSuccess)
+            return fail_cuda("tick streams");
+        const size_t B = static_cast<size_t>(c.max_sessions);
+        SFB_TRY(rdt::dalloc(*m, &m->st_lang, B * c.max_lang_len * c.lang_dim * 2));
+        SFB_TRY(rdt::dalloc(*m, &m->st_img, B * c.img_len * c.img_dim * 2));
+        SFB_TRY(rdt::dalloc(*m, &m->st_len, B * 4));
+        SFB_TRY(rdt::dalloc(*m, &m->st_state, B * c.state_dim * 2));
+    }
+    ++m->ticks;
+    if (need_encode) {
+        // The encode stream starts after the caller's prior work (its inputs)
+        // and after the previous denoise (which reads the K/V cache it rewrites).
+        if (cudaEventRecord(m->ev_prev, caller) != cudaSuccess || cudaStreamWaitEvent(m->enc, m->ev_prev, 0) != cudaSuccess ||
+            cudaEventRecord(m->ev_prev, m->own) != cudaSuccess || cudaStreamWaitEvent(m->enc, m->ev_prev, 0) != cudaSuccess)
+            return fail_cuda("tick ordering");
+        // host or device buffers: copied into the staging buffers (cudaMemcpyDefault)
+        if (cudaMemcpyAsync(m->st_lang, lang_tokens, lang_b, cudaMemcpyDefault, m->enc) != cudaSuccess ||
+            cudaMemcpyAsync(m->st_img, img_tokens, img_b, cudaMemcpyDefault, m->enc) != cudaSuccess ||
+            cudaMemcpyAsync(m->st_len, lang_len, len_b, cudaMemcpyDefault, m->enc) != cudaSuccess ||
+            cudaMemcpyAsync(m->st_state, state, state_b, cudaMemcpyDefault, m->enc) != cudaSuccess)
+            return fail_cuda("tick condition copy");
+        SFB_TRY(rdt::encode(*m, sessions, m->st_lang, static_cast<const int32_t*>(m->st_len), m->st_img,
+                            m->st_state, m->enc));
+        if (cudaEventRecord(m->ev_enc, m->enc) != cudaSuccess || cudaStreamWaitEvent(caller, m->ev_enc, 0) != cudaSuccess)
+            return fail_cuda("tick encode event");
+        m->cond_valid = true;
+        m->cond_frame = frame_id;
+        m->cond_sessions = sessions;
+        ++m->encodes;
+    } else {
+        // same frame: the cached K/V stay; only the robot state is new
+        // (the caller's stream already waits for the previous denoise, which reads it)
+        if (cudaMemcpyAsync(m->state, state, state_b, cudaMemcpyDefault, caller) != cudaSuccess)
+            return fail_cuda("tick state copy");
+    }
+    // the denoise (graph) on the model's stream, ordered after the caller's stream
+    return sfb_rdt1b_sample(handle, sessions, noise, actions, 1, stream);
+}
+
+int sfb_rdt1b_invalidate_condition(void* handle) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
+    m->cond_valid = false;
+    return SFB_OK;
+}
+
+int sfb_rdt1b_tick_stats(void* handle, int64_t* ticks, int64_t* encodes) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
+    if (ticks) *ticks = m->ticks;
+    if (encodes) *encodes = m->encodes;
     return SFB_OK;
 }
 

@@ -57,11 +57,11 @@ struct alignas(64) DenseStage {
     CUtensorMap tmX;                 // bf16 [M, K] (row stride ldx), box {64, 80}, SWIZZLE_128B
     const float* w_scale;            // [N]
     const __nv_bfloat16* bias;       // [N] or null
-    const __nv_bfloat16* residual;   // [M, N] (ldr) or null; may alias y
+    const void* residual;            // [M, N] (ldr) in y's dtype, or null; may alias y
     void* y;                         // [M, N] (ldy), bf16 or fp32
-    const __nv_bfloat16* g_next;     // [N] or null: also write xg = bf16(bf16(y) · g_next)
+    const __nv_bfloat16* g_next;     // [N] or null: also write xg = bf16(y · g_next) (y as stored)
     __nv_bfloat16* xg;               // [M, N] (ldg)
-    float* ss_out;                   // or null: [tiles · 4][80] partial Σ bf16(y)² per token row
+    float* ss_out;                   // or null: [tiles · 4][80] partial Σ y² per token row (y as stored)
     const float* ss_in;              // or null: [n_ss_in][80] partials of X's rows; scales rows by r[m]
     int64_t ldr, ldy, ldg;
     int32_t n_ss_in;
@@ -164,8 +164,10 @@ __device__ __forceinline__ int units_of(const DenseStage& S, int cl, int ncl) {
     return cl < S.tiles ? (S.tiles - cl + ncl - 1) / ncl : 0;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long long* __restrict__ ctr, int M) {
+// The kernel body: `stages` in global memory (a model's stage table) or in
+// the parameter space of a launch (dense_pair_kernel).
+__device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages, int nst,
+                                          unsigned long long* __restrict__ ctr, int M) {
     using namespace ptx;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -449,8 +451,12 @@ rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long l
 #pragma unroll
                             for (int k = 0; k < 8; ++k) bb[k] = 0.f;
                         }
-                        if (S.residual != nullptr) {
-                            const uint4 ru = *reinterpret_cast<const uint4*>(S.residual + m * S.ldr + n);
+                        if (S.residual != nullptr && S.y_f32) {
+                            const float* rp = static_cast<const float*>(S.residual) + m * S.ldr + n;
+                            const float4 a = *reinterpret_cast<const float4*>(rp), b = *reinterpret_cast<const float4*>(rp + 4);
+                            rr[0] = a.x; rr[1] = a.y; rr[2] = a.z; rr[3] = a.w; rr[4] = b.x; rr[5] = b.y; rr[6] = b.z; rr[7] = b.w;
+                        } else if (S.residual != nullptr) {
+                            const uint4 ru = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(S.residual) + m * S.ldr + n);
                             const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
 #pragma unroll
                             for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(r2[k]); rr[2 * k] = f.x; rr[2 * k + 1] = f.y; }
@@ -469,6 +475,18 @@ rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long l
                             float* dst = static_cast<float*>(S.y) + m * S.ldy + n;
                             *reinterpret_cast<float4*>(dst) = make_float4(outv[0], outv[1], outv[2], outv[3]);
                             *reinterpret_cast<float4*>(dst + 4) = make_float4(outv[4], outv[5], outv[6], outv[7]);
+                            if (S.g_next != nullptr) {
+                                const uint4 gu = *reinterpret_cast<const uint4*>(S.g_next + n);
+                                const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
+                                uint4 q;
+                                __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&q);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const float2 g = __bfloat1622float2(g2[k]);
+                                    q2[k] = __floats2bfloat162_rn(outv[2 * k] * g.x, outv[2 * k + 1] * g.y);
+                                }
+                                *reinterpret_cast<uint4*>(S.xg + m * S.ldg + n) = q;
+                            }
                         } else {
                             uint4 o;
                             __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -529,6 +547,19 @@ rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long l
     }
 }
 
+__global__ void __launch_bounds__(kThreads, 1)
+rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long long* __restrict__ ctr, int M) {
+    dense_run(stages, nst, ctr, M);
+}
+
+// Two stages passed by value (tensor maps in the parameter space): a launch
+// that needs no stage table in device memory.
+struct DenseStagePair { DenseStage s[2]; };
+__global__ void __launch_bounds__(kThreads, 1)
+dense_pair_kernel(const __grid_constant__ DenseStagePair p, unsigned long long* __restrict__ ctr, int M) {
+    dense_run(p.s, 2, ctr, M);
+}
+
 }  // namespace dense
 
 // Clusters of the dense kernel resident at once (one CTA per SM), cached.
@@ -537,7 +568,9 @@ int dense_clusters(const DeviceInfo& dev) {
     std::atomic<int>& slot = cache[dev.ordinal & 63];
     if (const int n = slot.load(std::memory_order_relaxed); n != 0) return n;
     auto kern = dense::rdt_dense_kernel;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dense::kSmemBytes) != cudaSuccess) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dense::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(dense::dense_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dense::kSmemBytes) != cudaSuccess) {
         (void)cudaGetLastError();
         return -1;
     }
@@ -588,28 +621,93 @@ int dense_stage_init(DenseStage& S, const void* x, int64_t ldx, int M, const int
     return SFB_OK;
 }
 
-// One launch over stages[0, nst) (device memory); ctr: nst + 1 counters of
-// this launch slot (zero at allocation, never reset).
-int dense_launch(const DenseStage* stages, int nst, unsigned long long* ctr, int M, cudaStream_t stream, bool pdl) {
-    const DeviceInfo& dev = device_info();
-    const int ncl = dense_clusters(dev);
-    if (ncl <= 0) { record_cuda_error(cudaErrorInvalidConfiguration, "dense kernel clusters"); return SFB_ERR_LAUNCH; }
+// Launch configuration shared by both kernels (cluster of kSplit CTAs, one
+// CTA per SM, as many clusters as are resident at once).
+static cudaLaunchConfig_t dense_config(int ncl, cudaStream_t stream, cudaLaunchAttribute* attr, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ncl * dense::kSplit, 1, 1);
     cfg.blockDim = dim3(dense::kThreads, 1, 1);
     cfg.dynamicSmemBytes = dense::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = dense::kSplit;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1 + pdl_attr(&attr[1], pdl);
+    return cfg;
+}
+
+// One launch over stages[0, nst) (device memory); ctr: nst + 1 counters of
+// this launch slot (zero at allocation, never reset).
+int dense_launch(const DenseStage* stages, int nst, unsigned long long* ctr, int M, cudaStream_t stream, bool pdl) {
+    const DeviceInfo& dev = device_info();
+    const int ncl = dense_clusters(dev);
+    if (ncl <= 0) { record_cuda_error(cudaErrorInvalidConfiguration, "dense kernel clusters"); return SFB_ERR_LAUNCH; }
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = dense_config(ncl, stream, attr, pdl);
     cudaError_t e = cudaLaunchKernelEx(&cfg, dense::rdt_dense_kernel, stages, nst, ctr, M);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
         record_cuda_error(e, "dense kernel launch");
+        return SFB_ERR_LAUNCH;
+    }
+    return SFB_OK;
+}
+
+// Counters of a two-stage launch: start + one per stage, padded to 256 B.
+constexpr size_t kMlpCtrBytes = 256;
+
+size_t w8a16_mlp_workspace_bytes(int M, int F) {
+    const size_t h = static_cast<size_t>(std::max(M, 0)) * std::max(F, 0) * 2;
+    return kMlpCtrBytes + ((h + 255) / 256) * 256;
+}
+
+// y = fc2(act(fc1(x))) [+ residual] as one launch of the persistent kernel:
+// stage 0 writes h = act(x·W1ᵀ·s1 + b1) (bf16, [M, F]) into the workspace,
+// stage 1 reads it. The workspace holds the counters (cleared on every call)
+// and h.
+int w8a16_mlp_launch(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const void* b1,
+                     const int8_t* w2, const float* s2, const void* b2, const void* residual, int64_t ldr,
+                     void* y, int64_t ldy, int32_t y_dtype, int32_t M, int32_t K, int32_t F, int32_t N,
+                     int32_t act, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (x == nullptr || w1 == nullptr || s1 == nullptr || w2 == nullptr || s2 == nullptr || y == nullptr ||
+        workspace == nullptr)
+        return SFB_ERR_INVALID;
+    if (M < 1 || M > dense::kBN || K < 1 || F < 1 || N < 1) return SFB_ERR_SHAPE;
+    if (N % 64 != 0 || F % 64 != 0) return SFB_ERR_SHAPE;
+    if (y_dtype != SFB_BF16 && y_dtype != SFB_F32) return SFB_ERR_DTYPE;
+    if (act < 0 || act > 2) return SFB_ERR_INVALID;
+    if (ldy < N || (residual != nullptr && ldr < N) || ldx < K) return SFB_ERR_SHAPE;
+    auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || (ldx * 2) % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return SFB_ERR_ALIGN;
+    if (workspace_bytes < w8a16_mlp_workspace_bytes(M, F)) return SFB_ERR_WORKSPACE;
+    const DeviceInfo& dev = device_info();
+    if (!is_sm100(dev)) return SFB_ERR_UNSUPPORTED;
+    const int ncl = dense_clusters(dev);
+    if (ncl <= 0) { record_cuda_error(cudaErrorInvalidConfiguration, "dense kernel clusters"); return SFB_ERR_LAUNCH; }
+    unsigned long long* ctr = static_cast<unsigned long long*>(workspace);
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + kMlpCtrBytes);
+    dense::DenseStagePair p;
+    std::memset(&p, 0, sizeof(p));
+    DenseStage& a = p.s[0];
+    DenseStage& b = p.s[1];
+    SFB_TRY(dense_stage_init(a, x, ldx, M, w1, F, K, 64));
+    a.w_scale = s1; a.bias = static_cast<const __nv_bfloat16*>(b1); a.y = h; a.ldy = F; a.act = act; a.eps = 1e-6f;
+    SFB_TRY(dense_stage_init(b, h, F, M, w2, N, F, 64));
+    b.w_scale = s2; b.bias = static_cast<const __nv_bfloat16*>(b2); b.residual = residual; b.ldr = ldr;
+    b.y = y; b.ldy = ldy; b.y_f32 = y_dtype == SFB_F32 ? 1 : 0; b.eps = 1e-6f;
+    // every call starts its counters from zero (one generation per call)
+    cudaError_t e = cudaMemsetAsync(ctr, 0, kMlpCtrBytes, stream);
+    if (e != cudaSuccess) { record_cuda_error(e, "mlp counters"); return SFB_ERR_CUDA; }
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = dense_config(ncl, stream, attr, false);
+    e = cudaLaunchKernelEx(&cfg, dense::dense_pair_kernel, p, ctr, M);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        record_cuda_error(e, "mlp launch");
         return SFB_ERR_LAUNCH;
     }
     return SFB_OK;

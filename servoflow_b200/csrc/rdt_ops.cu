@@ -12,7 +12,7 @@
 //   sincos_embed    [cos(t·f_i), sin(t·f_i)], f_i = 10000^(−i/half)
 //                   (dit_block.cu:58-72).
 //   assemble_x      x = [t_emb, freq_emb, state_traj, action_traj] + x_pos_embed
-//                   per session (rdt1b.cpp:305-340).
+//                   per session (rdt1b.cpp:305-340), into the fp32 residual stream.
 //   adaptor_input   cat([state | x_t], ones) per session, the state-adaptor input
 //                   (test_rdt1b_alignment.py:204-209).
 //   add_rows        cond += pos (condition position embeddings).
@@ -73,8 +73,20 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
 // is read before the dependency wait and the row is kept in registers, so the
 // kernel's critical path is one load of x, the reduction and the store. Same
 // operation order as rms_norm_kernel (identical results).
-template <int kC>
-__global__ void rms_norm_reg_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+// Eight consecutive values of a bf16 or fp32 row as fp32.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(h[k]); v[2 * k] = f.x; v[2 * k + 1] = f.y; }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <int kC, typename TX>
+__global__ void rms_norm_reg_kernel(const TX* __restrict__ x, int64_t ldx,
                                     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                     int64_t ldo, int rows, float eps) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -84,19 +96,15 @@ __global__ void rms_norm_reg_kernel(const __nv_bfloat16* __restrict__ x, int64_t
     pdl_trigger();
     pdl_wait();
     if (warp >= rows) return;
-    const __nv_bfloat16* xr = x + warp * ldx;
-    uint4 u[kC];
+    const TX* xr = x + warp * ldx;
+    float u[kC][8];
 #pragma unroll
-    for (int i = 0; i < kC; ++i) u[i] = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
+    for (int i = 0; i < kC; ++i) load8(xr + (i * 32 + lane) * 8, u[i]);
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < kC; ++i) {
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 f = __bfloat1622float2(h[k]);
-            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-        }
+        for (int k = 0; k < 4; ++k) ss = fmaf(u[i][2 * k], u[i][2 * k], fmaf(u[i][2 * k + 1], u[i][2 * k + 1], ss));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -104,14 +112,13 @@ __global__ void rms_norm_reg_kernel(const __nv_bfloat16* __restrict__ x, int64_t
     __nv_bfloat16* orow = out + warp * ldo;
 #pragma unroll
     for (int i = 0; i < kC; ++i) {
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
         const __nv_bfloat162* gw = reinterpret_cast<const __nv_bfloat162*>(&g[i]);
         uint4 r;
         __nv_bfloat162* ro = reinterpret_cast<__nv_bfloat162*>(&r);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const float2 f = __bfloat1622float2(h[k]), gg = __bfloat1622float2(gw[k]);
-            ro[k] = __floats2bfloat162_rn(f.x * inv * gg.x, f.y * inv * gg.y);
+            const float2 gg = __bfloat1622float2(gw[k]);
+            ro[k] = __floats2bfloat162_rn(u[i][2 * k] * inv * gg.x, u[i][2 * k + 1] * inv * gg.y);
         }
         *reinterpret_cast<uint4*>(orow + (i * 32 + lane) * 8) = r;
     }
@@ -169,7 +176,7 @@ __global__ void assemble_x_kernel(const __nv_bfloat16* __restrict__ t_emb,
                                   const __nv_bfloat16* __restrict__ f_emb,
                                   const __nv_bfloat16* __restrict__ seq,   // [B·(S−2), D]
                                   const __nv_bfloat16* __restrict__ pos,   // [S, D]
-                                  __nv_bfloat16* __restrict__ x, int B, int S, int D) {
+                                  float* __restrict__ x, int B, int S, int D) {   // fp32 residual stream
     pdl_trigger();
     pdl_wait();
     const int64_t n8 = static_cast<int64_t>(B) * S * D / 8;
@@ -186,14 +193,14 @@ __global__ void assemble_x_kernel(const __nv_bfloat16* __restrict__ t_emb,
         const uint4 p = *reinterpret_cast<const uint4*>(pos + static_cast<int64_t>(s) * D + col);
         const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
         const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&p);
-        uint4 o;
-        __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+        float o[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const float2 fa = __bfloat1622float2(ha[k]), fp = __bfloat1622float2(hp[k]);
-            ho[k] = __floats2bfloat162_rn(fa.x + fp.x, fa.y + fp.y);
+            o[2 * k] = fa.x + fp.x; o[2 * k + 1] = fa.y + fp.y;
         }
-        *reinterpret_cast<uint4*>(x + e) = o;
+        *reinterpret_cast<float4*>(x + e) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4*>(x + e + 4) = make_float4(o[4], o[5], o[6], o[7]);
     }
 }
 
@@ -292,27 +299,27 @@ __global__ void bf16_to_f16_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, in
 // The inputs of a norm folded into the next projection (the persistent
 // projection kernel): per row m, ss[m] = Σ_k x[m,k]² (fp32 of the bf16
 // values) and xg[m, :] = bf16(x[m, :] · g). Warp per row; D % 256 == 0.
-__global__ void norm_prep_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+__global__ void norm_prep_kernel(const float* __restrict__ x, int64_t ldx,
                                  const __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ xg,
                                  int64_t ldg, float* __restrict__ ss, int rows, int D) {
     pdl_trigger();
     pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
-    const __nv_bfloat16* xr = x + warp * ldx;
+    const float* xr = x + warp * ldx;
     float a = 0.f;
     for (int c = lane * 8; c < D; c += 256) {
-        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+        float f[8];
+        load8(xr + c, f);
         const uint4 gu = *reinterpret_cast<const uint4*>(g + c);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
         const __nv_bfloat162* gg = reinterpret_cast<const __nv_bfloat162*>(&gu);
         uint4 o;
         __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const float2 f = __bfloat1622float2(h[i]), w = __bfloat1622float2(gg[i]);
-            a = fmaf(f.x, f.x, fmaf(f.y, f.y, a));
-            ho[i] = __floats2bfloat162_rn(f.x * w.x, f.y * w.y);
+            const float2 w = __bfloat1622float2(gg[i]);
+            a = fmaf(f[2 * i], f[2 * i], fmaf(f[2 * i + 1], f[2 * i + 1], a));
+            ho[i] = __floats2bfloat162_rn(f[2 * i] * w.x, f[2 * i + 1] * w.y);
         }
         *reinterpret_cast<uint4*>(xg + warp * ldg + c) = o;
     }
@@ -352,14 +359,21 @@ inline unsigned grid_for(int64_t n, int threads) {
 }  // namespace rdt
 
 int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_t ldo, int rows,
-                    int D, float eps, cudaStream_t s) {
+                    int D, float eps, cudaStream_t s, bool x_f32) {
     if (D % 256 != 0 || (ldx % 8) || (ldo % 8)) return SFB_ERR_SHAPE;
     if (rows <= 0) return SFB_OK;
     const int warps_per_block = 4;
     const unsigned grid = (rows + warps_per_block - 1) / warps_per_block;
+    if (x_f32) {
+        if (D != 2048) return SFB_ERR_SHAPE;
+        prefer_max_shared(rdt::rms_norm_reg_kernel<8, float>);
+        return launch_kernel(rdt::rms_norm_reg_kernel<8, float>, grid, 32 * warps_per_block, 0, s, true,
+                             static_cast<const float*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+                             static_cast<__nv_bfloat16*>(out), ldo, rows, eps);
+    }
     if (D == 2048) {
-        prefer_max_shared(rdt::rms_norm_reg_kernel<8>);
-        return launch_kernel(rdt::rms_norm_reg_kernel<8>, grid, 32 * warps_per_block, 0, s, true,
+        prefer_max_shared(rdt::rms_norm_reg_kernel<8, __nv_bfloat16>);
+        return launch_kernel(rdt::rms_norm_reg_kernel<8, __nv_bfloat16>, grid, 32 * warps_per_block, 0, s, true,
                              static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
                              static_cast<__nv_bfloat16*>(out), ldo, rows, eps);
     }

@@ -6,7 +6,7 @@
 // X: bf16 activations [M, K] (row stride ldx); Wq: int8 weights [N, K]
 // (row-major, one row per output channel, contiguous); s: fp32 per-output-
 // channel scales; bias: optional bf16 [N]; act: none, GELU (tanh form) or SiLU;
-// R: optional bf16 residual [M, N] (may alias Y); Y: bf16 or fp32 [M, N].
+// R: optional residual [M, N] in Y's dtype (may alias Y); Y: bf16 or fp32 [M, N].
 //
 // It replaces the reference's two-step path — dequantise the whole weight
 // (src/backend/cuda/ops/quantization.cu:18-95), then cuBLASLt GEMM + bias/GELU
@@ -45,7 +45,7 @@ namespace sfb {
 struct W8Params {
     const float*   w_scale;
     const void*    bias;          // bf16 [N] or nullptr
-    const void*    residual;      // bf16 [M, N] (row stride ldr) or nullptr
+    const void*    residual;      // [M, N] (row stride ldr) in y's dtype, or nullptr
     void*          y;             // bf16 or fp32
     int64_t        ldy, ldr;
     int32_t        M, N, K;
@@ -107,6 +107,27 @@ constexpr uint64_t kDrainNs = 100000000ull;        // bound of each wait for in-
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;   // sqrt(2/pi), GELU tanh form
     return 0.5f * x * (1.f + tanhf(k0 * fmaf(k1 * x * x, x, x)));
+}
+
+// Eight residual values R[m, n..n+7] in fp32 (R has Y's dtype); zeros when !use.
+__device__ __forceinline__ void load_res8(const W8Params& p, int m, int n, bool use, float (&r)[8]) {
+    if (!use) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r[k] = 0.f;
+        return;
+    }
+    if (p.y_f32) {
+        const float* src = static_cast<const float*>(p.residual) + static_cast<int64_t>(m) * p.ldr + n;
+        const float4 a = *reinterpret_cast<const float4*>(src);
+        const float4 b = *reinterpret_cast<const float4*>(src + 4);
+        r[0] = a.x; r[1] = a.y; r[2] = a.z; r[3] = a.w; r[4] = b.x; r[5] = b.y; r[6] = b.z; r[7] = b.w;
+    } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(
+            static_cast<const __nv_bfloat16*>(p.residual) + static_cast<int64_t>(m) * p.ldr + n);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(h[k]); r[2 * k] = f.x; r[2 * k + 1] = f.y; }
+    }
 }
 
 // kAct: 0 none, 1 GELU (tanh), 2 SiLU; kSplit: K split across a cluster;
@@ -328,7 +349,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
     const int seg_per_row = (kTM / p.splits) / 8;      // 8-channel segments per owned row
     const int nunits = mvalid * seg_per_row;
     constexpr int kMaxIt = 4;                          // (128 tokens · 8 segs) / 256 threads
-    uint4 rres[kMaxIt];
+    float rres[kMaxIt][8];
     if constexpr (kSplit) {
         if (epi) {
             const int nb = n0 + split * (kTM / p.splits);
@@ -336,10 +357,7 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
             for (int it = 0; it < kMaxIt; ++it) {
                 const int u = tid - 64 + it * kConvWarps * 32;
                 const int mm = u / seg_per_row, n = nb + (u - mm * seg_per_row) * 8;
-                rres[it] = make_uint4(0u, 0u, 0u, 0u);
-                if (p.residual && u < nunits && n < p.N)
-                    rres[it] = *reinterpret_cast<const uint4*>(
-                        static_cast<const __nv_bfloat16*>(p.residual) + (m0 + mm) * p.ldr + n);
+                load_res8(p, m0 + mm, n, p.residual && u < nunits && n < p.N, rres[it]);
             }
         }
     }
@@ -378,14 +396,10 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                         const float4 b = *reinterpret_cast<const float4*>(stg + r * kStageStride + seg + 4);
                         float y[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
                         if (p.residual) {
-                            const uint4 rr = *reinterpret_cast<const uint4*>(
-                                static_cast<const __nv_bfloat16*>(p.residual) + m * p.ldr + n);
-                            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+                            float rr[8];
+                            load_res8(p, m, n, true, rr);
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const float2 f = __bfloat1622float2(r2[k]);
-                                y[2 * k] += f.x; y[2 * k + 1] += f.y;
-                            }
+                            for (int k = 0; k < 8; ++k) y[k] += rr[k];
                         }
                         if (p.y_f32) {
                             float* dst = static_cast<float*>(p.y) + m * p.ldy + n;
@@ -461,13 +475,8 @@ w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmX,
                     y[0] += a4.x; y[1] += a4.y; y[2] += a4.z; y[3] += a4.w;
                     y[4] += b4.x; y[5] += b4.y; y[6] += b4.z; y[7] += b4.w;
                 }
-                const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rres[it]);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float2 f = __bfloat1622float2(r2[k]);   // zero without a residual
-                    y[2 * k] = act(y[2 * k]) + f.x;
-                    y[2 * k + 1] = act(y[2 * k + 1]) + f.y;
-                }
+                for (int k = 0; k < 8; ++k) y[k] = act(y[k]) + rres[it][k];   // zero without a residual
                 if (p.y_f32) {
                     float* dst = static_cast<float*>(p.y) + m * p.ldy + n;
                     *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);

@@ -37,6 +37,10 @@ def _declare(lib):
                                        c.c_int32]
     lib.sfb_rdt1b_graph_kernels.argtypes = [c.c_void_p, c.c_int32, c.POINTER(c.c_int64)]
     lib.sfb_rdt1b_set_path.argtypes = [c.c_void_p, c.c_int32]
+    lib.sfb_rdt1b_tick.argtypes = [c.c_void_p, c.c_int32, c.c_uint64, c.c_void_p, c.c_void_p, c.c_void_p,
+                                   c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p]
+    lib.sfb_rdt1b_invalidate_condition.argtypes = [c.c_void_p]
+    lib.sfb_rdt1b_tick_stats.argtypes = [c.c_void_p, c.POINTER(c.c_int64), c.POINTER(c.c_int64)]
     lib.sfb_rdt1b_config_from_json.argtypes = [c.c_char_p, c.POINTER(RDT1BConfig)]
     lib.sfb_rdt1b_load_safetensors.argtypes = [c.c_void_p, c.c_char_p, c.POINTER(c.c_int64),
                                                c.POINTER(c.c_int64)]
@@ -44,7 +48,7 @@ def _declare(lib):
                                               c.POINTER(c.c_int64)]
     lib.sfb_rdt1b_params_missing.argtypes = [c.c_void_p, c.POINTER(c.c_int64), c.c_char_p, c.c_int32]
     for f in ("default_config", "create", "destroy", "encode", "forward", "sample", "param",
-              "schedule", "graph_kernels", "set_path", "config_from_json", "load_safetensors", "load_checkpoint",
+              "schedule", "graph_kernels", "set_path", "tick", "invalidate_condition", "tick_stats", "config_from_json", "load_safetensors", "load_checkpoint",
               "params_missing"):
         getattr(lib, "sfb_rdt1b_" + f).restype = c.c_int
     lib._rdt_declared = True
@@ -108,6 +112,24 @@ class RDT1B:
         assert not noise.is_cuda and not out.is_cuda
         _capi.check(self.lib.sfb_rdt1b_sample(self.h, noise.shape[0], noise.data_ptr(), out.data_ptr(),
                                               1, _sh(stream)), "rdt1b sample")
+
+    def tick(self, frame_id: int, state, noise, actions, lang=None, lang_len=None, img=None,
+             stream=None) -> None:
+        """One control tick (sfb_rdt1b_tick): re-encodes lang/img only when
+        frame_id changed, then denoises noise into actions. Every tensor may
+        live on the host (pinned) or the device."""
+        p = lambda t: None if t is None else t.data_ptr()
+        _capi.check(self.lib.sfb_rdt1b_tick(self.h, noise.shape[0], int(frame_id), p(lang), p(lang_len), p(img),
+                                            p(state), p(noise), p(actions), _sh(stream)), "tick")
+
+    def invalidate_condition(self) -> None:
+        _capi.check(self.lib.sfb_rdt1b_invalidate_condition(self.h), "invalidate_condition")
+
+    def tick_stats(self):
+        """(ticks, encodes) run on this handle."""
+        t, e = ctypes.c_int64(), ctypes.c_int64()
+        _capi.check(self.lib.sfb_rdt1b_tick_stats(self.h, ctypes.byref(t), ctypes.byref(e)), "tick_stats")
+        return t.value, e.value
 
     def set_path(self, path: int) -> None:
         """One-session execution path: 0 persistent projection kernel (default),

@@ -35,6 +35,8 @@ def make(M, N, K, seed, dev, bias=True, residual=False):
 
 def check(be, M, N, K, seed, dev, act="none", bias=True, residual=False, splits=0, f32=False):
     x, q, s, b, r = make(M, N, K, seed, dev, bias, residual)
+    if f32 and r is not None:
+        r = (r.float() + 1e-3).contiguous()             # the residual has the output's dtype
     y = torch.empty(M, N, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
     be.w8a16_linear(x, q, s, y, bias=b, residual=r, act=act, num_splits=splits)
     torch.cuda.synchronize()
@@ -118,3 +120,47 @@ def test_reference_dequant_then_matmul(be, gpu):
 @pytest.mark.parametrize("M,act,residual", [(2144, "none", False), (1072, "gelu", True)])
 def test_serving_shapes(be, gpu, M, act, residual):
     check(be, M, 2048, 2048, 70 + M, gpu, act=act, residual=residual)
+
+
+@pytest.mark.parametrize("M,splits", [(67, 0), (67, 1), (300, 0)])
+def test_fp32_output_with_fp32_residual(be, gpu, M, splits):
+    # the model's residual stream is fp32: y = x·Wᵀ + b + r with r and y fp32 (may alias)
+    check(be, M, 2048, 2048, 13 + M, gpu, residual=True, f32=True, splits=splits)
+
+
+@pytest.mark.parametrize("M,K,F,N,f32", [(67, 2048, 2048, 2048, False), (67, 2048, 2048, 2048, True),
+                                         (80, 1024, 512, 128, False), (1, 256, 256, 64, True)])
+def test_mlp_as_one_launch(be, gpu, M, K, F, N, f32):
+    """sfb_w8a16_mlp (two stages of the persistent projection kernel) against
+    the oracle, and against two sfb_w8a16_linear calls within one output ulp."""
+    g = torch.Generator().manual_seed(M + K + F + N)
+    x = torch.randn(M, K, generator=g).bfloat16().to(gpu)
+
+    def layer(n, k):
+        wf = torch.randn(n, k, generator=g) * 0.02
+        s = wf.abs().amax(dim=1) / 127.0
+        q = torch.round(wf / s[:, None]).clamp(-127, 127).to(torch.int8)
+        b = (torch.randn(n, generator=g) * 0.1).bfloat16()
+        return q.to(gpu), s.float().to(gpu), b.to(gpu)
+
+    q1, s1, b1 = layer(F, K)
+    q2, s2, b2 = layer(N, F)
+    dt = torch.float32 if f32 else torch.bfloat16
+    r = torch.randn(M, N, generator=g).to(dt).to(gpu)
+    y = torch.empty(M, N, dtype=dt, device=gpu)
+    be.w8a16_mlp(x, q1, s1, q2, s2, y, b1=b1, b2=b2, residual=r, act="gelu")
+    h = torch.empty(M, F, dtype=torch.bfloat16, device=gpu)
+    y2 = torch.empty_like(y)
+    be.w8a16_linear(x, q1, s1, h, bias=b1, act="gelu")
+    be.w8a16_linear(h, q2, s2, y2, bias=b2, residual=r)
+    torch.cuda.synchronize()
+    hr = oracle.w8a16_linear(x.float().cpu().numpy(), q1.cpu().numpy(), s1.cpu().numpy(),
+                             b1.float().cpu().numpy(), None, act=1)
+    hr = torch.from_numpy(hr).bfloat16().float().numpy()          # h is stored in bf16
+    ref = oracle.w8a16_linear(hr, q2.cpu().numpy(), s2.cpu().numpy(), b2.float().cpu().numpy(),
+                              r.float().cpu().numpy(), act=0)
+    out = y.float().cpu().numpy()
+    # h may round differently in one bf16 ulp where the two kernels' fp32 sums differ
+    tol = 4 * ulp_bf16(ref) + 2e-3 * np.abs(ref).max()
+    assert (np.abs(out - ref) <= tol).all(), np.abs(out - ref).max()
+    assert (y.float() - y2.float()).abs().max().item() <= float(tol.max())
