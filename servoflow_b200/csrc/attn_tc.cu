@@ -215,7 +215,10 @@ __device__ __forceinline__ uint32_t key_bits(const AttnTcParams& p, int b, int k
     return bits;
 }
 
-template <typename T>
+// kAMask: the instantiation that applies an additive mask (sfb_attn_args.
+// attn_mask); the other carries no mask code, so its softmax loop keeps the
+// compact body it was tuned with.
+template <typename T, bool kAMask>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
@@ -542,7 +545,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             wait(bar_s(u), (j / kBufs) & 1);
             SFB_T(3 + 4 * uses);
             tc_fence_after_sync();
-            const bool full = (key0 + kTileKeys <= kend) && !use_mask && !p.causal && p.amask == nullptr;
+            const bool full = (key0 + kTileKeys <= kend) && !use_mask && !p.causal && !kAMask;
             // pass 1: row max of the raw logits. In a tile with invalid keys
             // (beyond kv_len, masked, or causal) those logits are replaced by
             // -inf in TMEM first, so pass 2 is the same code for every tile.
@@ -561,15 +564,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         a[i]  = (va >> i) & 1u ? a[i] : -INFINITY;
                         bb[i] = (vb >> i) & 1u ? bb[i] : -INFINITY;
                     }
-                    if (p.amask != nullptr && qi < p.Lq) {
+                    if constexpr (kAMask) {
                         // additive mask: raw logit + m / scale, so that the later
-                        // scaling gives scale·q·k + m
-                        const int64_t mrow = static_cast<int64_t>(b) * p.am_sb + static_cast<int64_t>(qi) * p.am_ss;
-                        const int ka = key0 + 64 * hh, kb = ka + 32;
+                        // scaling gives scale·q·k + m (masked keys stay -inf)
+                        if (qi < p.Lq) {
+                            const int64_t mrow = static_cast<int64_t>(b) * p.am_sb + static_cast<int64_t>(qi) * p.am_ss;
+                            const int ka = key0 + 64 * hh;
 #pragma unroll 4
-                        for (int i = 0; i < 32; ++i) {
-                            if ((va >> i) & 1u) a[i] = fmaf(attn_mask_at(p.amask, p.am_dt, mrow + ka + i), p.inv_scale, a[i]);
-                            if ((vb >> i) & 1u) bb[i] = fmaf(attn_mask_at(p.amask, p.am_dt, mrow + kb + i), p.inv_scale, bb[i]);
+                            for (int i = 0; i < 32; ++i) {
+                                if ((va >> i) & 1u) a[i] = fmaf(attn_mask_at(p.amask, p.am_dt, mrow + ka + i), p.inv_scale, a[i]);
+                                if ((vb >> i) & 1u) bb[i] = fmaf(attn_mask_at(p.amask, p.am_dt, mrow + ka + 32 + i), p.inv_scale, bb[i]);
+                            }
                         }
                     }
                     tmem_st32(tS + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(a));
@@ -860,11 +865,14 @@ int attention_tc_launch(const sfb_attn_args& a, cudaStream_t stream, const AttnO
     if (p.splits > std::max(1, ntiles_max)) p.splits = std::max(1, ntiles_max);
     if ((p.o_ss % 8) != 0 && p.splits == 1) return SFB_ERR_ALIGN;
 
-    auto kern = a.dtype == SFB_BF16 ? attn_tc::attn_fwd_tc_kernel<__nv_bfloat16>
-                                    : attn_tc::attn_fwd_tc_kernel<__half>;
-    // kernel attributes, set once per dtype and device (idempotent: a race only repeats them)
-    static std::atomic<bool> attr_done[2][64];
-    const int ki = a.dtype == SFB_BF16 ? 0 : 1;
+    const bool am = a.attn_mask != nullptr;
+    auto kern = a.dtype == SFB_BF16 ? (am ? attn_tc::attn_fwd_tc_kernel<__nv_bfloat16, true>
+                                          : attn_tc::attn_fwd_tc_kernel<__nv_bfloat16, false>)
+                                    : (am ? attn_tc::attn_fwd_tc_kernel<__half, true>
+                                          : attn_tc::attn_fwd_tc_kernel<__half, false>);
+    // kernel attributes, set once per variant and device (idempotent: a race only repeats them)
+    static std::atomic<bool> attr_done[4][64];
+    const int ki = (a.dtype == SFB_BF16 ? 0 : 1) + (am ? 2 : 0);
     if (!attr_done[ki][dev.ordinal & 63].load(std::memory_order_acquire)) {
         cudaError_t e1 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               attn_tc::kSmemBytes);

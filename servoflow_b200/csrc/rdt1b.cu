@@ -276,6 +276,10 @@ static int build_dense(Model& m) {
         const Block& bl = m.blocks[l];
         f = static_cast<int>(st.size());
         SFB_TRY(stage(bl.proj, m.attn, 64, 0, m.x, D, true, m.x, nullptr, 0, bl.norm2));
+        // the block's cross-attention K/V (one session) are read right after this
+        // launch: pulled into L2 while its two projections run
+        st.back().l2_prefetch = reinterpret_cast<const uint8_t*>(m.kv[l]);
+        st.back().l2_bytes = static_cast<uint64_t>(l % 2 == 0 ? c.max_lang_len : c.img_len) * 2 * D * 2;
         SFB_TRY(stage(bl.cq, m.xg, 64, 0, m.h, D, false, nullptr, m.ss, nss, nullptr));
         launch(f);
         f = static_cast<int>(st.size());
@@ -304,7 +308,7 @@ static int build_dense(Model& m) {
 
 static int dense(const Model& m, int i, cudaStream_t s) {
     const Model::DenseLaunch& d = m.dl[i];
-    return dense_launch(m.d_stages + d.first, d.count, m.d_ctr + d.ctr, m.S(), s, true);
+    return dense_launch(m.d_stages + d.first, d.count, m.d_ctr + d.ctr, m.S(), s, true, i);
 }
 
 static int create(Model& m) {

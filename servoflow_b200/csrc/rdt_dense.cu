@@ -63,6 +63,8 @@ struct alignas(64) DenseStage {
     __nv_bfloat16* xg;               // [M, N] (ldg)
     float* ss_out;                   // or null: [tiles · 4][80] partial Σ y² per token row (y as stored)
     const float* ss_in;              // or null: [n_ss_in][80] partials of X's rows; scales rows by r[m]
+    const uint8_t* l2_prefetch;      // or null: a region the next kernel reads (a cross-attention
+    uint64_t l2_bytes;               // K/V cache), pulled into L2 while this stage runs
     int64_t ldr, ldy, ldg;
     int32_t n_ss_in;
     int32_t N, K, TM, tiles, act, y_f32;
@@ -154,6 +156,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         if ((it & 63u) == 63u && ptx::global_timer_ns() - t0 > timeout_ns) return false;
     }
 }
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void dsmem_st_v4(uint32_t addr, float4 v) {
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};"
                  ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
@@ -166,9 +172,23 @@ __device__ __forceinline__ int units_of(const DenseStage& S, int cl, int ncl) {
 
 // The kernel body: `stages` in global memory (a model's stage table) or in
 // the parameter space of a launch (dense_pair_kernel).
+#ifdef SFB_TRACE
+// per launch slot: [CTA < 160][stage < 16, then 16 = setup][4] global-timer stamps
+constexpr int kTrStages = 17;
+#define DN_T(st, k) do { if (trace != nullptr && blockIdx.x < 160 && (st) < kTrStages) \
+        trace[(blockIdx.x * kTrStages + (st)) * 4 + (k)] = ptx::global_timer_ns(); } while (0)
+#else
+#define DN_T(st, k) do { } while (0)
+#endif
+
 __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages, int nst,
-                                          unsigned long long* __restrict__ ctr, int M) {
+                                          unsigned long long* __restrict__ ctr, int M
+#ifdef SFB_TRACE
+                                          , unsigned long long* trace
+#endif
+                                          ) {
     using namespace ptx;
+    if (threadIdx.x == 0) DN_T(16, 0);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -215,6 +235,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
     cluster_wait();
     const uint32_t tmem = *tmem_holder;
     const uint64_t target = (*gen_slot + 1) * ncta;     // a stage is done when every CTA added 1
+    if (tid == 0) DN_T(16, 1);
 
     bool ok = true;
     auto wait = [&](int b, uint32_t parity) {
@@ -229,6 +250,18 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
             const DenseStage& S = stages[s];
             const int nu = units_of(S, cl, ncl), nk = S.K / 64 / kSplit;
             const uint32_t bytes = static_cast<uint32_t>(S.TM) * 64u;
+            if (S.l2_prefetch != nullptr && lane == 0) {
+                // this CTA's slice of the region, in 64 KB bulk prefetches (16-byte granules)
+                const uint64_t total = S.l2_bytes & ~15ull;
+                const uint64_t per = ((total + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+                const uint64_t b0 = per * blockIdx.x;
+                const uint64_t b1 = b0 + per < total ? b0 + per : total;
+                for (uint64_t o = b0; o < b1; o += 65536) {
+                    const uint64_t n = b1 - o < 65536 ? b1 - o : 65536;
+                    prefetch_l2_bulk(S.l2_prefetch + o, static_cast<uint32_t>(n));
+                }
+            }
+            __syncwarp();
             for (int j = 0; j < nu && ok; ++j) {
                 const int n0 = (cl + j * ncl) * S.TM;
                 for (int c = 0; c < nk; ++c, ++gw) {
@@ -267,6 +300,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 }
             }
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0 && ok;
+            if (lane == 0) DN_T(s, 0);
             fence_proxy_async_global();                    // generic writes of other CTAs → this TMA
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[kBarDep]);    // also after a failure: nobody waits in vain
@@ -375,12 +409,38 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 if (j == 0) {
                     wait(kBarDep, xs & 1);
                     if (S.ss_in != nullptr) {
-                        for (int m = warp - 2; m < mvalid; m += 8) {
+                        // warp w sums rows w, w + 8, ...: every load is issued before any
+                        // sum needs it (one L2 round trip, not one per row)
+                        constexpr int kRowsPerWarp = (kBN + 7) / 8;
+                        const int np = S.n_ss_in;
+                        float part[kRowsPerWarp];
+#pragma unroll
+                        for (int i = 0; i < kRowsPerWarp; ++i) {
+                            const int m = warp - 2 + 8 * i;
                             float a = 0.f;
-                            for (int p = lane; p < S.n_ss_in; p += 32) a += S.ss_in[p * kBN + m];
+                            if (m < mvalid) {
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const int p = lane + 32 * q;
+                                    if (p < np) a += S.ss_in[p * kBN + m];
+                                }
+                            }
+                            part[i] = a;
+                        }
+                        for (int q = 4 * 32; q < np; q += 32) {      // more than 128 partials (not used by RDT-1B)
+#pragma unroll
+                            for (int i = 0; i < kRowsPerWarp; ++i) {
+                                const int m = warp - 2 + 8 * i;
+                                if (m < mvalid && q + lane < np) part[i] += S.ss_in[(q + lane) * kBN + m];
+                            }
+                        }
+#pragma unroll
+                        for (int i = 0; i < kRowsPerWarp; ++i) {
+                            float a = part[i];
 #pragma unroll
                             for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                            if (lane == 0) rinv[m] = 1.f / sqrtf(a / static_cast<float>(S.K) + S.eps);
+                            const int m = warp - 2 + 8 * i;
+                            if (lane == 0 && m < mvalid) rinv[m] = 1.f / sqrtf(a / static_cast<float>(S.K) + S.eps);
                         }
                     }
                     named_bar_sync(1, 256);
@@ -392,6 +452,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 const float sc = (lane_ok && n0 + trow < S.N) ? S.w_scale[n0 + trow] : 0.f;
                 float v[2][32];
                 wait(kBarAccFull + buf, (ue >> 1) & 1);
+                if (et == 0 && j == 0) DN_T(s, 1);
                 tc_fence_after_sync();
                 const uint32_t lane_off = static_cast<uint32_t>(win * 32) << 16;
                 tmem_ld32(tmem + buf * 128 + lane_off + 32 * hh, v[0]);
@@ -528,9 +589,11 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
             // (5) this CTA is done with stage s: publish its writes, bump the counter
             named_bar_sync(1, 256);
             if (et == 0) {
+                DN_T(s, 2);
                 fence_proxy_async_global();
                 __threadfence();
                 red_release_gpu_add(&ctr[1 + s], 1ull);
+                DN_T(s, 3);
             }
         }
     }
@@ -548,8 +611,16 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long long* __restrict__ ctr, int M) {
-    dense_run(stages, nst, ctr, M);
+rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long long* __restrict__ ctr, int M
+#ifdef SFB_TRACE
+                 , unsigned long long* trace
+#endif
+                 ) {
+    dense_run(stages, nst, ctr, M
+#ifdef SFB_TRACE
+              , trace
+#endif
+              );
 }
 
 // Two stages passed by value (tensor maps in the parameter space): a launch
@@ -557,7 +628,11 @@ rdt_dense_kernel(const DenseStage* __restrict__ stages, int nst, unsigned long l
 struct DenseStagePair { DenseStage s[2]; };
 __global__ void __launch_bounds__(kThreads, 1)
 dense_pair_kernel(const __grid_constant__ DenseStagePair p, unsigned long long* __restrict__ ctr, int M) {
-    dense_run(p.s, 2, ctr, M);
+    dense_run(p.s, 2, ctr, M
+#ifdef SFB_TRACE
+              , nullptr
+#endif
+              );
 }
 
 }  // namespace dense
@@ -640,13 +715,26 @@ static cudaLaunchConfig_t dense_config(int ncl, cudaStream_t stream, cudaLaunchA
 
 // One launch over stages[0, nst) (device memory); ctr: nst + 1 counters of
 // this launch slot (zero at allocation, never reset).
-int dense_launch(const DenseStage* stages, int nst, unsigned long long* ctr, int M, cudaStream_t stream, bool pdl) {
+#ifdef SFB_TRACE
+static unsigned long long* g_dense_trace = nullptr;
+extern "C" void sfb_debug_set_dense_trace(void* p) { g_dense_trace = static_cast<unsigned long long*>(p); }
+#endif
+
+int dense_launch(const DenseStage* stages, int nst, unsigned long long* ctr, int M, cudaStream_t stream, bool pdl,
+                 int trace_slot) {
     const DeviceInfo& dev = device_info();
     const int ncl = dense_clusters(dev);
     if (ncl <= 0) { record_cuda_error(cudaErrorInvalidConfiguration, "dense kernel clusters"); return SFB_ERR_LAUNCH; }
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = dense_config(ncl, stream, attr, pdl);
+#ifdef SFB_TRACE
+    unsigned long long* tr = (g_dense_trace != nullptr && trace_slot >= 0)
+                                 ? g_dense_trace + static_cast<size_t>(trace_slot) * 160 * dense::kTrStages * 4 : nullptr;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, dense::rdt_dense_kernel, stages, nst, ctr, M, tr);
+#else
+    (void)trace_slot;
     cudaError_t e = cudaLaunchKernelEx(&cfg, dense::rdt_dense_kernel, stages, nst, ctr, M);
+#endif
     if (e != cudaSuccess) {
         (void)cudaGetLastError();
         record_cuda_error(e, "dense kernel launch");

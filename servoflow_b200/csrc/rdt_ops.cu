@@ -29,50 +29,6 @@ namespace rdt {
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
 
-// x, out: [rows, D] with row strides; w: [D]; D % 256 == 0, D <= 8192.
-__global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
-                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
-                                int64_t ldo, int rows, int D, float eps) {
-    pdl_trigger();
-    pdl_wait();
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= rows) return;
-    const __nv_bfloat16* xr = x + warp * ldx;
-    float ss = 0.f;
-    for (int c = lane * 8; c < D; c += 256) {
-        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f = __bfloat1622float2(h[i]);
-            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + eps);
-    __nv_bfloat16* orow = out + warp * ldo;
-    for (int c = lane * 8; c < D; c += 256) {
-        const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
-        const uint4 g = *reinterpret_cast<const uint4*>(w + c);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-        const __nv_bfloat162* gw = reinterpret_cast<const __nv_bfloat162*>(&g);
-        uint4 r;
-        __nv_bfloat162* ro = reinterpret_cast<__nv_bfloat162*>(&r);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f = __bfloat1622float2(h[i]), gg = __bfloat1622float2(gw[i]);
-            // (x / rms) · w, the order of the reference's RmsNorm
-            ro[i] = __floats2bfloat162_rn(f.x * inv * gg.x, f.y * inv * gg.y);
-        }
-        *reinterpret_cast<uint4*>(orow + c) = r;
-    }
-}
-
-// rms_norm for D = 32·8·kC (kC 16-byte chunks per lane): the constant weight
-// is read before the dependency wait and the row is kept in registers, so the
-// kernel's critical path is one load of x, the reduction and the store. Same
-// operation order as rms_norm_kernel (identical results).
 // Eight consecutive values of a bf16 or fp32 row as fp32.
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
     const uint4 u = *reinterpret_cast<const uint4*>(p);
@@ -85,6 +41,48 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// x (bf16 or fp32), out (bf16): [rows, D] with row strides; w: [D]; D % 256 == 0.
+template <typename TX>
+__global__ void rms_norm_kernel(const TX* __restrict__ x, int64_t ldx,
+                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                int64_t ldo, int rows, int D, float eps) {
+    pdl_trigger();
+    pdl_wait();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const TX* xr = x + warp * ldx;
+    float ss = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+        float f[8];
+        load8(xr + c, f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss = fmaf(f[2 * i], f[2 * i], fmaf(f[2 * i + 1], f[2 * i + 1], ss));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + eps);
+    __nv_bfloat16* orow = out + warp * ldo;
+    for (int c = lane * 8; c < D; c += 256) {
+        float f[8];
+        load8(xr + c, f);
+        const uint4 g = *reinterpret_cast<const uint4*>(w + c);
+        const __nv_bfloat162* gw = reinterpret_cast<const __nv_bfloat162*>(&g);
+        uint4 r;
+        __nv_bfloat162* ro = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 gg = __bfloat1622float2(gw[i]);
+            // (x / rms) · w, the order of the reference's RmsNorm
+            ro[i] = __floats2bfloat162_rn(f[2 * i] * inv * gg.x, f[2 * i + 1] * inv * gg.y);
+        }
+        *reinterpret_cast<uint4*>(orow + c) = r;
+    }
+}
+
+// rms_norm for D = 32·8·kC (kC 16-byte chunks per lane): the constant weight
+// is read before the dependency wait and the row is kept in registers, so the
+// kernel's critical path is one load of x, the reduction and the store. Same
+// operation order as rms_norm_kernel (identical results).
 template <int kC, typename TX>
 __global__ void rms_norm_reg_kernel(const TX* __restrict__ x, int64_t ldx,
                                     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
@@ -365,11 +363,16 @@ int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_
     const int warps_per_block = 4;
     const unsigned grid = (rows + warps_per_block - 1) / warps_per_block;
     if (x_f32) {
-        if (D != 2048) return SFB_ERR_SHAPE;
-        prefer_max_shared(rdt::rms_norm_reg_kernel<8, float>);
-        return launch_kernel(rdt::rms_norm_reg_kernel<8, float>, grid, 32 * warps_per_block, 0, s, true,
+        if (D == 2048) {
+            prefer_max_shared(rdt::rms_norm_reg_kernel<8, float>);
+            return launch_kernel(rdt::rms_norm_reg_kernel<8, float>, grid, 32 * warps_per_block, 0, s, true,
+                                 static_cast<const float*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+                                 static_cast<__nv_bfloat16*>(out), ldo, rows, eps);
+        }
+        prefer_max_shared(rdt::rms_norm_kernel<float>);
+        return launch_kernel(rdt::rms_norm_kernel<float>, grid, 32 * warps_per_block, 0, s, true,
                              static_cast<const float*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
-                             static_cast<__nv_bfloat16*>(out), ldo, rows, eps);
+                             static_cast<__nv_bfloat16*>(out), ldo, rows, D, eps);
     }
     if (D == 2048) {
         prefer_max_shared(rdt::rms_norm_reg_kernel<8, __nv_bfloat16>);
@@ -377,8 +380,8 @@ int rms_norm_launch(const void* x, int64_t ldx, const void* w, void* out, int64_
                              static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
                              static_cast<__nv_bfloat16*>(out), ldo, rows, eps);
     }
-    prefer_max_shared(rdt::rms_norm_kernel);
-    return launch_kernel(rdt::rms_norm_kernel, grid, 32 * warps_per_block, 0, s, true,
+    prefer_max_shared(rdt::rms_norm_kernel<__nv_bfloat16>);
+    return launch_kernel(rdt::rms_norm_kernel<__nv_bfloat16>, grid, 32 * warps_per_block, 0, s, true,
                          static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
                          static_cast<__nv_bfloat16*>(out), ldo, rows, D, eps);
 }
