@@ -211,6 +211,27 @@ int sfb_w8a16_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1,
                   void* y, int64_t ldy, int32_t y_dtype, int32_t M, int32_t K, int32_t F, int32_t N,
                   int32_t act, void* workspace, size_t workspace_bytes, void* stream);
 
+/* sfb_w8a16_mlp without a workspace: no counterpart in the reference. For
+ * callers that cannot allocate device memory where they run the MLP (a
+ * real-time loop that forbids cudaMalloc after start-up, a framework whose
+ * allocator owns all device memory, a plugin handed only its inputs and
+ * outputs). Its scratch (the stage counters and h) is a fixed array inside
+ * this library, sfb_w8a16_mlp_noalloc_max_bytes() bytes (about 320 KB: M·F <=
+ * 163840, e.g. M = 80 with F = 2048), which every GPU that loads the library
+ * holds until the process exits. Larger M·F return SFB_ERR_WORKSPACE with a
+ * message in sfb_last_error. The call allocates nothing: it clears the
+ * counters with cudaMemsetAsync on `stream` and launches. Every call shares
+ * the one array, so calls that overlap on the GPU (other streams, other
+ * threads) race; serialise them. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, once per device, with that
+ * device current); make that first call before any stream capture.
+ * Arguments and result as sfb_w8a16_mlp. */
+size_t sfb_w8a16_mlp_noalloc_max_bytes(void);
+int sfb_w8a16_mlp_noalloc(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const void* b1,
+                          const int8_t* w2, const float* s2, const void* b2, const void* residual, int64_t ldr,
+                          void* y, int64_t ldy, int32_t y_dtype, int32_t M, int32_t K, int32_t F, int32_t N,
+                          int32_t act, void* stream);
+
 /* ── RDT-1B denoising runtime ──────────────────────────────────────────────────
  * The model-level path around the kernels above, replacing for RDT-1B the
  * reference's RDT1BModel::encode_condition / denoise_step
