@@ -74,21 +74,29 @@ struct alignas(64) DenseStage {
 namespace dense {
 
 constexpr int kThreads = 11 * 32;
+// warp roles
+constexpr int kWarpW = 0;                     // int8 weight stream (TMA)
+constexpr int kWarpMma = 1;                   // tcgen05.mma issue
+constexpr int kWarpX = 2;                     // stage dependency + activation loads (TMA)
+constexpr int kWarpConv0 = 3;                 // warps 3..6: int8 → bf16 conversion
+constexpr int kWarpEpi0 = 7;                  // warps 7..10: epilogue (TMEM quadrant = warp % 4)
+constexpr int kEpiThreads = 128;
 constexpr int kBN = 80;                       // tokens per tile (MMA N): M <= 80
 constexpr int kSplit = 4;                     // cluster size = split-K ways
-constexpr int kNW = 6;                        // int8 weight ring slots (TM × 64 B, TM <= 128)
-constexpr int kNB = 3;                        // bf16 weight ring slots (SW128, TM × 128 B)
+constexpr int kNW = 4;                        // int8 weight ring slots (TM × 64 B, TM <= 128)
+constexpr int kNB = 4;                        // converted bf16 weight slots (SW128, TM × 128 B)
 constexpr int kNX = 8;                        // activation chunks per CTA (K / 4 / 64 <= 8)
 constexpr int kXBytes = kBN * 128;            // one activation chunk [80 × 64] bf16, SW128
 constexpr int kWBytes = 128 * 64;             // int8 slot
 constexpr int kWBBytes = 128 * 128;           // bf16 slot
 constexpr int kOffX = 0;
 constexpr int kOffWB = kOffX + kNX * kXBytes;                 // 81920
-constexpr int kOffW = kOffWB + kNB * kWBBytes;                // 131072
+constexpr int kOffW = kOffWB + kNB * kWBBytes;                // 147456
 constexpr int kOffRcv = kOffW + kNW * kWBytes;                // 180224
 constexpr int kRcvBytes = kSplit * 32 * kBN * 4;              // [4 sources][R <= 32][80] fp32
 constexpr int kOffRinv = kOffRcv + kRcvBytes;
-constexpr int kOffBar = kOffRinv + kBN * 4;
+constexpr int kOffRed = kOffRinv + kBN * 4;                   // [4 warps][80] partial row sums
+constexpr int kOffBar = kOffRed + 4 * kBN * 4;
 // barriers
 constexpr int kBarWFull = 0;                                  // [kNW]
 constexpr int kBarWFree = kBarWFull + kNW;                    // [kNW]
@@ -109,6 +117,7 @@ constexpr int kSmemBytes = kSmemUsed + 1024;                  // + alignment sla
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 static_assert(kOffWB % 1024 == 0 && kOffW % 1024 == 0 && kXBytes % 1024 == 0, "SW128 tile alignment");
 static_assert(kOffBar % 8 == 0, "barrier alignment");
+static_assert(kWarpEpi0 + 4 == kThreads / 32, "four epilogue warps last");
 constexpr uint64_t kWaitNs = 1000000000ull;
 constexpr uint64_t kDrainNs = 100000000ull;
 
@@ -160,6 +169,12 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
                  : "memory");
 }
+// Asynchronous store into a peer's shared memory that completes `16` bytes
+// of the transaction count of the peer's mbarrier at remote_bar.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float4 v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar) : "memory");
+}
 __device__ __forceinline__ void dsmem_st_v4(uint32_t addr, float4 v) {
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};"
                  ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
@@ -173,10 +188,10 @@ __device__ __forceinline__ int units_of(const DenseStage& S, int cl, int ncl) {
 // The kernel body: `stages` in global memory (a model's stage table) or in
 // the parameter space of a launch (dense_pair_kernel).
 #ifdef SFB_TRACE
-// per launch slot: [CTA < 160][stage < 16, then 16 = setup][4] global-timer stamps
+// per launch slot: [CTA < 160][stage < 16, then 16 = setup][8] global-timer stamps
 constexpr int kTrStages = 17;
 #define DN_T(st, k) do { if (trace != nullptr && blockIdx.x < 160 && (st) < kTrStages) \
-        trace[(blockIdx.x * kTrStages + (st)) * 4 + (k)] = ptx::global_timer_ns(); } while (0)
+        trace[(blockIdx.x * kTrStages + (st)) * 8 + (k)] = ptx::global_timer_ns(); } while (0)
 #else
 #define DN_T(st, k) do { } while (0)
 #endif
@@ -197,6 +212,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
     uint64_t* gen_slot = reinterpret_cast<uint64_t*>(smem + kOffGen);
     float* rcv = reinterpret_cast<float*>(smem + kOffRcv);
     float* rinv = reinterpret_cast<float*>(smem + kOffRinv);
+    float* red = reinterpret_cast<float*>(smem + kOffRed);
     auto sX = [&](int c) { return smem + kOffX + c * kXBytes; };
     auto sWB = [&](int s) { return smem + kOffWB + s * kWBBytes; };
     auto sW = [&](int s) { return smem + kOffW + s * kWBytes; };
@@ -211,9 +227,9 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         for (int i = 0; i < kNB; ++i) { mbar_init(&bars[kBarBFull + i], 4); mbar_init(&bars[kBarBFree + i], 1); }
         for (int i = 0; i < kNX; ++i) mbar_init(&bars[kBarXFull + i], 1);
         mbar_init(&bars[kBarDep], 1);
-        for (int i = 0; i < 2; ++i) { mbar_init(&bars[kBarAccFull + i], 1); mbar_init(&bars[kBarAccFree + i], 8); }
-        mbar_init(&bars[kBarRcv], 2 * kSplit);            // two warps of each source CTA
-        for (int i = 0; i < kSplit; ++i) mbar_init(&bars[kBarRcvFree + i], 8);   // the owner's 8 warps
+        for (int i = 0; i < 2; ++i) { mbar_init(&bars[kBarAccFull + i], 1); mbar_init(&bars[kBarAccFree + i], 4); }
+        mbar_init(&bars[kBarRcv], 1);                       // armed by the owner (expect_tx), filled by st.async
+        for (int i = 0; i < kSplit; ++i) mbar_init(&bars[kBarRcvFree + i], 4);   // the owner's 4 warps
         mbar_init(&bars[kBarDrain], 1);
         fence_mbarrier_init();
     }
@@ -242,7 +258,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         if (!mbar_wait(&bars[b], parity, ok ? kWaitNs : 0ull)) ok = false;
     };
 
-    if (warp == 0) {
+    if (warp == kWarpW) {
         // ── int8 weight stream, running ahead across stages ────────────────
         uint32_t gw = 0;
         const uint64_t pol = l2_evict_first_policy();
@@ -279,7 +295,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         // copies in flight land before the CTA leaves (bounded)
         for (uint32_t g = gw > kNW ? gw - kNW : 0; g < gw; ++g)
             if (!mbar_wait(&bars[kBarWFull + g % kNW], (g / kNW) & 1, kDrainNs)) ok = false;
-    } else if (warp == 10) {
+    } else if (warp == kWarpX) {
         // ── dependency + activation loads ──────────────────────────────────
         // xmask bit c: parity of the next completion of activation slot c
         // (stages may load different numbers of chunks)
@@ -321,7 +337,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         // the last loads land before the CTA leaves (bounded; immediate on the normal path)
         for (int c = 0; c < loaded; ++c)
             if (!mbar_wait(&bars[kBarXFull + c], (last_mask >> c) & 1u, kDrainNs)) ok = false;
-    } else if (warp == 1) {
+    } else if (warp == kWarpMma) {
         // ── MMA issuer ──────────────────────────────────────────────────────
         uint32_t gm = 0, um = 0, xmask = 0;                // xmask as the activation loader's
         for (int s = 0; s < nst && ok; ++s) {
@@ -360,24 +376,16 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
             __syncwarp();
             mbar_wait(&bars[kBarDrain], 0, kDrainNs);
         }
-    } else {
-        // ── converters, then the epilogue (warps 2..9) ─────────────────────
-        const int et = tid - 64;                           // 0..255
-        const int grp = (warp - 2) >> 2;                   // conversion group
-        const int ct = et - grp * 128;                     // 0..127 within the group
-        const int win = warp & 3;                          // TMEM lane window = owner rank
-        const int hh = (warp - 2) >> 2;                    // token half: columns [32hh, +32) and [64, 80) for hh = 0
-        uint32_t gc = 0, ue = 0, xs = 0;
-        const int mvalid = min(M, kBN);
+    } else if (warp < kWarpEpi0) {
+        // ── converters (warps 3..6): int8 [TM × 64] → bf16 SW128, running ahead
+        //    of the MMAs by up to kNB chunks, across units and stages ─────────
+        const int ct = tid - kWarpConv0 * 32;              // 0..127
+        uint32_t gc = 0;
         for (int s = 0; s < nst; ++s) {
             const DenseStage& S = stages[s];
-            const int nu = units_of(S, cl, ncl), nk = S.K / 64 / kSplit;
-            const int TM = S.TM, RPW = TM / 4;             // rows per TMEM window = rows per owner
-            for (int j = 0; j < nu; ++j, ++ue) {
-                const int n0 = (cl + j * ncl) * TM;
-                // (1) convert this unit's weight chunks: int8 [TM × 64] → bf16 SW128
+            const int nu = units_of(S, cl, ncl), nk = S.K / 64 / kSplit, TM = S.TM;
+            for (int j = 0; j < nu; ++j) {
                 for (int c = 0; c < nk; ++c, ++gc) {
-                    if ((gc & 1) != static_cast<uint32_t>(grp)) continue;
                     const int ws = gc % kNW, bs = gc % kNB;
                     wait(kBarWFull + ws, (gc / kNW) & 1);
                     if (gc >= kNB) wait(kBarBFree + bs, ((gc / kNB) - 1) & 1);
@@ -392,6 +400,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const uint32_t x = (h ? raw.y : raw.x) ^ 0x80808080u;
+                            // 0x4B0000bb = 2^23 + bb as fp32; minus (2^23 + 128) gives q exactly
                             const float f0 = __uint_as_float(prmt(x, 0x4B000000u, 0x7440u)) - 8388736.f;
                             const float f1 = __uint_as_float(prmt(x, 0x4B000000u, 0x7441u)) - 8388736.f;
                             const float f2 = __uint_as_float(prmt(x, 0x4B000000u, 0x7442u)) - 8388736.f;
@@ -405,149 +414,168 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                     __syncwarp();
                     if (lane == 0) { mbar_arrive(&bars[kBarWFree + ws]); mbar_arrive(&bars[kBarBFull + bs]); }
                 }
-                // (2) the stage's dependency (once per stage): rows' RMS factors
+            }
+        }
+    } else {
+        // ── epilogue (warps 7..10; TMEM quadrant q = warp % 4 = owner rank) ──
+        const int et = tid - kWarpEpi0 * 32;               // 0..127
+        const int q = warp & 3;
+        constexpr int kMaxIt = 3;                          // owner units (<= 80 · 32 / 8) / 128 threads
+        uint32_t ue = 0, xs = 0;
+        const int mvalid = min(M, kBN);
+        for (int s = 0; s < nst; ++s) {
+            const DenseStage& S = stages[s];
+            const int nu = units_of(S, cl, ncl);
+            const int TM = S.TM, RPW = TM / 4;             // rows per TMEM quadrant = rows per owner
+            const int segs = RPW / 8;                      // 8-channel segments per owned row
+            const int units = mvalid * segs;
+            for (int j = 0; j < nu; ++j, ++ue) {
+                const int n0 = (cl + j * ncl) * TM;
+                const int nb = n0 + rank * RPW;            // first channel this CTA owns
+                // (1) the stage's dependency (once per stage); rows' RMS factors
                 if (j == 0) {
                     wait(kBarDep, xs & 1);
                     if (S.ss_in != nullptr) {
-                        // warp w sums rows w, w + 8, ...: every load is issued before any
-                        // sum needs it (one L2 round trip, not one per row)
-                        constexpr int kRowsPerWarp = (kBN + 7) / 8;
+                        // warp w sums partials [w·np/4, (w+1)·np/4); lane l the rows l, l+32,
+                        // l+64 (consecutive floats: one 128-byte line per warp load); the
+                        // four warps' sums are then added in warp order
                         const int np = S.n_ss_in;
-                        float part[kRowsPerWarp];
-#pragma unroll
-                        for (int i = 0; i < kRowsPerWarp; ++i) {
-                            const int m = warp - 2 + 8 * i;
-                            float a = 0.f;
-                            if (m < mvalid) {
-#pragma unroll
-                                for (int q = 0; q < 4; ++q) {
-                                    const int p = lane + 32 * q;
-                                    if (p < np) a += S.ss_in[p * kBN + m];
-                                }
-                            }
-                            part[i] = a;
+                        const int p0 = (q * np) / 4, p1 = ((q + 1) * np) / 4;
+                        float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll 4
+                        for (int p = p0; p < p1; ++p) {
+                            const float* row = S.ss_in + p * kBN;
+                            a0 += row[lane];
+                            a1 += row[lane + 32];
+                            if (lane + 64 < kBN) a2 += row[lane + 64];
                         }
-                        for (int q = 4 * 32; q < np; q += 32) {      // more than 128 partials (not used by RDT-1B)
-#pragma unroll
-                            for (int i = 0; i < kRowsPerWarp; ++i) {
-                                const int m = warp - 2 + 8 * i;
-                                if (m < mvalid && q + lane < np) part[i] += S.ss_in[(q + lane) * kBN + m];
-                            }
-                        }
-#pragma unroll
-                        for (int i = 0; i < kRowsPerWarp; ++i) {
-                            float a = part[i];
-#pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                            const int m = warp - 2 + 8 * i;
-                            if (lane == 0 && m < mvalid) rinv[m] = 1.f / sqrtf(a / static_cast<float>(S.K) + S.eps);
+                        red[q * kBN + lane] = a0;
+                        red[q * kBN + lane + 32] = a1;
+                        if (lane + 64 < kBN) red[q * kBN + lane + 64] = a2;
+                        named_bar_sync(1, kEpiThreads);
+                        if (et < mvalid) {
+                            const float tot = ((red[et] + red[kBN + et]) + red[2 * kBN + et]) + red[3 * kBN + et];
+                            rinv[et] = 1.f / sqrtf(tot / static_cast<float>(S.K) + S.eps);
                         }
                     }
-                    named_bar_sync(1, 256);
+                    named_bar_sync(1, kEpiThreads);
+                }
+                // (2) this thread's owner-pass operands, loaded while the MMAs run
+                float rres[kMaxIt][8];
+                uint4 rbias[kMaxIt], rg[kMaxIt];
+#pragma unroll
+                for (int it = 0; it < kMaxIt; ++it) {
+                    const int u = et + it * kEpiThreads;
+                    const int m = u < units ? u / segs : 0, n = nb + (u < units ? (u - m * segs) * 8 : 0);
+                    const bool use = u < units && n < S.N;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) rres[it][k] = 0.f;
+                    rbias[it] = make_uint4(0u, 0u, 0u, 0u);
+                    rg[it] = make_uint4(0u, 0u, 0u, 0u);
+                    if (use && S.residual != nullptr) {
+                        if (S.y_f32) {
+                            const float* rp = static_cast<const float*>(S.residual) + m * S.ldr + n;
+                            const float4 a = *reinterpret_cast<const float4*>(rp), b = *reinterpret_cast<const float4*>(rp + 4);
+                            rres[it][0] = a.x; rres[it][1] = a.y; rres[it][2] = a.z; rres[it][3] = a.w;
+                            rres[it][4] = b.x; rres[it][5] = b.y; rres[it][6] = b.z; rres[it][7] = b.w;
+                        } else {
+                            const uint4 ru = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(S.residual) + m * S.ldr + n);
+                            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(r2[k]); rres[it][2 * k] = f.x; rres[it][2 * k + 1] = f.y; }
+                        }
+                    }
+                    if (use && S.bias != nullptr) rbias[it] = *reinterpret_cast<const uint4*>(S.bias + n);
+                    if (use && S.g_next != nullptr) rg[it] = *reinterpret_cast<const uint4*>(S.g_next + n);
                 }
                 // (3) accumulator → scaled partials into the owner's receive area
                 const int buf = ue & 1;
                 const bool lane_ok = lane < RPW;
-                const int trow = win * RPW + lane;             // tile row (owner win, slot lane)
+                const int trow = q * RPW + lane;               // tile row (owner q, slot lane)
                 const float sc = (lane_ok && n0 + trow < S.N) ? S.w_scale[n0 + trow] : 0.f;
-                float v[2][32];
+                // arm this CTA's receive barrier for the unit: the four sources' partials
+                // of its RPW rows (this thread has passed the previous unit's phase)
+                if (et == 0)
+                    mbar_arrive_expect_tx(&bars[kBarRcv], static_cast<uint32_t>(kSplit * RPW * kBN * 4));
+                if (ue >= 1) {
+                    // the owner has read this area's previous contents
+                    if (!mbar_wait_cluster(&bars[kBarRcvFree + q], (ue - 1) & 1, ok ? kWaitNs : 0ull)) ok = false;
+                }
                 wait(kBarAccFull + buf, (ue >> 1) & 1);
                 if (et == 0 && j == 0) DN_T(s, 1);
                 tc_fence_after_sync();
-                const uint32_t lane_off = static_cast<uint32_t>(win * 32) << 16;
-                tmem_ld32(tmem + buf * 128 + lane_off + 32 * hh, v[0]);
-                if (hh == 0) tmem_ld32(tmem + buf * 128 + lane_off + 64, v[1]);
-                tmem_ld_wait();
+                const uint32_t tq = tmem + buf * 128 + (static_cast<uint32_t>(q * 32) << 16);
+                const uint32_t base = dsmem_map(smem_u32(rcv + (rank * RPW + (lane_ok ? lane : 0)) * kBN),
+                                                static_cast<uint32_t>(q));
+                const uint32_t rbar = dsmem_map(smem_u32(&bars[kBarRcv]), static_cast<uint32_t>(q));
+#pragma unroll 1
+                for (int blk = 0; blk < 3; ++blk) {                 // 32 token columns at a time
+                    float v[32];
+                    tmem_ld32(tq + 32 * blk, v);
+                    tmem_ld_wait();
+                    if (lane_ok) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            if (blk * 32 + i < kBN)
+                                st_async_v4(base + (blk * 32 + i) * 4,
+                                            make_float4(v[i] * sc, v[i + 1] * sc, v[i + 2] * sc, v[i + 3] * sc), rbar);
+                        }
+                    }
+                }
                 tc_fence_before_sync();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars[kBarAccFree + buf]);
-                if (ue >= 1) {
-                    if (!mbar_wait_cluster(&bars[kBarRcvFree + win], (ue - 1) & 1, ok ? kWaitNs : 0ull)) ok = false;
-                }
-                if (lane_ok) {
-                    const uint32_t base = dsmem_map(smem_u32(rcv + (rank * RPW + lane) * kBN), static_cast<uint32_t>(win));
+                if (et == 0 && j == nu - 1) DN_T(s, 4);
+                // (4) owner pass: rows [nb, nb + RPW) of the tile, every token
+                if (!mbar_wait_cluster(&bars[kBarRcv], ue & 1, ok ? kWaitNs : 0ull)) ok = false;
+                if (et == 0 && j == nu - 1) DN_T(s, 5);
+                // sums of the four sources first, so the area is released before any
+                // global store of this pass
+                float ysum[kMaxIt][8];
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        dsmem_st_v4(base + (32 * hh + i) * 4,
-                                    make_float4(v[0][i] * sc, v[0][i + 1] * sc, v[0][i + 2] * sc, v[0][i + 3] * sc));
-                    if (hh == 0) {
+                for (int it = 0; it < kMaxIt; ++it) {
+                    const int u = et + it * kEpiThreads;
+                    const int m = u < units ? u / segs : 0, seg = u < units ? u - (u / segs) * segs : 0;
 #pragma unroll
-                        for (int i = 0; i < kBN - 64; i += 4)
-                            dsmem_st_v4(base + (64 + i) * 4,
-                                        make_float4(v[1][i] * sc, v[1][i + 1] * sc, v[1][i + 2] * sc, v[1][i + 3] * sc));
+                    for (int k = 0; k < 8; ++k) ysum[it][k] = 0.f;
+                    if (u < units) {
+#pragma unroll
+                        for (int src = 0; src < kSplit; ++src) {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) ysum[it][k] += rcv[(src * RPW + seg * 8 + k) * kBN + m];
+                        }
                     }
                 }
-                fence_acq_rel_cluster();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_remote(&bars[kBarRcv], static_cast<uint32_t>(win));
-                // (4) owner pass: rows [n0 + rank·RPW, +RPW) of the tile, every token
-                if (!mbar_wait_cluster(&bars[kBarRcv], ue & 1, ok ? kWaitNs : 0ull)) ok = false;
-                const int segs = RPW / 8;                      // 8-channel segments per row
-                const int units = mvalid * segs;
-                const int nb = n0 + rank * RPW;
-                for (int base_u = 0; base_u < units; base_u += 256) {
-                    const int u = base_u + et;
+                if (lane < kSplit) mbar_arrive_remote(&bars[kBarRcvFree + rank], static_cast<uint32_t>(lane));
+#pragma unroll
+                for (int it = 0; it < kMaxIt; ++it) {
+                    const int u = et + it * kEpiThreads;
+                    if (it * kEpiThreads >= units) break;          // uniform over the CTA
                     const bool valid = u < units && ok;
                     const int m = valid ? u / segs : 0, seg = valid ? u - (u / segs) * segs : 0;
                     const int n = nb + seg * 8;
                     float outv[8];
                     float sq = 0.f;
                     if (valid && n < S.N) {
-                        float yv[8];
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) yv[k] = 0.f;
-#pragma unroll
-                        for (int src = 0; src < kSplit; ++src) {
-#pragma unroll
-                            for (int k = 0; k < 8; ++k) yv[k] += rcv[(src * RPW + seg * 8 + k) * kBN + m];
-                        }
+                        const float* yv = ysum[it];
                         const float r = S.ss_in != nullptr ? rinv[m] : 1.f;
-                        float bb[8], rr[8];
-                        if (S.bias != nullptr) {
-                            const uint4 bu = *reinterpret_cast<const uint4*>(S.bias + n);
-                            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bu);
+                        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&rbias[it]);
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(b2[k]); bb[2 * k] = f.x; bb[2 * k + 1] = f.y; }
-                        } else {
+                        for (int k = 0; k < 4; ++k) {
+                            const float2 bb = __bfloat1622float2(b2[k]);
 #pragma unroll
-                            for (int k = 0; k < 8; ++k) bb[k] = 0.f;
-                        }
-                        if (S.residual != nullptr && S.y_f32) {
-                            const float* rp = static_cast<const float*>(S.residual) + m * S.ldr + n;
-                            const float4 a = *reinterpret_cast<const float4*>(rp), b = *reinterpret_cast<const float4*>(rp + 4);
-                            rr[0] = a.x; rr[1] = a.y; rr[2] = a.z; rr[3] = a.w; rr[4] = b.x; rr[5] = b.y; rr[6] = b.z; rr[7] = b.w;
-                        } else if (S.residual != nullptr) {
-                            const uint4 ru = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(S.residual) + m * S.ldr + n);
-                            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(r2[k]); rr[2 * k] = f.x; rr[2 * k + 1] = f.y; }
-                        } else {
-#pragma unroll
-                            for (int k = 0; k < 8; ++k) rr[k] = 0.f;
-                        }
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) {
-                            float t = fmaf(yv[k], r, bb[k]);
-                            if (S.act == 1) t = gelu_tanh(t);
-                            else if (S.act == 2) t = t / (1.f + expf(-t));
-                            outv[k] = t + rr[k];
+                            for (int h = 0; h < 2; ++h) {
+                                float t = fmaf(yv[2 * k + h], r, h ? bb.y : bb.x);
+                                if (S.act == 1) t = gelu_tanh(t);
+                                else if (S.act == 2) t = t / (1.f + expf(-t));
+                                outv[2 * k + h] = t + rres[it][2 * k + h];
+                            }
                         }
                         if (S.y_f32) {
                             float* dst = static_cast<float*>(S.y) + m * S.ldy + n;
                             *reinterpret_cast<float4*>(dst) = make_float4(outv[0], outv[1], outv[2], outv[3]);
                             *reinterpret_cast<float4*>(dst + 4) = make_float4(outv[4], outv[5], outv[6], outv[7]);
-                            if (S.g_next != nullptr) {
-                                const uint4 gu = *reinterpret_cast<const uint4*>(S.g_next + n);
-                                const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
-                                uint4 q;
-                                __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&q);
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    const float2 g = __bfloat1622float2(g2[k]);
-                                    q2[k] = __floats2bfloat162_rn(outv[2 * k] * g.x, outv[2 * k + 1] * g.y);
-                                }
-                                *reinterpret_cast<uint4*>(S.xg + m * S.ldg + n) = q;
-                            }
                         } else {
                             uint4 o;
                             __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -558,18 +586,17 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                                 outv[2 * k] = f.x; outv[2 * k + 1] = f.y;
                             }
                             *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(S.y) + m * S.ldy + n) = o;
-                            if (S.g_next != nullptr) {
-                                const uint4 gu = *reinterpret_cast<const uint4*>(S.g_next + n);
-                                const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
-                                uint4 q;
-                                __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&q);
+                        }
+                        if (S.g_next != nullptr) {
+                            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&rg[it]);
+                            uint4 qv;
+                            __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&qv);
 #pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    const float2 g = __bfloat1622float2(g2[k]);
-                                    q2[k] = __floats2bfloat162_rn(outv[2 * k] * g.x, outv[2 * k + 1] * g.y);
-                                }
-                                *reinterpret_cast<uint4*>(S.xg + m * S.ldg + n) = q;
+                            for (int k = 0; k < 4; ++k) {
+                                const float2 g = __bfloat1622float2(g2[k]);
+                                q2[k] = __floats2bfloat162_rn(outv[2 * k] * g.x, outv[2 * k + 1] * g.y);
                             }
+                            *reinterpret_cast<uint4*>(S.xg + m * S.ldg + n) = qv;
                         }
 #pragma unroll
                         for (int k = 0; k < 8; ++k) sq = fmaf(outv[k], outv[k], sq);
@@ -580,18 +607,15 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                         if (valid && seg == 0) S.ss_out[((n0 / TM) * kSplit + rank) * kBN + m] = sq;
                     }
                 }
-                // the receive area may be refilled by the sources: release it
-                fence_acq_rel_cluster();
-                __syncwarp();
-                if (lane < kSplit) mbar_arrive_remote(&bars[kBarRcvFree + rank], static_cast<uint32_t>(lane));
             }
             if (nu > 0) ++xs;
             // (5) this CTA is done with stage s: publish its writes, bump the counter
-            named_bar_sync(1, 256);
+            named_bar_sync(1, kEpiThreads);
             if (et == 0) {
+                // release at GPU scope: covers every epilogue thread's stores, which the
+                // named barrier ordered before it; readers acquire and fence the
+                // async proxy before their TMA loads
                 DN_T(s, 2);
-                fence_proxy_async_global();
-                __threadfence();
                 red_release_gpu_add(&ctr[1 + s], 1ull);
                 DN_T(s, 3);
             }
@@ -729,7 +753,7 @@ int dense_launch(const DenseStage* stages, int nst, unsigned long long* ctr, int
     cudaLaunchConfig_t cfg = dense_config(ncl, stream, attr, pdl);
 #ifdef SFB_TRACE
     unsigned long long* tr = (g_dense_trace != nullptr && trace_slot >= 0)
-                                 ? g_dense_trace + static_cast<size_t>(trace_slot) * 160 * dense::kTrStages * 4 : nullptr;
+                                 ? g_dense_trace + static_cast<size_t>(trace_slot) * 160 * dense::kTrStages * 8 : nullptr;
     cudaError_t e = cudaLaunchKernelEx(&cfg, dense::rdt_dense_kernel, stages, nst, ctr, M, tr);
 #else
     (void)trace_slot;
