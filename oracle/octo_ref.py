@@ -75,7 +75,7 @@ class RefOcto:
         p = f"blocks.{l}."
         r = self.r
         h = r(layer_norm(x, w[p + "norm1.weight"], w[p + "norm1.bias"]))
-        qkv = r(self.lin(h, p + "attn.qkv")).view(B, S, 3, H, 64)
+        qkv = r(self.lin(h, p + "attn.qkv")).view(B, S, 3, H, D // H)
         q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
         with torch.nn.attention.sdpa_kernel(torch.nn.attention.SDPBackend.MATH):
             o = r(F.scaled_dot_product_attention(q, k, v))
@@ -122,6 +122,7 @@ def load_weights(model, cfg) -> dict:
     """Every parameter of a servoflow_b200.octo.Octo as fp32 CPU tensors, the
     padded head weights cut to their valid blocks."""
     D, Fd, Hh = cfg.hidden, cfg.intermediate, cfg.head_hidden
+    Hp = (Hh + 63) // 64 * 64                     # the model pads the head's hidden width to 64
     HA = cfg.action_dim * cfg.action_horizon
     kin = HA + TIME_DIM + D
     kin_pad = (kin + 63) // 64 * 64
@@ -144,9 +145,9 @@ def load_weights(model, cfg) -> dict:
             w[p + n + ".bias"] = model.param(p + n + ".bias").float().cpu()
         lin(p + "attn.qkv", 3 * D, D); lin(p + "attn.proj", D, D)
         lin(p + "mlp.fc1", Fd, D); lin(p + "mlp.fc2", D, Fd)
-    lin("head.fc1", Hh, kin_pad, Hh, kin)
-    lin("head.fc2", Hh, Hh)
-    lin("head.fc3", out_pad, Hh, HA, Hh)
+    lin("head.fc1", Hp, kin_pad, Hh, kin)
+    lin("head.fc2", Hp, Hp, Hh, Hh)
+    lin("head.fc3", out_pad, Hp, HA, Hh)
     return w
 
 

@@ -42,6 +42,8 @@
 #include "common.cuh"
 
 namespace sfb {
+int attention_simt_launch(const sfb_attn_args& a, cudaStream_t stream);
+
 namespace octo {
 
 using rdt::Linear;
@@ -269,6 +271,7 @@ struct Model {
     std::vector<Block> blocks;
     Linear h1, h2, h3;                       // diffusion head
     int kin = 0, kin_pad = 0, out_pad = 0;   // head input width (valid / padded), fc3 rows (padded)
+    int hh_pad = 0;                          // head hidden width padded to 64 (zero rows / columns)
 
     __nv_bfloat16 *x, *xn, *qkv, *attn, *mid;          // backbone [B·S, ·]
     __nv_bfloat16 *cond, *hin, *hh1, *hh2;             // head
@@ -360,9 +363,10 @@ static int create(Model& m) {
     m.kin = HA + kTimeDim + D;
     m.kin_pad = (m.kin + 63) / 64 * 64;
     m.out_pad = (HA + 127) / 128 * 128;
-    SFB_TRY(new_linear(m, m.h1, c.head_hidden, m.kin_pad, "head.fc1", c.head_hidden, m.kin));
-    SFB_TRY(new_linear(m, m.h2, c.head_hidden, c.head_hidden, "head.fc2"));
-    SFB_TRY(new_linear(m, m.h3, m.out_pad, c.head_hidden, "head.fc3", HA, c.head_hidden));
+    m.hh_pad = (c.head_hidden + 63) / 64 * 64;
+    SFB_TRY(new_linear(m, m.h1, m.hh_pad, m.kin_pad, "head.fc1", c.head_hidden, m.kin));
+    SFB_TRY(new_linear(m, m.h2, m.hh_pad, m.hh_pad, "head.fc2", c.head_hidden, c.head_hidden));
+    SFB_TRY(new_linear(m, m.h3, m.out_pad, m.hh_pad, "head.fc3", HA, c.head_hidden));
 
     auto bf = [&](__nv_bfloat16** p, int64_t n) { return dalloc(m, reinterpret_cast<void**>(p), n * 2); };
     auto f32 = [&](float** p, int64_t n) { return dalloc(m, reinterpret_cast<void**>(p), n * 4); };
@@ -371,8 +375,8 @@ static int create(Model& m) {
     SFB_TRY(bf(&m.attn, BS * D)); SFB_TRY(bf(&m.mid, BS * F));
     SFB_TRY(bf(&m.cond, static_cast<int64_t>(B) * D));
     SFB_TRY(bf(&m.hin, static_cast<int64_t>(B) * m.kin_pad));
-    SFB_TRY(bf(&m.hh1, static_cast<int64_t>(B) * c.head_hidden));
-    SFB_TRY(bf(&m.hh2, static_cast<int64_t>(B) * c.head_hidden));
+    SFB_TRY(bf(&m.hh1, static_cast<int64_t>(B) * m.hh_pad));
+    SFB_TRY(bf(&m.hh2, static_cast<int64_t>(B) * m.hh_pad));
     SFB_TRY(f32(&m.xact, static_cast<int64_t>(B) * HA));
     SFB_TRY(f32(&m.vel, static_cast<int64_t>(B) * m.out_pad));
     // the condition starts as the reference's readout: a 0.1 fill
@@ -405,16 +409,21 @@ static int backbone(Model& m, int B, cudaStream_t s) {
         SFB_TRY(linear(bl.qkv, m.xn, D, M, m.qkv, 3 * D, 0, nullptr, s));
         sfb_attn_args a;
         std::memset(&a, 0, sizeof(a));
+        const int hd = c.head_dim;
         a.q = m.qkv; a.k = m.qkv + D; a.v = m.qkv + 2 * D; a.out = m.attn;
         const int64_t sb = static_cast<int64_t>(S) * 3 * D;
-        a.q_stride[0] = sb; a.q_stride[1] = 64; a.q_stride[2] = 3 * D;
+        a.q_stride[0] = sb; a.q_stride[1] = hd; a.q_stride[2] = 3 * D;
         for (int i = 0; i < 3; ++i) { a.k_stride[i] = a.q_stride[i]; a.v_stride[i] = a.q_stride[i]; }
-        a.out_stride[0] = static_cast<int64_t>(S) * D; a.out_stride[1] = 64; a.out_stride[2] = D;
+        a.out_stride[0] = static_cast<int64_t>(S) * D; a.out_stride[1] = hd; a.out_stride[2] = D;
         a.batch = B; a.heads = c.heads; a.heads_kv = c.heads; a.seq_q = S; a.seq_k = S;
-        a.head_dim = 64; a.dtype = SFB_BF16;               // scale 0: 1/sqrt(64)
-        AttnOpts o;
-        o.pdl = true;
-        SFB_TRY(attention_tc_launch(a, s, o));
+        a.head_dim = hd; a.dtype = SFB_BF16;               // scale 0: 1/sqrt(head_dim)
+        if (hd == 64) {
+            AttnOpts o;
+            o.pdl = true;
+            SFB_TRY(attention_tc_launch(a, s, o));
+        } else {
+            SFB_TRY(attention_simt_launch(a, s));
+        }
         SFB_TRY(linear(bl.proj, m.attn, D, M, m.x, D, 0, m.x, s));
         SFB_TRY(layer_norm(m.x, D, bl.ln2_g, bl.ln2_b, m.xn, D, M, D, s));
         SFB_TRY(linear(bl.fc1, m.xn, D, M, m.mid, F, 1, nullptr, s));
@@ -432,10 +441,9 @@ static int head_input(Model& m, int B, cudaStream_t s) {
 
 // fc1 → GELU → fc2 → GELU → fc3 of OctoDiffusionHead::forward on m.hin → m.vel.
 static int head_mlp(Model& m, int B, cudaStream_t s) {
-    const auto& c = m.c;
-    SFB_TRY(linear(m.h1, m.hin, m.kin_pad, B, m.hh1, c.head_hidden, 1, nullptr, s));
-    SFB_TRY(linear(m.h2, m.hh1, c.head_hidden, B, m.hh2, c.head_hidden, 1, nullptr, s));
-    return linear(m.h3, m.hh2, c.head_hidden, B, m.vel, m.out_pad, 0, nullptr, s, true);
+    SFB_TRY(linear(m.h1, m.hin, m.kin_pad, B, m.hh1, m.hh_pad, 1, nullptr, s));
+    SFB_TRY(linear(m.h2, m.hh1, m.hh_pad, B, m.hh2, m.hh_pad, 1, nullptr, s));
+    return linear(m.h3, m.hh2, m.hh_pad, B, m.vel, m.out_pad, 0, nullptr, s, true);
 }
 
 // num_steps head evaluations and Euler steps; the Euler step of step i and the
@@ -483,8 +491,12 @@ int sfb_octo_create(const sfb_octo_config* cfg, uint64_t seed, void** handle) {
     using namespace sfb;
     if (cfg == nullptr || handle == nullptr) return SFB_ERR_INVALID;
     const auto& c = *cfg;
-    if (c.head_dim != 64 || c.heads < 1 || c.hidden != c.heads * 64 || c.num_layers < 1 ||
-        c.intermediate < 64 || c.intermediate % 64 || c.head_hidden < 64 || c.head_hidden % 64 ||
+    // head_dim 64 runs the tensor-core attention, 16/32/128 the CUDA-core one
+    // (the reference's unit-test model has hidden 64 = 4 heads × 16,
+    // tests/models/test_octo.cpp:17-25); head_hidden is padded to 64 inside
+    if ((c.head_dim != 16 && c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128) || c.heads < 1 ||
+        c.hidden != c.heads * c.head_dim || c.hidden % 64 || c.num_layers < 1 ||
+        c.intermediate < 64 || c.intermediate % 64 || c.head_hidden < 1 ||
         c.action_dim < 1 || c.action_horizon < 1 || c.seq_len < 1 || c.max_sessions < 1 ||
         c.num_steps < 1 || c.num_steps > 1000 || c.hidden > 2048 || c.readout_token >= c.seq_len)
         return SFB_ERR_SHAPE;

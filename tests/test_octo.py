@@ -83,8 +83,9 @@ def test_api_argument_checks_without_a_gpu():
     cfg = default_config()
     assert lib.sfb_octo_create(None, 0, ctypes.byref(h)) == _capi.SFB_ERR_INVALID
     assert lib.sfb_octo_create(ctypes.byref(cfg), 0, None) == _capi.SFB_ERR_INVALID
-    for bad in (dict(head_dim=32), dict(hidden=400), dict(heads=5), dict(num_layers=0),
-                dict(intermediate=100), dict(head_hidden=100), dict(max_sessions=0), dict(num_steps=0),
+    for bad in (dict(head_dim=32), dict(head_dim=48, heads=8), dict(hidden=400), dict(heads=5),
+                dict(num_layers=0), dict(intermediate=100), dict(head_hidden=0), dict(max_sessions=0),
+                dict(num_steps=0),
                 dict(seq_len=0), dict(readout_token=64), dict(action_dim=0)):
         c = default_config(**bad)
         assert lib.sfb_octo_create(ctypes.byref(c), 0, ctypes.byref(h)) == _capi.SFB_ERR_SHAPE, bad

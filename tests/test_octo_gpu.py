@@ -156,3 +156,38 @@ def test_bad_session_counts(setup):
     assert e.value.status == _capi.SFB_ERR_SHAPE
     with pytest.raises(_capi.SfbError):
         m.sample(x, x)
+
+
+def test_reference_unit_test_config(gpu):
+    """The reference's own Octo unit-test model (tests/models/test_octo.cpp:17-25:
+    hidden 64 = 4 heads × head_dim 16, intermediate 128, 1 layer, head hidden
+    32): head_dim 16 runs the CUDA-core attention, the head's hidden width is
+    padded to 64 inside. The test's call pattern: a 0.1 context, x_t = 0.5,
+    t = 0.5, then one denoise_step; plus an encode of the backbone and a sample."""
+    cfg = default_config(hidden=64, heads=4, head_dim=16, intermediate=128, num_layers=1, action_dim=7,
+                         action_horizon=4, head_hidden=32, max_sessions=1)
+    model = Octo(cfg, seed=5)
+    try:
+        w = octo_ref.load_weights(model, cfg)
+        assert w["head.fc1.weight_full"].shape[0] == 64
+        assert torch.count_nonzero(w["head.fc1.weight_full"][32:]) == 0
+        ref = octo_ref.RefOcto(w, cfg, store=torch.bfloat16)
+        ctx = torch.full((1, cfg.hidden), 0.1).bfloat16()
+        model.set_condition(ctx.to(gpu))
+        x = torch.full((1, cfg.action_horizon, cfg.action_dim), 0.5)
+        v = torch.empty(1, cfg.action_horizon, cfg.action_dim, device=gpu)
+        model.denoise_step(x.to(gpu), 0.5, v)
+        torch.cuda.synchronize()
+        assert v.shape == x.shape and torch.isfinite(v).all()
+        max_abs, cos = close(v, ref.head(x, ctx.float()))
+        assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+        g = torch.Generator().manual_seed(9)
+        tokens = torch.randn(1, cfg.seq_len, cfg.hidden, generator=g).bfloat16()
+        feats = torch.empty(1, cfg.seq_len, cfg.hidden, dtype=torch.bfloat16, device=gpu)
+        model.encode(tokens.to(gpu), feats)
+        torch.cuda.synchronize()
+        out, _ = ref.encode(tokens.float())
+        excess, cos = close_tokens(feats, out)
+        assert excess < 0.05 and cos > 0.9999, (excess, cos)
+    finally:
+        model.close()
