@@ -138,17 +138,20 @@ struct Model {
     cudaStream_t own = nullptr;
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
 
-    // One session (B = 1): runs of consecutive projections between two
-    // attention kernels go through the persistent projection kernel
-    // (rdt_dense.cu) as stage tables built once here. dl[0] is block 0's
-    // qkv; then, per block l, dl[1 + 2l] = (proj, cross q) and
-    // dl[2 + 2l] = (cross proj, fc1, fc2, next qkv or the final layer).
+    // One session (B = 1): the network evaluation runs as stages of the
+    // persistent kernel (rdt_dense.cu) from stage tables built once here.
+    // dl[0]: every projection, self- and cross-attention of all blocks as one
+    // flat stage list, cut into launches of at most dense::kMaxStages stages (path 0).
+    // dl[1]: the projections and self-attention between two cross-attention
+    // kernels per launch (path 2): dl[1][0] = block 0's (qkv, self-attention,
+    // proj, cross q); dl[1][1 + l] = block l's (cross proj, fc1, fc2) followed
+    // by block l+1's first four stages, or by the final layer.
     struct DenseLaunch { int first, count, ctr; };
     bool dense_ok = false;
-    int path = 0;                             // 0: persistent kernel at one session; 1: per-projection kernels
-    DenseStage* d_stages = nullptr;           // device copy of the stage table
+    int path = 0;                             // 0, 2: persistent kernel at one session; 1: per-projection kernels
+    DenseStage* d_stages = nullptr;           // device copy of the stage tables
     unsigned long long* d_ctr = nullptr;      // completion counters, 1 + count per launch
-    std::vector<DenseLaunch> dl;
+    std::vector<DenseLaunch> dl[2];
     __nv_bfloat16* xg = nullptr;              // bf16(x · g) of the next pre-norm, [S, D]
     float* ss = nullptr;                      // partial Σ x² per token row, [D / 16][80]
 
@@ -241,13 +244,14 @@ static void dpm_coefficients(Model& m) {
     }
 }
 
-// The stage tables of the one-session path (see Model::dl). Without a
-// device that can hold the kernel's clusters, the path stays off.
+// The stage tables of the one-session paths (see Model::dl). Without a
+// device that can hold the kernel's clusters, those paths stay off.
 static int build_dense(Model& m) {
     const auto& c = m.c;
     const int D = c.hidden, S = m.S(), L = c.num_layers, A = c.action_dim;
     if (S > 80 || D % 256 != 0 || D / 64 / 4 > 8 || A % 64 != 0) return SFB_OK;
-    if (dense_clusters(device_info()) <= 0) return SFB_OK;
+    const int ncl = dense_clusters(device_info());
+    if (ncl <= 0 || c.heads * 64 != D || c.heads > ncl) return SFB_OK;
     std::vector<DenseStage> st;
     auto stage = [&](const Linear& Lw, const __nv_bfloat16* x, int TM, int act, void* y, int64_t ldy, bool y_f32,
                      const void* res, const float* ss_in, int n_ss_in, const __nv_bfloat16* g_next) {
@@ -263,37 +267,83 @@ static int build_dense(Model& m) {
     };
     const int nss = (D / 64) * 4;             // partials of an N = D stage with 64-row tiles
     int nctr = 0;
-    auto launch = [&](int first) {
-        const int n = static_cast<int>(st.size()) - first;
-        m.dl.push_back({first, n, nctr});
+    auto launch = [&](int v, int first, int n) {
+        m.dl[v].push_back({first, n, nctr});
         nctr += 1 + n;
     };
-    m.dl.clear();
-    int f = 0;
-    SFB_TRY(stage(m.blocks[0].qkv, m.xg, 128, 0, m.qkv, 3 * D, false, nullptr, m.ss, 1, nullptr));
-    launch(f);
-    for (int l = 0; l < L; ++l) {
+    auto self_attn = [&](int l) {
+        DenseStage d;
+        std::memset(&d, 0, sizeof(d));
+        SFB_TRY(dense_attn_stage_init(d, m.qkv, 3 * D, S, D, m.attn, D, m.blocks[l].qn, m.blocks[l].kn, 1e-6f,
+                                      0.125f));
+        st.push_back(d);
+        return SFB_OK;
+    };
+    auto cross_attn = [&](int l) {
+        DenseStage d;
+        std::memset(&d, 0, sizeof(d));
+        const bool lang_blk = (l % 2 == 0);
+        SFB_TRY(dense_cross_stage_init(d, m.h, D, S, D, m.kv[l], 2 * D, lang_blk ? c.max_lang_len : c.img_len,
+                                       lang_blk ? m.lang_len : nullptr, m.attn, D, m.blocks[l].cqn, 1e-6f, 0.125f));
+        st.push_back(d);
+        return SFB_OK;
+    };
+    // block l's self-attention half: qkv → self-attention → proj (+ norm2) → cross q;
+    // the proj stage pulls the block's cross K/V into L2 for the cross-attention
+    auto first_half = [&](int l) {
         const Block& bl = m.blocks[l];
-        f = static_cast<int>(st.size());
+        SFB_TRY(stage(bl.qkv, m.xg, 64, 0, m.qkv, 3 * D, false, nullptr, m.ss, l == 0 ? 1 : nss, nullptr));
+        SFB_TRY(self_attn(l));
         SFB_TRY(stage(bl.proj, m.attn, 64, 0, m.x, D, true, m.x, nullptr, 0, bl.norm2));
-        // the block's cross-attention K/V (one session) are read right after this
-        // launch: pulled into L2 while its two projections run
         st.back().l2_prefetch = reinterpret_cast<const uint8_t*>(m.kv[l]);
         st.back().l2_bytes = static_cast<uint64_t>(l % 2 == 0 ? c.max_lang_len : c.img_len) * 2 * D * 2;
         SFB_TRY(stage(bl.cq, m.xg, 64, 0, m.h, D, false, nullptr, m.ss, nss, nullptr));
-        launch(f);
-        f = static_cast<int>(st.size());
+        return SFB_OK;
+    };
+    // block l's second half: cross proj (+ norm3) → fc1 → fc2 (+ the next norm)
+    auto second_half = [&](int l) {
+        const Block& bl = m.blocks[l];
         SFB_TRY(stage(bl.cproj, m.attn, 64, 0, m.x, D, true, m.x, nullptr, 0, bl.norm3));
         SFB_TRY(stage(bl.fc1, m.xg, 64, 1, m.h, D, false, nullptr, m.ss, nss, nullptr));
         SFB_TRY(stage(bl.fc2, m.h, 64, 0, m.x, D, true, m.x, nullptr, 0,
                       l + 1 < L ? m.blocks[l + 1].norm1 : m.norm_final));
+        return SFB_OK;
+    };
+    auto final_layer = [&]() {
+        SFB_TRY(stage(m.fin1, m.xg, 64, 1, m.h, D, false, nullptr, m.ss, nss, nullptr));
+        SFB_TRY(stage(m.fin2, m.h, 64, 0, m.yfin, A, true, nullptr, nullptr, 0, nullptr));
+        return SFB_OK;
+    };
+    m.dl[0].clear();
+    m.dl[1].clear();
+    // path 0: one flat list
+    const int f0 = static_cast<int>(st.size());
+    for (int l = 0; l < L; ++l) {
+        SFB_TRY(first_half(l));
+        SFB_TRY(cross_attn(l));
+        SFB_TRY(second_half(l));
+    }
+    SFB_TRY(final_layer());
+    const int n0 = static_cast<int>(st.size()) - f0;
+    const int per = dense::kMaxStages, nl = (n0 + per - 1) / per;
+    for (int i = 0, first = f0; i < nl; ++i) {
+        const int n = (n0 - (first - f0)) / (nl - i);          // even cut
+        launch(0, first, n);
+        first += n;
+    }
+    // path 2: cross-attention kernels between launches
+    int f = static_cast<int>(st.size());
+    SFB_TRY(first_half(0));
+    launch(1, f, static_cast<int>(st.size()) - f);
+    for (int l = 0; l < L; ++l) {
+        f = static_cast<int>(st.size());
+        SFB_TRY(second_half(l));
         if (l + 1 < L) {
-            SFB_TRY(stage(m.blocks[l + 1].qkv, m.xg, 128, 0, m.qkv, 3 * D, false, nullptr, m.ss, nss, nullptr));
+            SFB_TRY(first_half(l + 1));
         } else {
-            SFB_TRY(stage(m.fin1, m.xg, 64, 1, m.h, D, false, nullptr, m.ss, nss, nullptr));
-            SFB_TRY(stage(m.fin2, m.h, 64, 0, m.yfin, A, true, nullptr, nullptr, 0, nullptr));
+            SFB_TRY(final_layer());
         }
-        launch(f);
+        launch(1, f, static_cast<int>(st.size()) - f);
     }
     SFB_TRY(dalloc(m, reinterpret_cast<void**>(&m.d_stages), st.size() * sizeof(DenseStage)));
     SFB_TRY(dalloc(m, reinterpret_cast<void**>(&m.d_ctr), static_cast<size_t>(nctr) * 8));
@@ -306,8 +356,8 @@ static int build_dense(Model& m) {
     return SFB_OK;
 }
 
-static int dense(const Model& m, int i, cudaStream_t s) {
-    const Model::DenseLaunch& d = m.dl[i];
+static int dense(const Model& m, int v, int i, cudaStream_t s) {
+    const Model::DenseLaunch& d = m.dl[v][i];
     return dense_launch(m.d_stages + d.first, d.count, m.d_ctr + d.ctr, m.S(), s, true, i);
 }
 
@@ -501,25 +551,25 @@ static int forward(Model& m, int B, float t, cudaStream_t s, int step = -1) {
     SFB_TRY(launch_kernel(rdt::assemble_x_kernel, grid_for(static_cast<int64_t>(M) * D / 8, 256), 256, 0, s, true,
         temb, m.femb, m.seq, m.x_pos, m.x, B, S, D));
 
-    if (B == 1 && m.dense_ok && m.path == 0) {
-        // one session: the projections between attentions run as stages of the
-        // persistent kernel, the pre-norms folded into them
+    if (B == 1 && m.dense_ok && m.path != 1) {
+        // one session: the projections (and on path 0 the attentions) run as
+        // stages of the persistent kernel, the pre-norms folded into them
         prefer_max_shared(rdt::norm_prep_kernel);
         SFB_TRY(launch_kernel(rdt::norm_prep_kernel, (S + 7) / 8, 256, 0, s, true,
             m.x, static_cast<int64_t>(D), m.blocks[0].norm1, m.xg, static_cast<int64_t>(D), m.ss, S, D));
-        SFB_TRY(dense(m, 0, s));
+        if (m.path == 0) {
+            for (int i = 0; i < static_cast<int>(m.dl[0].size()); ++i) SFB_TRY(dense(m, 0, i, s));
+            return SFB_OK;
+        }
+        SFB_TRY(dense(m, 1, 0, s));
         for (int l = 0; l < c.num_layers; ++l) {
             const Block& bl = m.blocks[l];
-            SFB_TRY(attention(m, m.qkv, static_cast<int64_t>(S) * 3 * D, 3 * D, m.qkv + D, m.qkv + 2 * D,
-                              static_cast<int64_t>(S) * 3 * D, 3 * D, m.attn, B, S, S, nullptr, false,
-                              bl.qn, bl.kn, s));
-            SFB_TRY(dense(m, 1 + 2 * l, s));
             const bool lang_blk = (l % 2 == 0);
             const int Lk = lang_blk ? c.max_lang_len : c.img_len;
             SFB_TRY(attention(m, m.h, static_cast<int64_t>(S) * D, D, m.kv[l], m.kv[l] + D,
                               static_cast<int64_t>(Lk) * 2 * D, 2 * D, m.attn, B, S, Lk,
                               lang_blk ? m.lang_len : nullptr, true, bl.cqn, nullptr, s));
-            SFB_TRY(dense(m, 2 + 2 * l, s));
+            SFB_TRY(dense(m, 1, 1 + l, s));
         }
         return SFB_OK;
     }
@@ -601,7 +651,7 @@ int sfb_rdt1b_create(const sfb_rdt1b_config* cfg, uint64_t seed, void** handle) 
     m->seed = seed;
     // SFB_RDT1B_PATH=1 selects the per-projection kernels at one session by
     // default (sfb_rdt1b_set_path changes it per handle)
-    if (const char* e = std::getenv("SFB_RDT1B_PATH")) m->path = std::strcmp(e, "1") == 0 ? 1 : 0;
+    if (const char* e = std::getenv("SFB_RDT1B_PATH")) m->path = (e[0] >= '0' && e[0] <= '2' && e[1] == 0) ? e[0] - '0' : 0;
     cudaGetDevice(&m->device);
     const int rc = rdt::create(*m);
     if (rc != SFB_OK) {
@@ -803,7 +853,7 @@ int sfb_rdt1b_tick_stats(void* handle, int64_t* ticks, int64_t* encodes) {
 
 int sfb_rdt1b_set_path(void* handle, int32_t path) {
     auto* m = static_cast<rdt::Model*>(handle);
-    if (m == nullptr || path < 0 || path > 1) return SFB_ERR_INVALID;
+    if (m == nullptr || path < 0 || path > 2) return SFB_ERR_INVALID;
     SFB_MODEL_ENTRY(m);
     if (path != m->path) {
         // captured graphs hold the other path's kernels

@@ -132,8 +132,10 @@ class RDT1B:
         return t.value, e.value
 
     def set_path(self, path: int) -> None:
-        """One-session execution path: 0 persistent projection kernel (default),
-        1 one kernel per projection and norm (sfb_rdt1b_set_path)."""
+        """One-session execution path (sfb_rdt1b_set_path): 0 the persistent
+        kernel runs every projection and attention as stages (default), 1 one
+        kernel per projection, norm and attention, 2 the persistent kernel
+        between cross-attention kernels."""
         _capi.check(self.lib.sfb_rdt1b_set_path(self.h, int(path)), "set_path")
 
     def graph_kernels(self, sessions: int = 1) -> int:

@@ -170,13 +170,14 @@ def one(gpu):
 
 
 def test_one_session_paths_match_oracle(one):
-    """Path 0 (persistent projection kernel, norms folded in) and path 1 (one
-    kernel per projection) both meet the bar against the oracle, and agree
-    with each other."""
+    """Path 0 (persistent kernel: projections, self- and cross-attention as
+    stages, norms folded in), path 1 (one kernel per projection) and path 2
+    (persistent kernel between cross-attention kernels) all meet the bar
+    against the oracle, and agree with each other."""
     s = one
     noise = s["noise"].to(s["dev"])
     outs = []
-    for path in (0, 1):
+    for path in (0, 1, 2):
         s["model"].set_path(path)
         y = torch.empty_like(noise)
         s["model"].forward(noise, 999.0, y)
@@ -188,8 +189,9 @@ def test_one_session_paths_match_oracle(one):
         max_abs, cos = close(y, ref)
         print(f"[parity] one session, path {path}: max |d| {max_abs:.3e}, cos {cos:.7f}")
         assert max_abs < 0.05 and cos > 0.9999, (path, max_abs, cos)
-    max_abs, cos = close(outs[0], outs[1].cpu())
-    assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
+    for y in outs[1:]:
+        max_abs, cos = close(outs[0], y.cpu())
+        assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
 
 
 def test_one_session_graph_replays_are_identical(one):
