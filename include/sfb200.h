@@ -319,6 +319,16 @@ int sfb_rdt1b_tick_stats(void* handle, int64_t* ticks, int64_t* encodes);
  * bit for bit. Changing it drops the captured graphs. No counterpart in the
  * reference. */
 int sfb_rdt1b_set_path(void* handle, int32_t path);
+/* Profiles one network evaluation of session 0 at timestep t on the
+ * persistent-kernel path (path 0, whatever the handle's path): CUDA events
+ * around each of its launches on `stream`. Writes the launch count to
+ * *n_launches and, when max_launches is large enough, each launch's
+ * algorithmic bytes (weights, scales and biases read, activations read and
+ * written, the K/V rows the cross-attention reads: the language blocks' valid
+ * keys only) and its duration in microseconds. Synchronises `stream`.
+ * Diagnostic; no counterpart in the reference. */
+int sfb_rdt1b_profile_dense(void* handle, float t, int32_t max_launches, int32_t* n_launches,
+                            double* alg_bytes, float* us, void* stream);
 /* Kernel launches in the captured sampling graph for `sessions` (known after
  * the first use_graph call for that session count). Diagnostic; no
  * counterpart in the reference. */

@@ -152,6 +152,12 @@ struct Model {
     DenseStage* d_stages = nullptr;           // device copy of the stage tables
     unsigned long long* d_ctr = nullptr;      // completion counters, 1 + count per launch
     std::vector<DenseLaunch> dl[2];
+    // algorithmic bytes of each stage of dl[0] (the language cross-attention
+    // stages without their K/V, which depend on the valid length), and which
+    // stages those are; events around each dense launch while profiling
+    std::vector<double> stage_bytes;
+    std::vector<char> stage_lang_kv;
+    std::vector<cudaEvent_t>* prof = nullptr;
     __nv_bfloat16* xg = nullptr;              // bf16(x · g) of the next pre-norm, [S, D]
     float* ss = nullptr;                      // partial Σ x² per token row, [D / 16][80]
 
@@ -253,6 +259,8 @@ static int build_dense(Model& m) {
     const int ncl = dense_clusters(device_info());
     if (ncl <= 0 || c.heads * 64 != D || c.heads > ncl) return SFB_OK;
     std::vector<DenseStage> st;
+    std::vector<double> bytes;
+    std::vector<char> lang_kv;
     auto stage = [&](const Linear& Lw, const __nv_bfloat16* x, int TM, int act, void* y, int64_t ldy, bool y_f32,
                      const void* res, const float* ss_in, int n_ss_in, const __nv_bfloat16* g_next) {
         DenseStage d;
@@ -263,6 +271,13 @@ static int build_dense(Model& m) {
         d.ss_in = ss_in; d.n_ss_in = n_ss_in; d.eps = 1e-6f;
         if (g_next != nullptr) { d.g_next = g_next; d.xg = m.xg; d.ldg = D; d.ss_out = m.ss; }
         st.push_back(d);
+        const double ysz = y_f32 ? 4.0 : 2.0, MN = static_cast<double>(S) * Lw.N;
+        double b = static_cast<double>(Lw.N) * Lw.K + Lw.N * 6.0 + 2.0 * S * Lw.K + MN * ysz;
+        if (res != nullptr) b += MN * ysz;
+        if (g_next != nullptr) b += 2.0 * MN + 2.0 * Lw.N + (Lw.N / 64) * 4 * 80 * 4.0;
+        if (ss_in != nullptr) b += n_ss_in * 80 * 4.0;
+        bytes.push_back(b);
+        lang_kv.push_back(0);
         return SFB_OK;
     };
     const int nss = (D / 64) * 4;             // partials of an N = D stage with 64-row tiles
@@ -277,6 +292,8 @@ static int build_dense(Model& m) {
         SFB_TRY(dense_attn_stage_init(d, m.qkv, 3 * D, S, D, m.attn, D, m.blocks[l].qn, m.blocks[l].kn, 1e-6f,
                                       0.125f));
         st.push_back(d);
+        bytes.push_back(4.0 * S * D * 2 + 4 * 64 * 2.0);
+        lang_kv.push_back(0);
         return SFB_OK;
     };
     auto cross_attn = [&](int l) {
@@ -286,6 +303,9 @@ static int build_dense(Model& m) {
         SFB_TRY(dense_cross_stage_init(d, m.h, D, S, D, m.kv[l], 2 * D, lang_blk ? c.max_lang_len : c.img_len,
                                        lang_blk ? m.lang_len : nullptr, m.attn, D, m.blocks[l].cqn, 1e-6f, 0.125f));
         st.push_back(d);
+        // Q, out, and (image blocks) the whole K/V cache
+        bytes.push_back(2.0 * S * D * 2 + 64 * 2.0 + (lang_blk ? 0.0 : 2.0 * c.img_len * D * 2));
+        lang_kv.push_back(lang_blk ? 1 : 0);
         return SFB_OK;
     };
     // block l's self-attention half: qkv → self-attention → proj (+ norm2) → cross q;
@@ -352,6 +372,8 @@ static int build_dense(Model& m) {
         record_cuda_error(cudaGetLastError(), "dense stage table");
         return SFB_ERR_CUDA;
     }
+    m.stage_bytes = bytes;
+    m.stage_lang_kv = lang_kv;
     m.dense_ok = true;
     return SFB_OK;
 }
@@ -558,7 +580,12 @@ static int forward(Model& m, int B, float t, cudaStream_t s, int step = -1) {
         SFB_TRY(launch_kernel(rdt::norm_prep_kernel, (S + 7) / 8, 256, 0, s, true,
             m.x, static_cast<int64_t>(D), m.blocks[0].norm1, m.xg, static_cast<int64_t>(D), m.ss, S, D));
         if (m.path == 0) {
-            for (int i = 0; i < static_cast<int>(m.dl[0].size()); ++i) SFB_TRY(dense(m, 0, i, s));
+            const int n = static_cast<int>(m.dl[0].size());
+            for (int i = 0; i < n; ++i) {
+                if (m.prof != nullptr) cudaEventRecord((*m.prof)[i], s);
+                SFB_TRY(dense(m, 0, i, s));
+            }
+            if (m.prof != nullptr) cudaEventRecord((*m.prof)[n], s);
             return SFB_OK;
         }
         SFB_TRY(dense(m, 1, 0, s));
@@ -888,6 +915,53 @@ int sfb_rdt1b_graph_kernels(void* handle, int32_t sessions, int64_t* kernels) {
     if (it == m->graph_kernels.end()) return SFB_ERR_INVALID;
     *kernels = it->second;
     return SFB_OK;
+}
+
+int sfb_rdt1b_profile_dense(void* handle, float t, int32_t max_launches, int32_t* n_launches,
+                            double* alg_bytes, float* us, void* stream) {
+    auto* m = static_cast<rdt::Model*>(handle);
+    if (m == nullptr || n_launches == nullptr) return SFB_ERR_INVALID;
+    SFB_MODEL_ENTRY(m);
+    if (!m->dense_ok) return SFB_ERR_UNSUPPORTED;
+    const int n = static_cast<int>(m->dl[0].size());
+    *n_launches = n;
+    if (max_launches < n || alg_bytes == nullptr || us == nullptr) return SFB_ERR_SHAPE;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // valid language keys of session 0 (the language cross-attention reads only those)
+    int32_t lang_len = 0;
+    if (cudaMemcpyAsync(&lang_len, m->lang_len, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        record_cuda_error(cudaGetLastError(), "rdt1b profile");
+        return SFB_ERR_CUDA;
+    }
+    lang_len = std::max(0, std::min(lang_len, m->c.max_lang_len));
+    std::vector<cudaEvent_t> ev(n + 1, nullptr);
+    int rc = SFB_OK;
+    for (auto& e : ev)
+        if (cudaEventCreate(&e) != cudaSuccess) rc = SFB_ERR_CUDA;
+    const int path = m->path;
+    if (rc == SFB_OK) {
+        m->path = 0;
+        m->prof = &ev;
+        rc = rdt::forward(*m, 1, t, s);
+        m->prof = nullptr;
+        m->path = path;
+        if (rc == SFB_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = SFB_ERR_CUDA;
+    }
+    for (int i = 0; rc == SFB_OK && i < n; ++i) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, ev[i], ev[i + 1]) != cudaSuccess) { rc = SFB_ERR_CUDA; break; }
+        us[i] = ms * 1e3f;
+        const auto& d = m->dl[0][i];
+        double b = 0.0;
+        for (int k = d.first; k < d.first + d.count; ++k)
+            b += m->stage_bytes[k] + (m->stage_lang_kv[k] ? 2.0 * lang_len * m->c.hidden * 2 : 0.0);
+        alg_bytes[i] = b;
+    }
+    for (auto& e : ev)
+        if (e != nullptr) cudaEventDestroy(e);
+    if (rc == SFB_ERR_CUDA) record_cuda_error(cudaGetLastError(), "rdt1b profile");
+    return rc;
 }
 
 int sfb_rdt1b_schedule(void* handle, float* timesteps, float* coef_a, float* coef_b, float* coef_c,

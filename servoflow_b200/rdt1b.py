@@ -37,6 +37,8 @@ def _declare(lib):
                                        c.c_int32]
     lib.sfb_rdt1b_graph_kernels.argtypes = [c.c_void_p, c.c_int32, c.POINTER(c.c_int64)]
     lib.sfb_rdt1b_set_path.argtypes = [c.c_void_p, c.c_int32]
+    lib.sfb_rdt1b_profile_dense.argtypes = [c.c_void_p, c.c_float, c.c_int32, c.POINTER(c.c_int32),
+                                            c.POINTER(c.c_double), c.POINTER(c.c_float), c.c_void_p]
     lib.sfb_rdt1b_tick.argtypes = [c.c_void_p, c.c_int32, c.c_uint64, c.c_void_p, c.c_void_p, c.c_void_p,
                                    c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p]
     lib.sfb_rdt1b_invalidate_condition.argtypes = [c.c_void_p]
@@ -137,6 +139,22 @@ class RDT1B:
         kernel per projection, norm and attention, 2 the persistent kernel
         between cross-attention kernels."""
         _capi.check(self.lib.sfb_rdt1b_set_path(self.h, int(path)), "set_path")
+
+    def profile_dense(self, t: float = 999.0):
+        """[(algorithmic bytes, microseconds)] of each persistent-kernel launch of
+        one session-0 network evaluation at timestep t (sfb_rdt1b_profile_dense;
+        synchronises the current stream)."""
+        import torch
+        n = ctypes.c_int32()
+        stream = torch.cuda.current_stream().cuda_stream
+        rc = self.lib.sfb_rdt1b_profile_dense(self.h, float(t), 0, ctypes.byref(n), None, None, stream)
+        if rc not in (0, _capi.SFB_ERR_SHAPE):
+            _capi.check(rc, "profile_dense")
+        b = (ctypes.c_double * n.value)()
+        us = (ctypes.c_float * n.value)()
+        _capi.check(self.lib.sfb_rdt1b_profile_dense(self.h, float(t), n.value, ctypes.byref(n), b, us, stream),
+                    "profile_dense")
+        return list(zip(b, us))
 
     def graph_kernels(self, sessions: int = 1) -> int:
         """Kernel launches in the captured sampling graph for `sessions`."""

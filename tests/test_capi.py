@@ -128,3 +128,5 @@ def test_model_api_argument_checks_without_a_gpu():
     n = ctypes.c_int64()
     assert lib.sfb_rdt1b_graph_kernels(None, 1, ctypes.byref(n)) == _capi.SFB_ERR_INVALID
     assert lib.sfb_rdt1b_schedule(None, None, None, None, None, 5) == _capi.SFB_ERR_INVALID
+    n32 = ctypes.c_int32()
+    assert lib.sfb_rdt1b_profile_dense(None, 999.0, 0, ctypes.byref(n32), None, None, None) == _capi.SFB_ERR_INVALID
