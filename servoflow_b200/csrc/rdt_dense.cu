@@ -187,7 +187,8 @@ constexpr int kBarCQ = kBarARcv + 1;                          // cross-attention
 constexpr int kBarCS = kBarCQ + 1;                            // [2]: S of TMEM buffer b
 constexpr int kBarCP = kBarCS + 2;                            // P written
 constexpr int kBarCO = kBarCP + 1;                            // O += P·V done
-constexpr int kNumBars = kBarCO + 1;
+constexpr int kBarDrain2 = kBarCO + 1;                        // the activation warp's MMAs after a failure
+constexpr int kNumBars = kBarDrain2 + 1;
 // TMEM columns: projection accumulators [0, 256); self-attention S [256, 336),
 // P (fp16 pairs) [336, 384), O [384, 448); cross-attention S buffers at 0
 // and 128 (the accumulators' columns: no projection runs in that stage), P
@@ -196,7 +197,17 @@ constexpr int kNumBars = kBarCO + 1;
 // at 0, then two K/V stages of [128 keys × 64] K (bf16) and V (fp16)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 256, kColP = 336, kColO = 384;
-constexpr uint32_t kColCrossP = 256;                          // cross-attention P buffers [256, 384)
+constexpr uint32_t kColCrossP = 256;
+// A projection unit's MMAs are issued by kIssuers warps (the MMA warp and the
+// activation warp, which is idle once its loads are out): warp w takes the
+// K chunks c with c % kIssuers == w into its own TMEM accumulator (chain w).
+// One thread's tcgen05.mma issue takes ~165 cycles whatever the shape, so a
+// unit's 32 small MMAs (64 × 80 × 16) from one warp cost ~2.9 µs; issue from
+// several warps overlaps. The epilogue adds the chains. Unit buffer b's chain
+// w sits at TMEM column b · kAccBufCols + w · kBN.
+constexpr int kIssuers = 2;
+constexpr uint32_t kAccBufCols = 256;
+static_assert(kIssuers * 80 <= static_cast<int>(kAccBufCols) && 2 * kAccBufCols <= 512, "accumulator columns");                          // cross-attention P buffers [256, 384)
 constexpr int kQKVBytes = 128 * 128;                          // one [128 × 64] bf16 tile, SW128
 constexpr int kOffKV = kOffX + kQKVBytes;                     // stage st: K at + st · 2 tiles, V after it
 static_assert(kOffKV + 4 * kQKVBytes <= kOffWB, "cross-attention tiles fit the activation area");
@@ -646,9 +657,12 @@ __device__ __forceinline__ void cross_attention_epilogue(const StageInfo& S, uin
 // per launch slot: [CTA < 160][stage < 16, then 16 = setup][8] global-timer stamps
 constexpr int kTrStages = kMaxStages + 1;                     // + the launch slot
 #define DN_T(st, k) do { if (trace != nullptr && blockIdx.x < 160 && (st) < kTrStages) \
-        trace[(blockIdx.x * kTrStages + (st)) * 16 + (k)] = ptx::global_timer_ns(); } while (0)
+        trace[(blockIdx.x * kTrStages + (st)) * 40 + (k)] = ptx::global_timer_ns(); } while (0)
+#define DN_C(st, k) do { if (trace != nullptr && blockIdx.x < 160 && (st) < kTrStages) \
+        trace[(blockIdx.x * kTrStages + (st)) * 40 + (k)] = clock64(); } while (0)
 #else
 #define DN_T(st, k) do { } while (0)
+#define DN_C(st, k) do { } while (0)
 #endif
 
 __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages, int nst,
@@ -683,10 +697,11 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         for (int i = 0; i < kNB; ++i) { mbar_init(&bars[kBarBFull + i], 4); mbar_init(&bars[kBarBFree + i], 1); }
         for (int i = 0; i < kNX; ++i) mbar_init(&bars[kBarXFull + i], 1);
         mbar_init(&bars[kBarDep], 1);
-        for (int i = 0; i < 2; ++i) { mbar_init(&bars[kBarAccFull + i], 1); mbar_init(&bars[kBarAccFree + i], 4); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&bars[kBarAccFull + i], kIssuers); mbar_init(&bars[kBarAccFree + i], 4); }
         mbar_init(&bars[kBarRcv], 1);                       // armed by the owner (expect_tx), filled by st.async
         for (int i = 0; i < kSplit; ++i) mbar_init(&bars[kBarRcvFree + i], 4);   // the owner's 4 warps
         mbar_init(&bars[kBarDrain], 1);
+        mbar_init(&bars[kBarDrain2], 1);
         mbar_init(&bars[kBarQK], 4);
         mbar_init(&bars[kBarS], 1);
         mbar_init(&bars[kBarP], 4);
@@ -725,6 +740,42 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
     const bool spin = spin_role(threadIdx.x >> 5);
     auto wait = [&](int b, uint32_t parity) {
         if (!dwait(&bars[b], parity, ok ? kWaitNs : 0ull, spin)) ok = false;
+    };
+
+    // Issuer w's share of projection unit j of stage s (see kIssuers): its K
+    // chunks into chain w of accumulator buffer um & 1, each chunk's weight
+    // slot released when its MMAs complete, the buffer's full barrier
+    // committed after the last (or at once when the unit has no chunk for w).
+    auto issue_unit = [&](const StageInfo& S, int s, int j, int nk, uint32_t um, uint32_t gm, uint32_t xm, int w) {
+        const int buf = um & 1;
+        if (um >= 2) wait(kBarAccFree + buf, ((um >> 1) - 1) & 1);
+        const uint32_t tacc = tmem + buf * kAccBufCols + static_cast<uint32_t>(w) * kBN;
+        const uint32_t idesc = idesc_f16(static_cast<uint32_t>(S.TM), kBN, 1, 0, 0);
+        int last = -1;
+        for (int c = w; c < nk; c += kIssuers) last = c;
+        for (int c = w; c < nk && ok; c += kIssuers) {
+            const uint32_t g = gm + static_cast<uint32_t>(c);
+            const int bs = g % kNB;
+            wait(kBarBFull + bs, (g / kNB) & 1);
+            wait(kBarXFull + c, (xm >> c) & 1u);
+            if (!ok) break;
+            tc_fence_after_sync();
+            if (w == 0 && j == 0 && (c == 0 || c == last) && lane == 0) DN_T(s, c == 0 ? 8 : 9);
+            const uint32_t aw = smem_u32(sWB(bs)), ax = smem_u32(sX(c));
+            if (elect_one()) {
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16_ss(tacc, smem_desc_sw128(aw + kk * 32, 16, 1024), smem_desc_sw128(ax + kk * 32, 16, 1024),
+                               idesc, (c > w || kk > 0) ? 1u : 0u);
+                mma_commit(&bars[kBarBFree + bs]);
+                if (c == last) mma_commit(&bars[kBarAccFull + buf]);
+            }
+            __syncwarp();
+        }
+        if (last < 0) {
+            if (elect_one()) mma_commit(&bars[kBarAccFull + buf]);
+            __syncwarp();
+        }
     };
 
     if (warp == kWarpW) {
@@ -786,6 +837,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         // xmask bit c: parity of the next completion of activation slot c
         // (stages may load different numbers of chunks)
         uint32_t xmask = 0, last_mask = 0, gkv = 0;        // gkv: cross-attention key tiles issued
+        uint32_t um2 = 0, gm2 = 0;                         // projection units / chunks, as the MMA warp's
         int loaded = 0;                                    // chunks of the last load issued
         pdl_wait();                                        // everything earlier kernels wrote
         for (int s = 0; s < nst; ++s) {
@@ -866,6 +918,9 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 last_mask = xmask;
                 loaded = nk;
                 xmask ^= (nk >= 32 ? 0xffffffffu : ((1u << nk) - 1u));
+                // then this warp's share of the stage's MMAs
+                const int nu = units_of(S, cl, ncl);
+                for (int j = 0; j < nu && ok; ++j, ++um2, gm2 += nk) issue_unit(S, s, j, nk, um2, gm2, last_mask, 1);
             }
         }
         // the last loads land before the CTA leaves (bounded; immediate on the normal path)
@@ -874,6 +929,12 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         for (uint32_t g = gkv > 2 ? gkv - 2 : 0; g < gkv; ++g)
             for (int t = 0; t < 2; ++t)
                 if (!mbar_wait(&bars[kBarKV + 2 * (g & 1) + t], (g >> 1) & 1, kDrainNs)) ok = false;
+        if (!ok) {
+            // this warp's MMAs in flight complete before the TMEM is freed
+            if (elect_one()) mma_commit(&bars[kBarDrain2]);
+            __syncwarp();
+            mbar_wait(&bars[kBarDrain2], 0, kDrainNs);
+        }
     } else if (warp == kWarpMma) {
         // ── MMA issuer ──────────────────────────────────────────────────────
         uint32_t gm = 0, um = 0, xmask = 0, au = 0;        // xmask as the activation loader's
@@ -972,33 +1033,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
             const int nu = units_of(S, cl, ncl);
             if (nu == 0) continue;
             const int nk = S.K / 64 / kSplit;
-            const uint32_t idesc = idesc_f16(static_cast<uint32_t>(S.TM), kBN, 1, 0, 0);
-            for (int j = 0; j < nu && ok; ++j, ++um) {
-                const int buf = um & 1;
-                if (um >= 2) wait(kBarAccFree + buf, ((um >> 1) - 1) & 1);
-                const uint32_t tacc = tmem + buf * 128;
-                for (int c = 0; c < nk && ok; ++c, ++gm) {
-                    const int bs = gm % kNB;
-                    wait(kBarBFull + bs, (gm / kNB) & 1);
-                    if (j == 0 && c == nk - 1 && lane == 0) DN_T(s, 15);
-                    wait(kBarXFull + c, (xmask >> c) & 1u);
-                    if (j == 0 && c == nk / 2 && lane == 0) DN_T(s, 14);
-                    if (!ok) break;
-                    tc_fence_after_sync();
-                    if (j == 0 && (c == 0 || c == nk - 1) && lane == 0) DN_T(s, c == 0 ? 8 : 9);
-                    const uint32_t aw = smem_u32(sWB(bs)), ax = smem_u32(sX(c));
-                    if (elect_one()) {
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_f16_ss(tacc, smem_desc_sw128(aw + kk * 32, 16, 1024),
-                                       smem_desc_sw128(ax + kk * 32, 16, 1024), idesc,
-                                       (c > 0 || kk > 0) ? 1u : 0u);
-                        mma_commit(&bars[kBarBFree + bs]);
-                        if (c == nk - 1) mma_commit(&bars[kBarAccFull + buf]);
-                    }
-                    __syncwarp();
-                }
-            }
+            for (int j = 0; j < nu && ok; ++j, ++um, gm += nk) issue_unit(S, s, j, nk, um, gm, xmask, 0);
             xmask ^= (nk >= 32 ? 0xffffffffu : ((1u << nk) - 1u));
         }
         if (!ok) {
@@ -1044,6 +1079,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                     __syncwarp();
                     if (lane == 0) { mbar_arrive(&bars[kBarWFree + ws]); mbar_arrive(&bars[kBarBFull + bs]); }
                     if (ct == 0 && j == 0 && c == nk - 1) DN_T(s, 11);
+                    if (lane == 0 && j == 0 && c < 8) DN_T(s, 32 + c);
                 }
             }
         }
@@ -1096,30 +1132,73 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
             for (int j = 0; j < nu; ++j, ++ue) {
                 const int n0 = (cl + j * ncl) * TM;
                 const int nb = n0 + rank * RPW;            // first channel this CTA owns
-                // (1) the stage's dependency (once per stage); rows' RMS factors
+                // (0) the unit's constants (weights' scales, bias, next norm's weight):
+                // independent of the stage's dependency, so loaded before waiting for it.
+                // Every global load below lands in the register it is used from, raw,
+                // so that nothing waits for it before its first use.
+                const bool lane_ok = lane < RPW;
+                const int trow = q * RPW + lane;               // tile row (owner q, slot lane)
+                float sc = 0.f;
+                if (lane_ok && n0 + trow < S.N)
+                    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(sc) : "l"(S.w_scale + n0 + trow));
+                uint4 rbias[kMaxIt], rg[kMaxIt], rr[kMaxIt][2];
+#pragma unroll
+                for (int it = 0; it < kMaxIt; ++it) {
+                    const int u = et + it * kEpiThreads;
+                    const int m = u < units ? u / segs : 0, n = nb + (u < units ? (u - m * segs) * 8 : 0);
+                    const bool use = u < units && n < S.N;
+                    rbias[it] = make_uint4(0u, 0u, 0u, 0u);
+                    rg[it] = make_uint4(0u, 0u, 0u, 0u);
+                    if (use && S.bias != nullptr) rbias[it] = ld_nc_u4(S.bias + n);
+                    if (use && S.g_next != nullptr) rg[it] = ld_nc_u4(S.g_next + n);
+                }
+                // (1) the stage's dependency (once per stage)
                 if (j == 0) {
                     wait(kBarDep, xs & 1);
+                    if (et == 0) { DN_T(s, 16); DN_C(s, 20); }
+                }
+                // (2) the residual rows this thread's owner pass adds (written by earlier stages)
+#pragma unroll
+                for (int it = 0; it < kMaxIt; ++it) {
+                    const int u = et + it * kEpiThreads;
+                    const int m = u < units ? u / segs : 0, n = nb + (u < units ? (u - m * segs) * 8 : 0);
+                    const bool use = u < units && n < S.N;
+                    rr[it][0] = make_uint4(0u, 0u, 0u, 0u);
+                    rr[it][1] = make_uint4(0u, 0u, 0u, 0u);
+                    if (use && S.residual != nullptr) {
+                        if (S.y_f32) {
+                            const float* rp = static_cast<const float*>(S.residual) + m * S.ldr + n;
+                            rr[it][0] = ld_cg_u4(rp);
+                            rr[it][1] = ld_cg_u4(rp + 4);
+                        } else {
+                            rr[it][0] = ld_cg_u4(static_cast<const __nv_bfloat16*>(S.residual) + m * S.ldr + n);
+                        }
+                    }
+                }
+                // (1b) rows' RMS factors from the producing stage's partial sums (once per stage)
+                if (j == 0) {
                     if (S.ss_in != nullptr) {
                         // Thread t < 120 sums the float4 column t % 20 (token rows
                         // 4·(t % 20) .. +3) over partials group t / 20 (six groups of
-                        // consecutive partials): up to 11 independent 16-byte loads in
+                        // consecutive partials): up to 22 independent 16-byte loads in
                         // flight per thread instead of a chain of dependent ones. The
                         // six group sums are then added in group order.
                         constexpr int kCols = kBN / 4, kGroups = kEpiThreads / kCols;   // 20, 6
+                        constexpr int kBatch = 22;          // loads in flight: a group's partials at once (128 / 6)
                         const int np = S.n_ss_in;
                         const int col = et % kCols, grpi = et / kCols;
                         const int per = (np + kGroups - 1) / kGroups;
                         const int p0 = grpi * per, p1 = min(np, p0 + per);
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                         if (grpi < kGroups) {
-                            for (int pb = p0; pb < p1; pb += 11) {
-                                float4 t[11];
+                            for (int pb = p0; pb < p1; pb += kBatch) {
+                                float4 t[kBatch];
 #pragma unroll
-                                for (int i = 0; i < 11; ++i)
+                                for (int i = 0; i < kBatch; ++i)
                                     t[i] = pb + i < p1 ? ld_cg_f4(S.ss_in + (pb + i) * kBN + 4 * col)
                                                        : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                                for (int i = 0; i < 11; ++i) {
+                                for (int i = 0; i < kBatch; ++i) {
                                     acc.x += t[i].x; acc.y += t[i].y; acc.z += t[i].z; acc.w += t[i].w;
                                 }
                             }
@@ -1135,41 +1214,12 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                     }
                     named_bar_sync(1, kEpiThreads);
                 }
-                // (2) this thread's owner-pass operands, loaded while the MMAs run
-                float rres[kMaxIt][8];
-                uint4 rbias[kMaxIt], rg[kMaxIt];
-#pragma unroll
-                for (int it = 0; it < kMaxIt; ++it) {
-                    const int u = et + it * kEpiThreads;
-                    const int m = u < units ? u / segs : 0, n = nb + (u < units ? (u - m * segs) * 8 : 0);
-                    const bool use = u < units && n < S.N;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) rres[it][k] = 0.f;
-                    rbias[it] = make_uint4(0u, 0u, 0u, 0u);
-                    rg[it] = make_uint4(0u, 0u, 0u, 0u);
-                    if (use && S.residual != nullptr) {
-                        if (S.y_f32) {
-                            const float* rp = static_cast<const float*>(S.residual) + m * S.ldr + n;
-                            const float4 a = ld_cg_f4(rp), b = ld_cg_f4(rp + 4);
-                            rres[it][0] = a.x; rres[it][1] = a.y; rres[it][2] = a.z; rres[it][3] = a.w;
-                            rres[it][4] = b.x; rres[it][5] = b.y; rres[it][6] = b.z; rres[it][7] = b.w;
-                        } else {
-                            const uint4 ru = ld_cg_u4(static_cast<const __nv_bfloat16*>(S.residual) + m * S.ldr + n);
-                            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) { const float2 f = __bfloat1622float2(r2[k]); rres[it][2 * k] = f.x; rres[it][2 * k + 1] = f.y; }
-                        }
-                    }
-                    if (use && S.bias != nullptr) rbias[it] = ld_nc_u4(S.bias + n);
-                    if (use && S.g_next != nullptr) rg[it] = ld_nc_u4(S.g_next + n);
-                }
+                if (et == 0 && j == 0) { DN_T(s, 17); DN_C(s, 21); }
+                if (et == 0 && j == 0) DN_T(s, 18);
                 // (3) accumulator → scaled partials into the owner's receive area
+                static_assert(kIssuers == 2, "the epilogue adds two chains");
+                const int nk_unit = S.K / 64 / kSplit;
                 const int buf = ue & 1;
-                const bool lane_ok = lane < RPW;
-                const int trow = q * RPW + lane;               // tile row (owner q, slot lane)
-                float sc = 0.f;
-                if (lane_ok && n0 + trow < S.N)
-                    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(sc) : "l"(S.w_scale + n0 + trow));
                 // arm this CTA's receive barrier for the unit: the four sources' partials
                 // of its RPW rows (this thread has passed the previous unit's phase)
                 if (et == 0)
@@ -1180,9 +1230,9 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 }
                 if (et == 0 && j == 0) DN_T(s, 10);
                 wait(kBarAccFull + buf, (ue >> 1) & 1);
-                if (et == 0 && j == 0) DN_T(s, 1);
+                if (et == 0 && j == 0) { DN_T(s, 1); DN_C(s, 22); }
                 tc_fence_after_sync();
-                const uint32_t tq = tmem + buf * 128 + (static_cast<uint32_t>(q * 32) << 16);
+                const uint32_t tq = tmem + buf * kAccBufCols + (static_cast<uint32_t>(q * 32) << 16);
                 const uint32_t base = dsmem_map(smem_u32(rcv + (rank * RPW + (lane_ok ? lane : 0)) * kBN),
                                                 static_cast<uint32_t>(q));
                 const uint32_t rbar = dsmem_map(smem_u32(&bars[kBarRcv]), static_cast<uint32_t>(q));
@@ -1190,6 +1240,13 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 for (int blk = 0; blk < 3; ++blk) {                 // 32 token columns at a time
                     float v[32];
                     tmem_ld32(tq + 32 * blk, v);
+                    if (nk_unit > 1) {                     // chain 1 (kIssuers == 2)
+                        float w[32];
+                        tmem_ld32(tq + kBN + 32 * blk, w);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] += w[i];
+                    }
                     tmem_ld_wait();
                     if (lane_ok) {
 #pragma unroll
@@ -1203,10 +1260,10 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 tc_fence_before_sync();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars[kBarAccFree + buf]);
-                if (et == 0 && j == nu - 1) DN_T(s, 4);
+                if (et == 0 && j == nu - 1) { DN_T(s, 4); DN_C(s, 23); }
                 // (4) owner pass: rows [nb, nb + RPW) of the tile, every token
                 if (!cwait(&bars[kBarRcv], ue & 1, ok ? kWaitNs : 0ull)) ok = false;
-                if (et == 0 && j == nu - 1) DN_T(s, 5);
+                if (et == 0 && j == nu - 1) { DN_T(s, 5); DN_C(s, 24); }
                 // sums of the four sources first, so the area is released before any
                 // global store of this pass
                 float ysum[kMaxIt][8];
@@ -1224,10 +1281,10 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                         }
                     }
                 }
-                if (et == 0 && j == nu - 1) DN_T(s, 13);
+                if (et == 0 && j == nu - 1) { DN_T(s, 13); DN_C(s, 25); }
                 __syncwarp();
                 if (lane < kSplit) mbar_arrive_remote(&bars[kBarRcvFree + rank], static_cast<uint32_t>(lane));
-                if (et == 0 && j == nu - 1) DN_T(s, 6);
+                if (et == 0 && j == nu - 1) { DN_T(s, 6); DN_C(s, 26); }
 #pragma unroll
                 for (int it = 0; it < kMaxIt; ++it) {
                     const int u = et + it * kEpiThreads;
@@ -1239,6 +1296,21 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                     float sq = 0.f;
                     if (valid && n < S.N) {
                         const float* yv = ysum[it];
+                        float rres[8];
+                        if (S.y_f32) {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                rres[k] = __uint_as_float((&rr[it][0].x)[k]);
+                                rres[4 + k] = __uint_as_float((&rr[it][1].x)[k]);
+                            }
+                        } else {
+                            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr[it][0]);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const float2 f = __bfloat1622float2(r2[k]);
+                                rres[2 * k] = f.x; rres[2 * k + 1] = f.y;
+                            }
+                        }
                         const float r = S.ss_in != nullptr ? rinv[m] : 1.f;
                         const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&rbias[it]);
 #pragma unroll
@@ -1249,7 +1321,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                                 float t = fmaf(yv[2 * k + h], r, h ? bb.y : bb.x);
                                 if (S.act == 1) t = gelu_tanh(t);
                                 else if (S.act == 2) t = t / (1.f + expf(-t));
-                                outv[2 * k + h] = t + rres[it][2 * k + h];
+                                outv[2 * k + h] = t + rres[2 * k + h];
                             }
                         }
                         if (S.y_f32) {
@@ -1289,16 +1361,16 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 }
             }
             if (nu > 0) ++xs;
-            if (et == 0) DN_T(s, 7);
+            if (et == 0) { DN_T(s, 7); DN_C(s, 27); }
             // (5) this CTA is done with stage s: publish its writes, bump the counter
             named_bar_sync(1, kEpiThreads);
             if (et == 0) {
                 // release at GPU scope: covers every epilogue thread's stores, which the
                 // named barrier ordered before it; readers acquire and fence the
                 // async proxy before their TMA loads
-                DN_T(s, 2);
+                { DN_T(s, 2); DN_C(s, 28); }
                 red_release_gpu_add(&ctr[1 + s], 1ull);
-                DN_T(s, 3);
+                { DN_T(s, 3); DN_C(s, 29); }
             }
         }
     }
@@ -1485,7 +1557,7 @@ int dense_launch(const DenseStage* stages, int nst, unsigned long long* ctr, int
     cudaLaunchConfig_t cfg = dense_config(ncl, stream, attr, pdl);
 #ifdef SFB_TRACE
     unsigned long long* tr = (g_dense_trace != nullptr && trace_slot >= 0)
-                                 ? g_dense_trace + static_cast<size_t>(trace_slot) * 160 * dense::kTrStages * 16 : nullptr;
+                                 ? g_dense_trace + static_cast<size_t>(trace_slot) * 160 * dense::kTrStages * 40 : nullptr;
     cudaError_t e = cudaLaunchKernelEx(&cfg, dense::rdt_dense_kernel, stages, nst, ctr, M, tr);
 #else
     (void)trace_slot;
