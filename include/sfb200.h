@@ -309,12 +309,12 @@ int sfb_rdt1b_tick(void* handle, int32_t sessions, uint64_t frame_id, const void
 int sfb_rdt1b_invalidate_condition(void* handle);
 /* Ticks run and conditions encoded so far on this handle (diagnostic). */
 int sfb_rdt1b_tick_stats(void* handle, int64_t* ticks, int64_t* encodes);
-/* Execution path of a one-session call (sessions == 1): 0 (the default) runs
- * the network evaluation as stages of the persistent kernel (every
- * projection, self-attention and cross-attention, with the pre-norms folded
- * into the projections), in launches of up to 48 stages; 1 runs one kernel
- * per projection, norm and attention (the path every batch of two or more
- * sessions takes); 2 runs the persistent kernel between separate
+/* Execution path of a one-session call (sessions == 1): 0 runs the network
+ * evaluation as stages of the persistent kernel (every projection,
+ * self-attention and cross-attention, with the pre-norms folded into the
+ * projections), in launches of up to 48 stages; 1 (the default, the fastest
+ * measured) runs one kernel per projection, norm and attention (the path
+ * every batch of two or more sessions takes); 2 runs the persistent kernel between separate
  * cross-attention kernels. Results agree within the model's tolerance, not
  * bit for bit. Changing it drops the captured graphs. No counterpart in the
  * reference. */

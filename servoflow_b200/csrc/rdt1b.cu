@@ -148,7 +148,7 @@ struct Model {
     // by block l+1's first four stages, or by the final layer.
     struct DenseLaunch { int first, count, ctr; };
     bool dense_ok = false;
-    int path = 0;                             // 0, 2: persistent kernel at one session; 1: per-projection kernels
+    int path = 1;                             // 0, 2: persistent kernel at one session; 1: per-projection kernels
     DenseStage* d_stages = nullptr;           // device copy of the stage tables
     unsigned long long* d_ctr = nullptr;      // completion counters, 1 + count per launch
     std::vector<DenseLaunch> dl[2];
@@ -676,9 +676,10 @@ int sfb_rdt1b_create(const sfb_rdt1b_config* cfg, uint64_t seed, void** handle) 
     if (m == nullptr) return SFB_ERR_CUDA;
     m->c = c;
     m->seed = seed;
-    // SFB_RDT1B_PATH=1 selects the per-projection kernels at one session by
-    // default (sfb_rdt1b_set_path changes it per handle)
-    if (const char* e = std::getenv("SFB_RDT1B_PATH")) m->path = (e[0] >= '0' && e[0] <= '2' && e[1] == 0) ? e[0] - '0' : 0;
+    // SFB_RDT1B_PATH=0|1|2 selects a handle's initial one-session path
+    // (sfb_rdt1b_set_path changes it per handle)
+    if (const char* e = std::getenv("SFB_RDT1B_PATH"))
+        if (e[0] >= '0' && e[0] <= '2' && e[1] == 0) m->path = e[0] - '0';
     cudaGetDevice(&m->device);
     const int rc = rdt::create(*m);
     if (rc != SFB_OK) {

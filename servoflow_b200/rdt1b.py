@@ -135,8 +135,8 @@ class RDT1B:
 
     def set_path(self, path: int) -> None:
         """One-session execution path (sfb_rdt1b_set_path): 0 the persistent
-        kernel runs every projection and attention as stages (default), 1 one
-        kernel per projection, norm and attention, 2 the persistent kernel
+        kernel runs every projection and attention as stages, 1 one kernel per
+        projection, norm and attention (default), 2 the persistent kernel
         between cross-attention kernels."""
         _capi.check(self.lib.sfb_rdt1b_set_path(self.h, int(path)), "set_path")
 

@@ -53,16 +53,23 @@ def full(gpu):
     model.close()
 
 
-def test_full_config_single_evaluation(full):
+@pytest.mark.parametrize("path", [1, 0])
+def test_full_config_single_evaluation(full, path):
+    """One evaluation on the per-projection path (1, the default) and on the
+    persistent kernel with every attention as a stage (0)."""
     f = full
     out = torch.empty(1, f["cfg"].horizon, f["cfg"].action_dim, device=f["dev"])
-    f["model"].forward(f["noise"].to(f["dev"]), 999.0, out)
-    torch.cuda.synchronize()
+    f["model"].set_path(path)
+    try:
+        f["model"].forward(f["noise"].to(f["dev"]), 999.0, out)
+        torch.cuda.synchronize()
+    finally:
+        f["model"].set_path(1)
     with torch.inference_mode():
         ref = f["ref"].forward(f["lang_c"], f["img_c"], f["lens"], f["state"].float(), f["noise"], 999,
                                f["kv"])
     max_abs, cos = close(out, ref)
-    print(f"[parity] config 4 forward t=999: max |d| {max_abs:.3e}, cos {cos:.7f}")
+    print(f"[parity] config 4 forward t=999, path {path}: max |d| {max_abs:.3e}, cos {cos:.7f}")
     assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
 
 
