@@ -11,6 +11,8 @@
 // l, l+32, ... of the running O.
 #include "common.cuh"
 
+#include <type_traits>
+
 namespace sfb {
 
 struct AttnSimtParams {
@@ -138,10 +140,201 @@ attn_fwd_simt_kernel(const AttnSimtParams p) {
     }
 }
 
+// Short key ranges (Lk <= kResKeys, the action self-attention's 67 keys):
+// the whole K and V of the head are loaded into shared memory at once, every
+// load in flight together, instead of one 32-key tile per round trip; eight
+// warps of two query rows each then run the same online softmax over the
+// resident 32-key tiles (same order of operations, so the same bits as the
+// tiled kernel).
+constexpr int kResKeys  = 128;
+constexpr int kResWarps = 8;
+constexpr int kResRowsPW = 2;
+constexpr int kResRows  = kResWarps * kResRowsPW;   // 16, as kRowsCTA
+
+__host__ __device__ constexpr int res_smem_floats(int dp, int lkp) {
+    return kResRows * dp + lkp * (dp + 1) + lkp * dp;
+}
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(kResWarps * 32)
+attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
+    constexpr int NC = DP / 32;
+    extern __shared__ float sres[];
+    float* sQ = sres;                                  // [16][DP]
+    float* sK = sQ + kResRows * DP;                    // [lkp][DP + 1]
+    float* sV = sK + lkp * (DP + 1);                   // [lkp][DP]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.z, h = blockIdx.y;
+    const int hk = h / (p.H / p.Hkv);
+    const int q0 = blockIdx.x * kResRows;
+    const T* Q = static_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh;
+    const T* K = static_cast<const T*>(p.k) + b * p.k_sb + hk * p.k_sh;
+    const T* V = static_cast<const T*>(p.v) + b * p.v_sb + hk * p.v_sh;
+
+    int kend = p.Lk;
+    if (p.kv_len != nullptr) kend = min(kend, max(0, p.kv_len[b]));
+    if (p.causal) kend = min(kend, min(p.Lq, q0 + kResRows));
+    const int ntile = (kend + kKeys - 1) / kKeys;
+    const int nkeys = ntile * kKeys;                   // <= lkp
+
+    // Q, K and V of the head: fp32 rows of exactly DP contiguous, 16-byte
+    // aligned values go as float4 loads, all issued before the first store
+    // (one memory latency); anything else element-wise.
+    bool vec = false;
+    if constexpr (std::is_same<T, float>::value && DP == 64) {
+        vec = p.D == DP && ((p.q_ss | p.k_ss | p.v_ss) & 3) == 0 &&
+              ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+                reinterpret_cast<uintptr_t>(V)) & 15) == 0;
+    }
+    if (vec) {
+        if constexpr (std::is_same<T, float>::value && DP == 64) {
+            constexpr int kV = DP / 4;                             // float4 per row
+            constexpr int kMax = (kResRows + 2 * kResKeys) * kV / (kResWarps * 32);   // 34
+            const int nq = kResRows * kV, nk = nkeys * kV, total = nq + 2 * nk;
+            float4 buf[kMax];
+#pragma unroll
+            for (int it = 0; it < kMax; ++it) {
+                const int i = tid + it * kResWarps * 32;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i < nq) {
+                    const int r = i / kV, c = i % kV;
+                    if (q0 + r < p.Lq) x = *reinterpret_cast<const float4*>(Q + (q0 + r) * p.q_ss + 4 * c);
+                } else if (i < total) {
+                    const int j = i - nq, isv = j >= nk, jj = isv ? j - nk : j;
+                    const int r = jj / kV, c = jj % kV;
+                    if (r < kend)
+                        x = *reinterpret_cast<const float4*>((isv ? V + r * p.v_ss : K + r * p.k_ss) + 4 * c);
+                }
+                buf[it] = x;
+            }
+#pragma unroll
+            for (int it = 0; it < kMax; ++it) {
+                const int i = tid + it * kResWarps * 32;
+                const float4 x = buf[it];
+                if (i < nq) {
+                    *reinterpret_cast<float4*>(sQ + i * 4) = x;
+                } else if (i < total) {
+                    const int j = i - nq, isv = j >= nk, jj = isv ? j - nk : j;
+                    const int r = jj / kV, c = jj % kV;
+                    if (isv) {
+                        *reinterpret_cast<float4*>(sV + r * DP + 4 * c) = x;
+                    } else {
+                        float* d = sK + r * (DP + 1) + 4 * c;          // padded rows: scalar stores
+                        d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+                    }
+                }
+            }
+        }
+    } else {
+#pragma unroll 4
+    for (int i = tid; i < kResRows * DP; i += blockDim.x) {
+        const int r = i / DP, d = i % DP;
+        const int qi = q0 + r;
+        sQ[r * DP + d] = (qi < p.Lq && d < p.D) ? ld<T>(Q + qi * p.q_ss + d) : 0.f;
+    }
+#pragma unroll 4
+    for (int i = tid; i < nkeys * DP; i += blockDim.x) {
+        const int r = i / DP, d = i % DP;
+        const bool in = r < kend && d < p.D;
+        sK[r * (DP + 1) + d] = in ? ld<T>(K + r * p.k_ss + d) : 0.f;
+        sV[r * DP + d] = in ? ld<T>(V + r * p.v_ss + d) : 0.f;
+    }
+    }
+    __syncthreads();
+
+    float m[kResRowsPW], l[kResRowsPW], o[kResRowsPW][NC];
+#pragma unroll
+    for (int r = 0; r < kResRowsPW; ++r) {
+        m[r] = -INFINITY; l[r] = 0.f;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) o[r][c] = 0.f;
+    }
+    for (int k0 = 0; k0 < nkeys; k0 += kKeys) {
+        const int kj = k0 + lane;
+        bool kvalid = kj < kend;
+        if (kvalid && p.key_mask != nullptr) kvalid = p.key_mask[b * p.mask_sb + kj] != 0;
+        const float* kr = sK + kj * (DP + 1);
+#pragma unroll
+        for (int r = 0; r < kResRowsPW; ++r) {
+            const int row = warp * kResRowsPW + r;
+            const int qi = q0 + row;
+            const float* qr = sQ + row * DP;
+            float s = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < DP; ++d) s = fmaf(qr[d], kr[d], s);
+            s *= p.scale;
+            const bool valid = kvalid && (!p.causal || kj <= qi);
+            if (valid && p.amask != nullptr && qi < p.Lq)
+                s += attn_mask_at(p.amask, p.am_dt, b * p.am_sb + qi * p.am_ss + kj);
+            if (!valid) s = -INFINITY;
+            float tmax = s;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+            const float mnew = fmaxf(m[r], tmax);
+            const float muse = mnew == -INFINITY ? 0.f : mnew;
+            const float alpha = expf(m[r] - muse);
+            const float pk = valid ? expf(s - muse) : 0.f;
+            l[r] = l[r] * alpha + pk;
+            m[r] = mnew;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) o[r][c] *= alpha;
+            const float* vt = sV + k0 * DP;
+#pragma unroll 4
+            for (int kk = 0; kk < kKeys; ++kk) {
+                const float pb = __shfl_sync(0xffffffffu, pk, kk);
+#pragma unroll
+                for (int c = 0; c < NC; ++c) o[r][c] = fmaf(pb, vt[kk * DP + lane + 32 * c], o[r][c]);
+            }
+        }
+    }
+
+    T* O = static_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh;
+#pragma unroll
+    for (int r = 0; r < kResRowsPW; ++r) {
+        float lt = l[r];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+        const int qi = q0 + warp * kResRowsPW + r;
+        if (qi >= p.Lq) continue;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int d = lane + 32 * c;
+            if (d < p.D) O[qi * p.o_ss + d] = cvt<T>(o[r][c] * inv);
+        }
+    }
+}
+
 }  // namespace attn_simt
+
+template <typename T, int DP>
+static int launch_simt_res(const AttnSimtParams& p, cudaStream_t stream) {
+    using namespace attn_simt;
+    const int lkp = (p.Lk + kKeys - 1) / kKeys * kKeys;
+    const size_t smem = static_cast<size_t>(res_smem_floats(DP, lkp)) * 4;
+    static bool attr_set[64] = {};                     // per device: the maximum is constant
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+        const cudaError_t e = cudaFuncSetAttribute(attn_fwd_simt_res_kernel<T, DP>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   res_smem_floats(DP, kResKeys) * 4);
+        if (e != cudaSuccess) { record_cuda_error(e, "attention smem attribute"); return SFB_ERR_CUDA; }
+        attr_set[dev & 63] = true;
+    }
+    dim3 grid((p.Lq + kResRows - 1) / kResRows, p.H, p.B);
+    attn_fwd_simt_res_kernel<T, DP><<<grid, kResWarps * 32, smem, stream>>>(p, lkp);
+    return launch_status();
+}
 
 template <typename T>
 static int launch_simt_t(const AttnSimtParams& p, cudaStream_t stream) {
+    if (p.Lk <= attn_simt::kResKeys) {
+        if (p.D <= 32) return launch_simt_res<T, 32>(p, stream);
+        if (p.D <= 64) return launch_simt_res<T, 64>(p, stream);
+        return launch_simt_res<T, 128>(p, stream);
+    }
     dim3 grid((p.Lq + attn_simt::kRowsCTA - 1) / attn_simt::kRowsCTA, p.H, p.B);
     dim3 block(attn_simt::kWarps * 32);
     if (p.D <= 32)
