@@ -208,3 +208,25 @@ def test_one_session_graph_replays_are_identical(one):
     assert max_abs < 0.05 and cos > 0.9999, (max_abs, cos)
     from servoflow_b200.backend import B200Backend
     assert B200Backend(0).device_error(reset=True) == 0
+
+
+def test_profile_dense_reports_every_launch(one):
+    """sfb_rdt1b_profile_dense: one entry per persistent-kernel launch of an
+    evaluation, with positive bytes and durations, and the handle's path
+    unchanged afterwards."""
+    s = one
+    s["model"].set_path(1)
+    prof = s["model"].profile_dense(999.0)
+    cfg = s["cfg"]
+    stages = cfg.num_layers * 8 + 2                       # per block 8 stages, then the final layer's 2
+    assert len(prof) == (stages + 47) // 48
+    assert all(b > 0 and us > 0 for b, us in prof)
+    # the weights alone: every block's int8 projections are read once
+    D = cfg.hidden
+    assert sum(b for b, _ in prof) > cfg.num_layers * 8 * D * D
+    noise = s["noise"].to(s["dev"])
+    y = torch.empty_like(noise)
+    s["model"].forward(noise, 999.0, y)                   # still path 1: the per-projection kernels
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all()
+    s["model"].set_path(0)
