@@ -163,7 +163,9 @@ constexpr int kRcvBytes = 24576;                              // [4 sources][16 
 static_assert(kRcvBytes >= kSplit * (kTM / 4) * kBN * 4 && kRcvBytes >= kSplit * 20 * 68 * 4, "receive area");
 constexpr int kOffRinv = kOffRcv + kRcvBytes;
 constexpr int kOffRed = kOffRinv + kBN * 4;                   // [6 groups][80] partial row sums
-constexpr int kOffBar = kOffRed + 6 * kBN * 4;
+constexpr int kOffSSt = kOffRed + 6 * kBN * 4;                 // [80] this CTA's quarter of the row sums
+constexpr int kOffSSx = kOffSSt + kBN * 4;                    // [4 ranks][80] the cluster's quarters
+constexpr int kOffBar = kOffSSx + kSplit * kBN * 4;
 // barriers
 constexpr int kBarWFull = 0;                                  // [kNW]
 constexpr int kBarWFree = kBarWFull + kNW;                    // [kNW]
@@ -188,7 +190,8 @@ constexpr int kBarCS = kBarCQ + 1;                            // [2]: S of TMEM 
 constexpr int kBarCP = kBarCS + 2;                            // P written
 constexpr int kBarCO = kBarCP + 1;                            // O += P·V done
 constexpr int kBarDrain2 = kBarCO + 1;                        // the activation warp's MMAs after a failure
-constexpr int kNumBars = kBarDrain2 + 1;
+constexpr int kBarSS = kBarDrain2 + 1;                        // the cluster's RMS quarter sums landed
+constexpr int kNumBars = kBarSS + 1;
 // TMEM columns: projection accumulators [0, 256); self-attention S [256, 336),
 // P (fp16 pairs) [336, 384), O [384, 448); cross-attention S buffers at 0
 // and 128 (the accumulators' columns: no projection runs in that stage), P
@@ -682,6 +685,8 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
     float* rcv = reinterpret_cast<float*>(smem + kOffRcv);
     float* rinv = reinterpret_cast<float*>(smem + kOffRinv);
     float* red = reinterpret_cast<float*>(smem + kOffRed);
+    float* sst = reinterpret_cast<float*>(smem + kOffSSt);
+    float* ssx = reinterpret_cast<float*>(smem + kOffSSx);
     StageInfo* sinfo = reinterpret_cast<StageInfo*>(smem + kOffInfo);
     auto sX = [&](int c) { return smem + kOffX + c * kXBytes; };
     auto sWB = [&](int s) { return smem + kOffWB + s * kWBBytes; };
@@ -702,6 +707,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         for (int i = 0; i < kSplit; ++i) mbar_init(&bars[kBarRcvFree + i], 4);   // the owner's 4 warps
         mbar_init(&bars[kBarDrain], 1);
         mbar_init(&bars[kBarDrain2], 1);
+        mbar_init(&bars[kBarSS], 1);                        // armed by this CTA (expect_tx), filled by st.async
         mbar_init(&bars[kBarQK], 4);
         mbar_init(&bars[kBarS], 1);
         mbar_init(&bars[kBarP], 4);
@@ -1089,6 +1095,7 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
         const int q = warp & 3;
         constexpr int kMaxIt = 2;                          // owner units (<= 80 · 16 / 8) / 128 threads
         uint32_t ue = 0, xs = 0, au = 0, xmask = 0;        // xmask as the activation loader's
+        uint32_t ssn = 0;                                  // stages whose RMS sums this CTA exchanged
         uint32_t cq = 0, ct = 0;                           // cross-attention stages / key tiles
         const int mvalid = min(M, kBN);
         for (int s = 0; s < nst; ++s) {
@@ -1178,17 +1185,23 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                 // (1b) rows' RMS factors from the producing stage's partial sums (once per stage)
                 if (j == 0) {
                     if (S.ss_in != nullptr) {
+                        // The cluster's four CTAs each read a quarter of the
+                        // partials (one read of every partial per cluster instead of
+                        // per CTA: 132 CTAs would all hit the same lines) and
+                        // exchange their 80 quarter sums through shared memory.
                         // Thread t < 120 sums the float4 column t % 20 (token rows
                         // 4·(t % 20) .. +3) over partials group t / 20 (six groups of
-                        // consecutive partials): up to 22 independent 16-byte loads in
-                        // flight per thread instead of a chain of dependent ones. The
-                        // six group sums are then added in group order.
+                        // consecutive partials of the quarter), all its loads in
+                        // flight at once; the group sums, then the quarters, are
+                        // added in a fixed order.
                         constexpr int kCols = kBN / 4, kGroups = kEpiThreads / kCols;   // 20, 6
-                        constexpr int kBatch = 22;          // loads in flight: a group's partials at once (128 / 6)
+                        constexpr int kBatch = 8;           // loads in flight: a group's share of a quarter
                         const int np = S.n_ss_in;
+                        const int q0p = rank * np / kSplit, q1p = (rank + 1) * np / kSplit;
                         const int col = et % kCols, grpi = et / kCols;
-                        const int per = (np + kGroups - 1) / kGroups;
-                        const int p0 = grpi * per, p1 = min(np, p0 + per);
+                        const int per = (q1p - q0p + kGroups - 1) / kGroups;
+                        const int p0 = q0p + grpi * per, p1 = min(q1p, p0 + per);
+                        if (et == 0) mbar_arrive_expect_tx(&bars[kBarSS], static_cast<uint32_t>(kSplit * kBN * 4));
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                         if (grpi < kGroups) {
                             for (int pb = p0; pb < p1; pb += kBatch) {
@@ -1205,10 +1218,24 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
                             *reinterpret_cast<float4*>(red + grpi * kBN + 4 * col) = acc;
                         }
                         named_bar_sync(1, kEpiThreads);
-                        if (et < mvalid) {
+                        if (et < kBN) {
                             float tot = 0.f;
 #pragma unroll
                             for (int g = 0; g < kGroups; ++g) tot += red[g * kBN + et];
+                            sst[et] = tot;
+                        }
+                        named_bar_sync(1, kEpiThreads);
+                        if (et < kSplit * kCols) {
+                            // thread t: float4 column t % 20 of this quarter to rank t / 20
+                            const uint32_t dst_rank = static_cast<uint32_t>(et / kCols), c4 = et % kCols;
+                            const uint32_t dst = dsmem_map(smem_u32(ssx + rank * kBN + 4 * c4), dst_rank);
+                            const uint32_t rb = dsmem_map(smem_u32(&bars[kBarSS]), dst_rank);
+                            st_async_v4(dst, *reinterpret_cast<const float4*>(sst + 4 * c4), rb);
+                        }
+                        if (!cwait(&bars[kBarSS], ssn & 1, ok ? kWaitNs : 0ull)) ok = false;
+                        ++ssn;
+                        if (et < mvalid) {
+                            const float tot = (ssx[et] + ssx[kBN + et]) + (ssx[2 * kBN + et] + ssx[3 * kBN + et]);
                             rinv[et] = 1.f / sqrtf(tot / static_cast<float>(S.K) + S.eps);
                         }
                     }
