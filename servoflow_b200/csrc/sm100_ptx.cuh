@@ -103,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
     }
 }
 
-// ── TMA (tensor tile loads, no multicast) ───────────────────────────────────
+// ── TMA (tensor tile loads, this CTA only) ───────────────────────────────────
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
