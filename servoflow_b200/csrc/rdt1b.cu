@@ -261,6 +261,7 @@ static int build_dense(Model& m) {
     std::vector<DenseStage> st;
     std::vector<double> bytes;
     std::vector<char> lang_kv;
+    std::vector<std::pair<const int8_t*, uint64_t>> wts;   // each stage's int8 weights (projections)
     auto stage = [&](const Linear& Lw, const __nv_bfloat16* x, int TM, int act, void* y, int64_t ldy, bool y_f32,
                      const void* res, const float* ss_in, int n_ss_in, const __nv_bfloat16* g_next) {
         DenseStage d;
@@ -271,6 +272,7 @@ static int build_dense(Model& m) {
         d.ss_in = ss_in; d.n_ss_in = n_ss_in; d.eps = 1e-6f;
         if (g_next != nullptr) { d.g_next = g_next; d.xg = m.xg; d.ldg = D; d.ss_out = m.ss; }
         st.push_back(d);
+        wts.push_back({Lw.w, static_cast<uint64_t>(Lw.N) * Lw.K});
         const double ysz = y_f32 ? 4.0 : 2.0, MN = static_cast<double>(S) * Lw.N;
         double b = static_cast<double>(Lw.N) * Lw.K + Lw.N * 6.0 + 2.0 * S * Lw.K + MN * ysz;
         if (res != nullptr) b += MN * ysz;
@@ -293,6 +295,7 @@ static int build_dense(Model& m) {
                                       0.125f));
         st.push_back(d);
         bytes.push_back(4.0 * S * D * 2 + 4 * 64 * 2.0);
+        wts.push_back({nullptr, 0});
         lang_kv.push_back(0);
         return SFB_OK;
     };
@@ -305,6 +308,7 @@ static int build_dense(Model& m) {
         st.push_back(d);
         // Q, out, and (image blocks) the whole K/V cache
         bytes.push_back(2.0 * S * D * 2 + 64 * 2.0 + (lang_blk ? 0.0 : 2.0 * c.img_len * D * 2));
+        wts.push_back({nullptr, 0});
         lang_kv.push_back(lang_blk ? 1 : 0);
         return SFB_OK;
     };
@@ -350,6 +354,22 @@ static int build_dense(Model& m) {
         const int n = (n0 - (first - f0)) / (nl - i);          // even cut
         launch(0, first, n);
         first += n;
+    }
+    // a launch starts with its first projection's weights already in L2: the
+    // launch before pulls them in during its last stages (a stage that does not
+    // prefetch anything else carries the region)
+    for (size_t i = 0; i + 1 < m.dl[0].size(); ++i) {
+        const auto& cur = m.dl[0][i];
+        const auto& nxt = m.dl[0][i + 1];
+        int w = nxt.first;
+        while (w < nxt.first + nxt.count && wts[w].first == nullptr) ++w;
+        if (w == nxt.first + nxt.count) continue;
+        for (int k = cur.first + cur.count - 1; k >= cur.first + cur.count - 3 && k >= cur.first; --k)
+            if (st[k].l2_prefetch == nullptr) {
+                st[k].l2_prefetch = reinterpret_cast<const uint8_t*>(wts[w].first);
+                st[k].l2_bytes = wts[w].second;
+                break;
+            }
     }
     // path 2: cross-attention kernels between launches
     int f = static_cast<int>(st.size());
