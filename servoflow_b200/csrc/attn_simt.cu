@@ -143,16 +143,21 @@ attn_fwd_simt_kernel(const AttnSimtParams p) {
 // Short key ranges (Lk <= kResKeys, the action self-attention's 67 keys):
 // the whole K and V of the head are loaded into shared memory at once, every
 // load in flight together, instead of one 32-key tile per round trip; eight
-// warps of two query rows each then run the same online softmax over the
-// resident 32-key tiles (same order of operations, so the same bits as the
-// tiled kernel).
+// warps of two query rows each (one pass over a key or V row serves both
+// rows) then run the same online softmax over the resident 32-key tiles
+// (per row the same order of operations as the tiled kernel). 16 warps of
+// one row measured slower: the extra shared-memory loads cost more than the
+// shorter per-warp chains gain.
 constexpr int kResKeys  = 128;
 constexpr int kResWarps = 8;
 constexpr int kResRowsPW = 2;
 constexpr int kResRows  = kResWarps * kResRowsPW;   // 16, as kRowsCTA
 
+// K rows padded to dp + 4 floats: 16-byte aligned, and a warp's float4 loads
+// of 32 consecutive rows hit distinct bank groups
+__host__ __device__ constexpr int res_k_stride(int dp) { return dp + 4; }
 __host__ __device__ constexpr int res_smem_floats(int dp, int lkp) {
-    return kResRows * dp + lkp * (dp + 1) + lkp * dp;
+    return kResRows * dp + lkp * res_k_stride(dp) + lkp * dp;
 }
 
 template <typename T, int DP>
@@ -161,8 +166,9 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
     constexpr int NC = DP / 32;
     extern __shared__ float sres[];
     float* sQ = sres;                                  // [16][DP]
-    float* sK = sQ + kResRows * DP;                    // [lkp][DP + 1]
-    float* sV = sK + lkp * (DP + 1);                   // [lkp][DP]
+    constexpr int KS = res_k_stride(DP);
+    float* sK = sQ + kResRows * DP;                    // [lkp][KS]
+    float* sV = sK + lkp * KS;                         // [lkp][DP]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.z, h = blockIdx.y;
@@ -190,7 +196,7 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
     if (vec) {
         if constexpr (std::is_same<T, float>::value && DP == 64) {
             constexpr int kV = DP / 4;                             // float4 per row
-            constexpr int kMax = (kResRows + 2 * kResKeys) * kV / (kResWarps * 32);   // 34
+            constexpr int kMax = ((kResRows + 2 * kResKeys) * kV + kResWarps * 32 - 1) / (kResWarps * 32);
             const int nq = kResRows * kV, nk = nkeys * kV, total = nq + 2 * nk;
             float4 buf[kMax];
 #pragma unroll
@@ -220,8 +226,7 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
                     if (isv) {
                         *reinterpret_cast<float4*>(sV + r * DP + 4 * c) = x;
                     } else {
-                        float* d = sK + r * (DP + 1) + 4 * c;          // padded rows: scalar stores
-                        d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+                        *reinterpret_cast<float4*>(sK + r * KS + 4 * c) = x;
                     }
                 }
             }
@@ -237,7 +242,7 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
     for (int i = tid; i < nkeys * DP; i += blockDim.x) {
         const int r = i / DP, d = i % DP;
         const bool in = r < kend && d < p.D;
-        sK[r * (DP + 1) + d] = in ? ld<T>(K + r * p.k_ss + d) : 0.f;
+        sK[r * KS + d] = in ? ld<T>(K + r * p.k_ss + d) : 0.f;
         sV[r * DP + d] = in ? ld<T>(V + r * p.v_ss + d) : 0.f;
     }
     }
@@ -254,16 +259,28 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
         const int kj = k0 + lane;
         bool kvalid = kj < kend;
         if (kvalid && p.key_mask != nullptr) kvalid = p.key_mask[b * p.mask_sb + kj] != 0;
-        const float* kr = sK + kj * (DP + 1);
+        // both rows' logits from one pass over this lane's key (float4 loads;
+        // per row the same sequential FMA order as the tiled kernel)
+        const float4* kr4 = reinterpret_cast<const float4*>(sK + kj * KS);
+        float sr[kResRowsPW];
+#pragma unroll
+        for (int r = 0; r < kResRowsPW; ++r) sr[r] = 0.f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < DP / 4; ++d4) {
+            const float4 kv = kr4[d4];
+#pragma unroll
+            for (int r = 0; r < kResRowsPW; ++r) {
+                const float4 qv = reinterpret_cast<const float4*>(sQ + (warp * kResRowsPW + r) * DP)[d4];
+                sr[r] = fmaf(qv.x, kv.x, sr[r]); sr[r] = fmaf(qv.y, kv.y, sr[r]);
+                sr[r] = fmaf(qv.z, kv.z, sr[r]); sr[r] = fmaf(qv.w, kv.w, sr[r]);
+            }
+        }
+        float pk[kResRowsPW];
 #pragma unroll
         for (int r = 0; r < kResRowsPW; ++r) {
             const int row = warp * kResRowsPW + r;
             const int qi = q0 + row;
-            const float* qr = sQ + row * DP;
-            float s = 0.f;
-#pragma unroll 8
-            for (int d = 0; d < DP; ++d) s = fmaf(qr[d], kr[d], s);
-            s *= p.scale;
+            float s = sr[r] * p.scale;
             const bool valid = kvalid && (!p.causal || kj <= qi);
             if (valid && p.amask != nullptr && qi < p.Lq)
                 s += attn_mask_at(p.amask, p.am_dt, b * p.am_sb + qi * p.am_ss + kj);
@@ -274,17 +291,24 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
             const float mnew = fmaxf(m[r], tmax);
             const float muse = mnew == -INFINITY ? 0.f : mnew;
             const float alpha = expf(m[r] - muse);
-            const float pk = valid ? expf(s - muse) : 0.f;
-            l[r] = l[r] * alpha + pk;
+            pk[r] = valid ? expf(s - muse) : 0.f;
+            l[r] = l[r] * alpha + pk[r];
             m[r] = mnew;
 #pragma unroll
             for (int c = 0; c < NC; ++c) o[r][c] *= alpha;
-            const float* vt = sV + k0 * DP;
+        }
+        // P·V for both rows from one pass over the tile's V rows
+        const float* vt = sV + k0 * DP;
 #pragma unroll 4
-            for (int kk = 0; kk < kKeys; ++kk) {
-                const float pb = __shfl_sync(0xffffffffu, pk, kk);
+        for (int kk = 0; kk < kKeys; ++kk) {
+            float pb[kResRowsPW];
 #pragma unroll
-                for (int c = 0; c < NC; ++c) o[r][c] = fmaf(pb, vt[kk * DP + lane + 32 * c], o[r][c]);
+            for (int r = 0; r < kResRowsPW; ++r) pb[r] = __shfl_sync(0xffffffffu, pk[r], kk);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const float vv = vt[kk * DP + lane + 32 * c];
+#pragma unroll
+                for (int r = 0; r < kResRowsPW; ++r) o[r][c] = fmaf(pb[r], vv, o[r][c]);
             }
         }
     }
