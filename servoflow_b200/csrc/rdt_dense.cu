@@ -148,10 +148,7 @@ constexpr int kNW = 8;                        // int8 weight ring slots (kTM × 
 constexpr int kNB = 8;                        // converted bf16 weight slots (SW128, kTM × 128 B)
 constexpr int kNX = 8;                        // activation chunks per CTA (K / 4 / 64 <= 8)
 constexpr int kXBytes = kBN * 128;            // one activation chunk [80 × 64] bf16, SW128
-#ifndef SFB_DENSE_XROWS
-#define SFB_DENSE_XROWS 80
-#endif
-constexpr int kXRows = SFB_DENSE_XROWS;       // rows of an activation box (>= M; the rest of the tile is unused)
+constexpr int kXRows = kBN;                   // rows of an activation box (>= M)
 constexpr uint32_t kXBoxBytes = kXRows * 128;
 constexpr int kWBytes = kTM * 64;             // int8 slot
 constexpr int kWBBytes = kTM * 128;           // bf16 slot
@@ -271,43 +268,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         if ((it & 63u) == 63u && ptx::global_timer_ns() - t0 > timeout_ns) return false;
     }
 }
-// Wait policy. A blocking try_wait may leave the warp suspended for hundreds
-// of cycles after the phase completes; the polling test_wait resumes within
-// a few cycles but takes issue slots from the warps that share its
-// scheduler. kSpinLevel: 0 try_wait everywhere; 1 polling in the MMA and
-// activation warps; 2 also in the weight and converter warps; 3 everywhere.
-#ifndef SFB_DENSE_SPIN
-#define SFB_DENSE_SPIN 0
-#endif
-constexpr int kSpinLevel = SFB_DENSE_SPIN;
-__device__ __forceinline__ bool spin_role(int warp) {
-    if (kSpinLevel >= 3) return true;
-    if (kSpinLevel >= 2 && warp < kWarpEpi0) return true;
-    return kSpinLevel >= 1 && (warp == kWarpMma || warp == kWarpX);
-}
-__device__ __forceinline__ bool dwait(uint64_t* bar, uint32_t parity, uint64_t ns, bool spin) {
-    return spin ? ptx::mbar_wait_spin(bar, parity, ns) : ptx::mbar_wait(bar, parity, ns);
-}
-__device__ __forceinline__ bool mbar_wait_cluster_spin(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
-    const uint32_t a = ptx::smem_u32(bar);
-    auto probe = [&]() {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred P;\n\t"
-            "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
-            "selp.b32 %0, 1, 0, P;\n\t}"
-            : "=r"(ok) : "r"(a), "r"(parity) : "memory");
-        return ok != 0;
-    };
-    if (probe()) return true;
-    const uint64_t t0 = ptx::global_timer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (probe()) return true;
-        if ((it & 255u) == 255u && ptx::global_timer_ns() - t0 > timeout_ns) return false;
-    }
-}
+// Waits of the kernel: blocking try_wait with the kernel's limit. (Polling
+// test_wait in any of the roles measured no faster.)
 __device__ __forceinline__ bool cwait(uint64_t* bar, uint32_t parity, uint64_t ns) {
-    return kSpinLevel >= 3 ? mbar_wait_cluster_spin(bar, parity, ns) : mbar_wait_cluster(bar, parity, ns);
+    return mbar_wait_cluster(bar, parity, ns);
 }
 
 // Pulls one box of a tensor map into L2 (no shared memory, no completion).
@@ -395,9 +359,8 @@ __device__ __forceinline__ void self_attention_epilogue(const StageInfo& S, uint
     using namespace ptx;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int et = threadIdx.x - kWarpEpi0 * 32, q = warp & 3;
-    const bool spin = spin_role(threadIdx.x >> 5);
     auto wait = [&](int b, uint32_t parity) {
-        if (!dwait(&bars[b], parity, ok ? kWaitNs : 0ull, spin)) ok = false;
+        if (!mbar_wait(&bars[b], parity, ok ? kWaitNs : 0ull)) ok = false;
     };
     uint8_t* sQ = smem + kOffX;
     uint8_t* sK = sQ + kQKVBytes;
@@ -498,9 +461,8 @@ __device__ __forceinline__ void cross_attention_epilogue(const StageInfo& S, uin
     using namespace ptx;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int et = threadIdx.x - kWarpEpi0 * 32, q = warp & 3;
-    const bool spin = spin_role(threadIdx.x >> 5);
     auto wait = [&](int b, uint32_t parity) {
-        if (!dwait(&bars[b], parity, ok ? kWaitNs : 0ull, spin)) ok = false;
+        if (!mbar_wait(&bars[b], parity, ok ? kWaitNs : 0ull)) ok = false;
     };
     constexpr int kOwnRows = (kBN + kSplit - 1) / kSplit;         // 20: rows per owner CTA
     constexpr int kRowF = 68;                                     // floats per sent row: O[64], m, l, pad
@@ -743,9 +705,8 @@ __device__ __forceinline__ void dense_run(const DenseStage* __restrict__ stages,
     if (tid == 0) DN_T(kMaxStages, 1);
 
     bool ok = true;
-    const bool spin = spin_role(threadIdx.x >> 5);
     auto wait = [&](int b, uint32_t parity) {
-        if (!dwait(&bars[b], parity, ok ? kWaitNs : 0ull, spin)) ok = false;
+        if (!mbar_wait(&bars[b], parity, ok ? kWaitNs : 0ull)) ok = false;
     };
 
     // Issuer w's share of projection unit j of stage s (see kIssuers): its K
