@@ -230,3 +230,33 @@ def test_profile_dense_reports_every_launch(one):
     torch.cuda.synchronize()
     assert torch.isfinite(y).all()
     s["model"].set_path(0)
+
+
+@pytest.mark.parametrize("lang_len", [1, 64, 96])
+def test_one_session_persistent_kernel_language_lengths(gpu, lang_len):
+    """The persistent kernel's cross-attention stage splits a head's valid
+    keys over its cluster's four CTAs: one key (three CTAs with no tile), a
+    length inside the first tile, and every key of the cache, each against
+    the oracle (the image stage covers several tiles per CTA elsewhere)."""
+    cfg = default_config(num_layers=2, max_lang_len=96, img_len=600, max_sessions=1)
+    model = RDT1B(cfg, seed=99)
+    try:
+        g = torch.Generator().manual_seed(7 + lang_len)
+        lang = torch.randn(1, cfg.max_lang_len, cfg.lang_dim, generator=g).bfloat16()
+        img = torch.randn(1, cfg.img_len, cfg.img_dim, generator=g).bfloat16()
+        state = torch.randn(1, cfg.state_dim, generator=g).bfloat16()
+        lens = torch.tensor([lang_len], dtype=torch.int32)
+        noise = torch.randn(1, cfg.horizon, cfg.action_dim, generator=g)
+        model.encode(lang.to(gpu), lens.to(gpu), img.to(gpu), state.to(gpu))
+        model.set_path(0)
+        y = torch.empty(1, cfg.horizon, cfg.action_dim, device=gpu)
+        model.forward(noise.to(gpu), 999.0, y)
+        torch.cuda.synchronize()
+        ref = rdt1b_ref.RefRDT(rdt1b_ref.load_weights(model, cfg), cfg)
+        lang_c, img_c = ref.encode(lang.float(), img.float())
+        r = ref.forward(lang_c, img_c, lens, state.float(), noise, 999)
+        max_abs, cos = close(y, r)
+        print(f"[parity] path 0, lang_len {lang_len}: max |d| {max_abs:.3e}, cos {cos:.7f}")
+        assert max_abs < 0.05 and cos > 0.9999, (lang_len, max_abs, cos)
+    finally:
+        model.close()
