@@ -142,12 +142,11 @@ attn_fwd_simt_kernel(const AttnSimtParams p) {
 
 // Short key ranges (Lk <= kResKeys, the action self-attention's 67 keys):
 // the whole K and V of the head are loaded into shared memory at once, every
-// load in flight together, instead of one 32-key tile per round trip; eight
-// warps of two query rows each (one pass over a key or V row serves both
-// rows) then run the same online softmax over the resident 32-key tiles
-// (per row the same order of operations as the tiled kernel). 16 warps of
-// one row measured slower: the extra shared-memory loads cost more than the
-// shorter per-warp chains gain.
+// load in flight together, instead of one 32-key tile per round trip. Eight
+// warps of two query rows each then compute every score of their rows (one
+// key per lane and tile, independent FMA chains), the exact row maximum, the
+// exponentials and P·V; with the keys resident no online rescaling is needed.
+// (16 warps of one row measured slower: more shared-memory loads.)
 constexpr int kResKeys  = 128;
 constexpr int kResWarps = 8;
 constexpr int kResRowsPW = 2;
@@ -248,62 +247,76 @@ attn_fwd_simt_res_kernel(const AttnSimtParams p, int lkp) {
     }
     __syncthreads();
 
-    float m[kResRowsPW], l[kResRowsPW], o[kResRowsPW][NC];
+    // Every score of the warp's two rows first (one key per lane and tile:
+    // up to 4 tiles x 2 rows of independent FMA chains), then the exact row
+    // maximum, the exponentials and P·V: the key range is resident, so no
+    // online rescaling is needed.
+    constexpr int kT = kResKeys / kKeys;               // 4
+    float sc[kResRowsPW][kT];
+#pragma unroll
+    for (int r = 0; r < kResRowsPW; ++r)
+#pragma unroll
+        for (int t = 0; t < kT; ++t) sc[r][t] = 0.f;
+#pragma unroll 2
+    for (int d4 = 0; d4 < DP / 4; ++d4) {
+        float4 qv[kResRowsPW];
+#pragma unroll
+        for (int r = 0; r < kResRowsPW; ++r)
+            qv[r] = reinterpret_cast<const float4*>(sQ + (warp * kResRowsPW + r) * DP)[d4];
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+            if (t >= ntile) break;
+            const float4 kv = reinterpret_cast<const float4*>(sK + (t * kKeys + lane) * KS)[d4];
+#pragma unroll
+            for (int r = 0; r < kResRowsPW; ++r) {
+                sc[r][t] = fmaf(qv[r].x, kv.x, sc[r][t]); sc[r][t] = fmaf(qv[r].y, kv.y, sc[r][t]);
+                sc[r][t] = fmaf(qv[r].z, kv.z, sc[r][t]); sc[r][t] = fmaf(qv[r].w, kv.w, sc[r][t]);
+            }
+        }
+    }
+    float l[kResRowsPW], o[kResRowsPW][NC];
+    float pk[kResRowsPW][kT];
 #pragma unroll
     for (int r = 0; r < kResRowsPW; ++r) {
-        m[r] = -INFINITY; l[r] = 0.f;
+        const int qi = q0 + warp * kResRowsPW + r;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+            float s = -INFINITY;
+            if (t < ntile) {
+                const int kj = t * kKeys + lane;
+                bool valid = kj < kend && (!p.causal || kj <= qi);
+                if (valid && p.key_mask != nullptr) valid = p.key_mask[b * p.mask_sb + kj] != 0;
+                if (valid) {
+                    s = sc[r][t] * p.scale;
+                    if (p.amask != nullptr && qi < p.Lq)
+                        s += attn_mask_at(p.amask, p.am_dt, b * p.am_sb + qi * p.am_ss + kj);
+                }
+            }
+            sc[r][t] = s;
+            mx = fmaxf(mx, s);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const float muse = mx == -INFINITY ? 0.f : mx;
+        l[r] = 0.f;
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+            pk[r][t] = sc[r][t] == -INFINITY ? 0.f : expf(sc[r][t] - muse);
+            l[r] += pk[r][t];
+        }
 #pragma unroll
         for (int c = 0; c < NC; ++c) o[r][c] = 0.f;
     }
-    for (int k0 = 0; k0 < nkeys; k0 += kKeys) {
-        const int kj = k0 + lane;
-        bool kvalid = kj < kend;
-        if (kvalid && p.key_mask != nullptr) kvalid = p.key_mask[b * p.mask_sb + kj] != 0;
-        // both rows' logits from one pass over this lane's key (float4 loads;
-        // per row the same sequential FMA order as the tiled kernel)
-        const float4* kr4 = reinterpret_cast<const float4*>(sK + kj * KS);
-        float sr[kResRowsPW];
 #pragma unroll
-        for (int r = 0; r < kResRowsPW; ++r) sr[r] = 0.f;
-#pragma unroll 4
-        for (int d4 = 0; d4 < DP / 4; ++d4) {
-            const float4 kv = kr4[d4];
-#pragma unroll
-            for (int r = 0; r < kResRowsPW; ++r) {
-                const float4 qv = reinterpret_cast<const float4*>(sQ + (warp * kResRowsPW + r) * DP)[d4];
-                sr[r] = fmaf(qv.x, kv.x, sr[r]); sr[r] = fmaf(qv.y, kv.y, sr[r]);
-                sr[r] = fmaf(qv.z, kv.z, sr[r]); sr[r] = fmaf(qv.w, kv.w, sr[r]);
-            }
-        }
-        float pk[kResRowsPW];
-#pragma unroll
-        for (int r = 0; r < kResRowsPW; ++r) {
-            const int row = warp * kResRowsPW + r;
-            const int qi = q0 + row;
-            float s = sr[r] * p.scale;
-            const bool valid = kvalid && (!p.causal || kj <= qi);
-            if (valid && p.amask != nullptr && qi < p.Lq)
-                s += attn_mask_at(p.amask, p.am_dt, b * p.am_sb + qi * p.am_ss + kj);
-            if (!valid) s = -INFINITY;
-            float tmax = s;
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-            const float mnew = fmaxf(m[r], tmax);
-            const float muse = mnew == -INFINITY ? 0.f : mnew;
-            const float alpha = expf(m[r] - muse);
-            pk[r] = valid ? expf(s - muse) : 0.f;
-            l[r] = l[r] * alpha + pk[r];
-            m[r] = mnew;
-#pragma unroll
-            for (int c = 0; c < NC; ++c) o[r][c] *= alpha;
-        }
-        // P·V for both rows from one pass over the tile's V rows
-        const float* vt = sV + k0 * DP;
+    for (int t = 0; t < kT; ++t) {
+        if (t >= ntile) break;
+        const float* vt = sV + t * kKeys * DP;
 #pragma unroll 4
         for (int kk = 0; kk < kKeys; ++kk) {
             float pb[kResRowsPW];
 #pragma unroll
-            for (int r = 0; r < kResRowsPW; ++r) pb[r] = __shfl_sync(0xffffffffu, pk[r], kk);
+            for (int r = 0; r < kResRowsPW; ++r) pb[r] = __shfl_sync(0xffffffffu, pk[r][t], kk);
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const float vv = vt[kk * DP + lane + 32 * c];
