@@ -336,3 +336,37 @@ def test_reference_fa2_pins_oracle(gpu, cfg):
     print(f"[parity] {cfg}: reference FA2 vs oracle {fa2_err:.3e}; ours vs oracle {ours_err:.3e}; "
           f"ours vs FA2 {(ours.float() - out.float()).abs().max().item():.3e}")
     assert fa2_err <= 1e-2          # the reference itself agrees with the oracle
+
+
+@pytest.mark.parametrize("Lk", [1, 33, 67, 128])
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_fp32_resident_keys(be, gpu, Lk, D):
+    """fp32 with at most 128 keys runs the kernel that keeps the head's K/V in
+    shared memory: key counts at and between its 32-key tiles, every head
+    width, grouped K/V heads, per-session valid lengths (one of them zero)."""
+    q, k, v = make(3, 4, 2, 67, Lk, D, torch.float32, 300 + Lk + D, gpu)
+    check_close(run(be, q, k, v), oracle_of(q, k, v), torch.float32, f"fp32 Lk {Lk} D {D}")
+    lens = torch.tensor([Lk, 0, (Lk + 1) // 2], dtype=torch.int32)
+    out = run(be, q, k, v, mask=lens.to(gpu))
+    assert torch.all(out[1] == 0)
+    check_close(out, oracle_of(q, k, v, kv_len=lens.numpy()), torch.float32, f"fp32 Lk {Lk} D {D} kv_len")
+
+
+@pytest.mark.parametrize("form", ["causal", "bytes", "additive"])
+def test_fp32_resident_keys_masks(be, gpu, form):
+    """The masks on the shared-memory-resident fp32 path (Lk = 100)."""
+    B, Lq, Lk = 2, 67, 100
+    q, k, v = make(B, 4, 4, Lq, Lk, 64, torch.float32, 400, gpu)
+    g = torch.Generator().manual_seed(401)
+    if form == "causal":
+        out, ref = run(be, q, k, v, is_causal=True), oracle_of(q, k, v, causal=True)
+    elif form == "bytes":
+        keep = torch.rand(B, Lk, generator=g) > 0.3
+        out, ref = run(be, q, k, v, mask=keep.to(gpu)), oracle_of(q, k, v, key_mask=keep.numpy())
+    else:
+        m = torch.randn(B, 1, Lq, Lk, generator=g) * 2
+        m[torch.rand(B, 1, Lq, Lk, generator=g) < 0.3] = float("-inf")
+        m[..., 0] = 0.0
+        out = run(be, q, k, v, mask=m.to(gpu))
+        ref = oracle_of(q, k, v, attn_mask=m.numpy())
+    check_close(out, ref, torch.float32, f"fp32 resident {form}")
