@@ -189,6 +189,27 @@ template <> struct HalfOps<__half> {
 // Validity bits of keys [key, key+32) for one query row: key < kend_row and,
 // with a key-padding mask, a nonzero mask byte. Mask rows are read 16 bytes
 // at a time when aligned.
+// The session whose valid length (clamped to [0, Lk]) has rank `rank` in
+// descending order (ties by index); every lane of the calling warp gets it.
+__device__ __forceinline__ int session_by_length_rank(const int32_t* len, int B, int Lk, int rank, int lane) {
+    int found = rank;
+    for (int base = 0; base < B; base += 32) {
+        const int s = base + lane;
+        int r = -1;
+        if (s < B) {
+            const int ls = min(Lk, max(0, len[s]));
+            r = 0;
+            for (int t = 0; t < B; ++t) {
+                const int lt = min(Lk, max(0, len[t]));
+                r += (lt > ls || (lt == ls && t < s)) ? 1 : 0;
+            }
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, r == rank);
+        if (m != 0u) found = base + __ffs(m) - 1;
+    }
+    return found;
+}
+
 __device__ __forceinline__ uint32_t key_bits(const AttnTcParams& p, int b, int key, int kend_row) {
     const int n = kend_row - key;
     uint32_t bits = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
@@ -244,8 +265,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int lane = tid & 31;
     const int split = blockIdx.x;
     const int h     = blockIdx.y;
-    const int b     = blockIdx.z / p.qtiles;
-    const int qt    = blockIdx.z - b * p.qtiles;
+    int b           = blockIdx.z / p.qtiles;       // remapped below when sessions have lengths
+    const int qt    = blockIdx.z % p.qtiles;
     const int hk    = h / (p.H / p.Hkv);
     const int q0    = qt * 128;
     const int rows  = min(128, p.Lq - q0);
@@ -306,6 +327,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 #endif
     SFB_T(1);
 
+    // With per-session lengths, CTA row z of the grid takes the session of
+    // rank z by descending length, so the longest sessions' CTAs are scheduled
+    // first and the last wave holds the short ones.
+    if (p.kv_len != nullptr && p.B > 1 && p.B <= 64) b = session_by_length_rank(p.kv_len, p.B, p.Lk, b, lane);
     // Key range of this (batch, q-tile), then this CTA's share of its tiles.
     int kend = p.Lk;
     if (p.kv_len != nullptr) kend = min(kend, max(0, p.kv_len[b]));
